@@ -1,0 +1,155 @@
+/*
+ * b2s.h -- C ABI of the B200 (sm_100a) ternary i2_s mul_mat library (libb2s.so).
+ *
+ * Drop-in boundary for one node type of a ggml graph: MUL_MAT with an i2_s (2-bit ternary, one fp32
+ * scale per tensor) weight, as a BitVLA engine would emit it at every linear layer, e.g.
+ *   ggml_tensor * q = ggml_mul_mat(ctx0, layer.wq, cur);       (src/models/pi0/vlm.cpp:217-223 pattern)
+ * plus the neighbouring nodes that produce and consume its activations (RMSNorm + ggml_mul,
+ * squared-ReLU gate product, soft_max_ext). Everything is plain C: pointers, sizes, status codes.
+ *
+ * Conventions (ggml's):
+ *   - A tensor is described by b2s_tensor {type, ne[4], nb[4], data}; ne[0] is the innermost
+ *     (contiguous) dimension, nb[] are byte strides (src/models/smolvla/vision.cpp:477-480 builds
+ *     weights as ne = [in_features, out_features]).
+ *   - mul_mat(W, X): W ne=[K,N] (i2_s), X ne=[K,M] f32 -> Y ne=[N,M] f32, Y[m][n] = sum_k W[n][k] X[m][k]
+ *     through per-token int8 quantization of X (see b2s_act_quant).
+ *   - Every data pointer passed to an entry point that takes a stream is DEVICE memory of the current
+ *     CUDA device; `stream` is a cudaStream_t (NULL = legacy default stream).
+ *   - Calls never abort and never throw. They return B2S_OK (0) or a negative b2s_status; the message
+ *     of the last failure on the calling thread is b2s_last_error(). Shape, type and alignment errors
+ *     are reported before anything is launched.
+ *   - Entry points that take a stream only enqueue work; a bounded wait that ran out inside a kernel
+ *     is reported by b2s_device_error() after the stream is synchronized.
+ *
+ * i2_s byte layout (flattened over the tensor, n = ne0*ne1 a multiple of 128): weight g = r*K + k is the
+ * 2-bit code at bit shift 6-2*((g%128)/32) of byte 32*(g/128) + (g%128)%32; codes 0,1,2 mean -1,0,+1;
+ * the n/4 code bytes are followed by 32 bytes whose first four hold the fp32 scale. nbytes = n/4 + 32.
+ * This is the x86 I2_S layout of microsoft/BitNet's ggml fork (quantize_i2_s), which the reference
+ * would load through gguf_loader::load as opaque ggml_nbytes() bytes (src/models/gguf_loader.cpp:115-137).
+ */
+#ifndef B2S_H
+#define B2S_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define B2S_VERSION_MAJOR 0
+#define B2S_VERSION_MINOR 1
+
+typedef enum b2s_status {
+    B2S_OK = 0,
+    B2S_ERR_INVALID_ARG = -1,    /* null pointer, bad shape, inconsistent strides */
+    B2S_ERR_UNSUPPORTED = -2,    /* type / layout / alignment this op does not implement */
+    B2S_ERR_WORKSPACE = -3,      /* workspace missing or smaller than b2s_mul_mat_workspace_size() */
+    B2S_ERR_CUDA = -4,           /* CUDA runtime or launch error (message has the CUDA error string) */
+    B2S_ERR_DEVICE = -5,         /* current device is not an sm_100 (B200-class) GPU */
+    B2S_ERR_DEVICE_TIMEOUT = -6  /* a kernel's bounded wait ran out (see b2s_device_error) */
+} b2s_status;
+
+/* Tensor types. F32/I8/I32 keep ggml's numeric ids (GGML_TYPE_F32=0, I8=24, I32=26). I2_S is the
+ * flattened BitNet-fork layout above; I2_S_R is this library's row-padded device layout (each row
+ * padded to a multiple of 128 weights with zero codes, scale after the codes), produced by
+ * b2s_i2s_repack_rows and required when ne0 % 128 != 0. For ne0 % 128 == 0 the two are identical. */
+typedef enum b2s_type {
+    B2S_TYPE_F32 = 0,
+    B2S_TYPE_I8 = 24,
+    B2S_TYPE_I32 = 26,
+    B2S_TYPE_I2_S = 36,
+    B2S_TYPE_I2_S_R = 1036
+} b2s_type;
+
+/* Mirrors the fields of ggml_tensor that an op reads: type, ne[4], nb[4], data. */
+typedef struct b2s_tensor {
+    int32_t type;
+    int64_t ne[4];
+    size_t nb[4];
+    void *data;
+} b2s_tensor;
+
+/* ---------------------------------------------------------------- library / errors */
+const char *b2s_version(void);
+/* Message of the last failed call on this thread ("" if none). */
+const char *b2s_last_error(void);
+/* B2S_OK if the current CUDA device is sm_100 (compute capability 10.0). */
+int b2s_device_check(void);
+/* Reads (and with clear != 0 resets) the device error word of the current device: bit 0 = a pipeline
+ * wait timed out, bit 1 = a drain wait at kernel exit timed out. Synchronous. */
+int b2s_device_error(uint32_t *out_bits, int clear);
+
+/* ---------------------------------------------------------------- i2_s type traits (host) */
+/* Bytes of an i2_s tensor of nrow rows x n_per_row weights (ggml_nbytes for GGML_TYPE_I2_S). */
+size_t b2s_i2s_nbytes(int64_t nrow, int64_t n_per_row);
+/* Bytes of the row-padded device layout. */
+size_t b2s_i2s_r_nbytes(int64_t nrow, int64_t n_per_row);
+/* from_float trait (host): pack float weights that are already ternary times a scale; the scale is
+ * max|w| and |w| < 1e-6 counts as zero. Returns nbytes, or 0 if nrow*n_per_row % 128 != 0.
+ * Replaces the fork's quantize_i2_s as called by a converter (cf. the ctypes bulk-quantizer of
+ * tools/quant/quantize-vla-gguf.py:335-360). */
+size_t b2s_i2s_quantize(const float *src, void *dst, int64_t nrow, int64_t n_per_row);
+/* to_float trait (host): dst = t * scale. Returns 0 on success, negative on bad arguments. */
+int b2s_i2s_dequantize(const void *src, float *dst, int64_t nrow, int64_t n_per_row);
+
+/* ---------------------------------------------------------------- device entry points */
+/* Load-time repack (device): flattened i2_s -> row-padded I2_S_R. dst holds b2s_i2s_r_nbytes bytes. */
+int b2s_i2s_repack_rows(const void *src, void *dst, int64_t nrow, int64_t n_per_row, void *stream);
+
+/* Per-token act-quant (the vec_dot_type conversion of src1 inside MUL_MAT):
+ *   s[m] = 127 / max(1e-5, max_k |x[m,k]|), q[m,k] = clamp(round_half_away(x*s), -128, 127),
+ *   sums[m] = sum_k q[m,k] (sums may be NULL). x rows have stride ldx floats, q rows ldq bytes. */
+int b2s_act_quant(const float *x, int64_t M, int64_t K, int64_t ldx, int8_t *q, int64_t ldq, float *s,
+                  int32_t *sums, void *stream);
+
+/* RMSNorm + weight + act-quant in one pass (ggml_rms_norm(x, eps) then ggml_mul(., g) then the
+ * act-quant above; src/models/smolvla/action_expert.cpp:731-736). g may be NULL (no weight). The
+ * normalized fp32 row is not written. */
+int b2s_rms_norm_act_quant(const float *x, const float *g, int64_t M, int64_t K, int64_t ldx, float eps,
+                           int8_t *q, int64_t ldq, float *s, int32_t *sums, void *stream);
+
+/* Workspace bytes b2s_mul_mat needs for these operands (int8 activations, scales, sums). */
+size_t b2s_mul_mat_workspace_size(const b2s_tensor *W, const b2s_tensor *X);
+
+/* The MUL_MAT node: Y = mul_mat(W, X). W: I2_S (ne0 % 128 == 0) or I2_S_R, ne=[K,N], contiguous;
+ * X: F32 ne=[K,M], rows contiguous (nb[0] = 4); Y: F32 ne=[N,M], rows contiguous. Uses the caller's
+ * workspace for the quantized activations; allocates nothing. Decode sizes (M <= 8) run the dp4a GEMV,
+ * larger M the tcgen05 tensor-core GEMM. */
+int b2s_mul_mat(const b2s_tensor *W, const b2s_tensor *X, b2s_tensor *Y, void *workspace, size_t workspace_bytes,
+                void *stream);
+
+/* MUL_MAT on already-quantized activations (producer-fused path): q [M x ldq] int8 (ldq % 16 == 0,
+ * 16-byte aligned), s [M], sums [M] from b2s_act_quant / b2s_rms_norm_act_quant. Y [M x ldy] f32. */
+int b2s_mul_mat_q8(const b2s_tensor *W, const int8_t *q, int64_t ldq, const float *s, const int32_t *sums,
+                   int64_t M, float *Y, int64_t ldy, void *stream);
+/* Same with the kernel chosen explicitly: path 0 = automatic, 1 = dp4a GEMV (any M, run in token groups
+ * of 8), 2 = tcgen05 tensor-core GEMM (any M). For tests and tuning; results are identical. */
+int b2s_mul_mat_q8_ex(const b2s_tensor *W, const int8_t *q, int64_t ldq, const float *s, const int32_t *sums,
+                      int64_t M, float *Y, int64_t ldy, int path, void *stream);
+
+/* FFN gate/up with the squared-ReLU gate product fused into the epilogue:
+ *   P[m,n] = relu(G)^2 * U,  G = mul_mat(W_gate, X), U = mul_mat(W_up, X)  (ggml_relu, ggml_sqr,
+ *   ggml_mul in a BitNet-style FFN), from quantized activations as in b2s_mul_mat_q8. */
+int b2s_ffn_gate_up_sqrelu_q8(const b2s_tensor *W_gate, const b2s_tensor *W_up, const int8_t *q, int64_t ldq,
+                              const float *s, const int32_t *sums, int64_t M, float *P, int64_t ldp, void *stream);
+
+/* Workspace bytes for b2s_ffn_block with M tokens, hidden H and FFN width F. */
+size_t b2s_ffn_block_workspace_size(int64_t M, int64_t H, int64_t F);
+
+/* Whole FFN block: Y = down(rms_norm2(relu(gate(xn))^2 * up(xn))), xn = rms_norm1(X); the BitNet
+ * FFN (RMSNorm(H) -> gate/up H->F -> squared-ReLU product -> RMSNorm(F) -> down F->H). X, Y [M x H]
+ * f32 contiguous; g1 [H], g2 [F] norm weights (may be NULL). Four kernel launches, no allocation. */
+int b2s_ffn_block(const float *X, int64_t M, const float *g1, const float *g2, float eps, const b2s_tensor *W_gate,
+                  const b2s_tensor *W_up, const b2s_tensor *W_down, float *Y, void *workspace,
+                  size_t workspace_bytes, void *stream);
+
+/* ggml_soft_max_ext(x, mask, scale, 0.0f): y[m,:] = softmax(x[m,:]*scale + mask[m % mask_rows,:]).
+ * mask may be NULL. Rows contiguous, N columns (src/models/smolvla/action_expert.cpp:773). */
+int b2s_soft_max_ext(const float *x, const float *mask, int64_t mask_rows, int64_t M, int64_t N, float scale,
+                     float *y, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* B2S_H */

@@ -1,0 +1,221 @@
+"""ctypes wrapper over the oracle library (TEST INFRASTRUCTURE).
+
+The oracle is the CPU restatement of the i2_s mul_mat path (algorithm, provenance and byte layout in
+``i2s_oracle.h``). Only ``tests/``, ``__graft_entry__.smoke()`` and the CPU-baseline leg of ``bench.py``
+may import this module; the product library never does.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+_LIB_PATH = os.path.join(_HERE, "liboracle.so")
+_lib = None
+
+_f32p = np.ctypeslib.ndpointer(np.float32, flags="C_CONTIGUOUS")
+_u8p = np.ctypeslib.ndpointer(np.uint8, flags="C_CONTIGUOUS")
+_i8p = np.ctypeslib.ndpointer(np.int8, flags="C_CONTIGUOUS")
+_i32p = np.ctypeslib.ndpointer(np.int32, flags="C_CONTIGUOUS")
+_i64 = C.c_int64
+
+
+def build() -> str:
+    """Compile the oracle with its Makefile (gcc, -ffp-contract=off)."""
+    subprocess.run(["make", "-s", "-C", _HERE], check=True)
+    return _LIB_PATH
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(_LIB_PATH):
+            build()
+        L = C.CDLL(_LIB_PATH)
+        L.orc_i2s_nbytes.restype = C.c_size_t
+        L.orc_i2s_nbytes.argtypes = [_i64, _i64]
+        L.orc_i2s_r_nbytes.restype = C.c_size_t
+        L.orc_i2s_r_nbytes.argtypes = [_i64, _i64]
+        L.orc_i2s_quantize.restype = C.c_size_t
+        L.orc_i2s_quantize.argtypes = [_f32p, _u8p, _i64, _i64]
+        L.orc_i2s_pack_ternary.restype = C.c_size_t
+        L.orc_i2s_pack_ternary.argtypes = [_i8p, C.c_float, _u8p, _i64, _i64]
+        L.orc_i2s_unpack_ternary.restype = C.c_float
+        L.orc_i2s_unpack_ternary.argtypes = [_u8p, _i8p, _i64, _i64]
+        L.orc_i2s_dequantize.restype = None
+        L.orc_i2s_dequantize.argtypes = [_u8p, _f32p, _i64, _i64]
+        L.orc_i2s_to_rowpadded.restype = C.c_size_t
+        L.orc_i2s_to_rowpadded.argtypes = [_u8p, _u8p, _i64, _i64]
+        L.orc_act_quant.restype = None
+        L.orc_act_quant.argtypes = [_f32p, _i64, _i64, _i8p, _f32p, _i32p]
+        L.orc_gemm_i32.restype = None
+        L.orc_gemm_i32.argtypes = [_i8p, _i8p, _i64, _i64, _i64, _i32p]
+        L.orc_rescale.restype = None
+        L.orc_rescale.argtypes = [_i32p, _f32p, C.c_float, _i64, _i64, _f32p]
+        L.orc_mul_mat_i2s.restype = None
+        L.orc_mul_mat_i2s.argtypes = [_u8p, _f32p, _i64, _i64, _i64, _f32p]
+        L.orc_rms_norm.restype = None
+        L.orc_rms_norm.argtypes = [_f32p, C.c_void_p, _i64, _i64, C.c_float, _f32p]
+        L.orc_sqrelu_mul.restype = None
+        L.orc_sqrelu_mul.argtypes = [_f32p, _f32p, _i64, _f32p]
+        L.orc_soft_max_ext.restype = None
+        L.orc_soft_max_ext.argtypes = [_f32p, C.c_void_p, _i64, _i64, _i64, C.c_float, _f32p]
+        L.orc_ffn_block.restype = None
+        L.orc_ffn_block.argtypes = [_f32p, _i64, _i64, _i64, _f32p, _f32p, C.c_float,
+                                    _u8p, _u8p, _u8p, _f32p, C.c_void_p]
+        L.orc_fast_mul_mat_i2s.restype = None
+        L.orc_fast_mul_mat_i2s.argtypes = [_u8p, _f32p, _i64, _i64, _i64, _f32p, C.c_int]
+        L.orc_fast_ffn_block.restype = None
+        L.orc_fast_ffn_block.argtypes = [_f32p, _i64, _i64, _i64, _f32p, _f32p, C.c_float,
+                                         _u8p, _u8p, _u8p, _f32p, C.c_int]
+        L.orc_fast_isa.restype = C.c_int
+        L.orc_fast_isa.argtypes = []
+        _lib = L
+    return _lib
+
+
+def _c(a, dt):
+    return np.ascontiguousarray(a, dtype=dt)
+
+
+def _ptr(a):
+    return None if a is None else a.ctypes.data_as(C.c_void_p)
+
+
+def i2s_nbytes(N: int, K: int) -> int:
+    return int(lib().orc_i2s_nbytes(N, K))
+
+
+def i2s_quantize(w: np.ndarray) -> np.ndarray:
+    """Pack float weights [N, K] (ternary times a scale) into i2_s bytes."""
+    w = _c(w, np.float32)
+    N, K = w.shape
+    out = np.zeros(i2s_nbytes(N, K), np.uint8)
+    if lib().orc_i2s_quantize(w, out, N, K) == 0:
+        raise ValueError("i2_s needs N*K to be a multiple of 128")
+    return out
+
+
+def i2s_pack_ternary(t: np.ndarray, scale: float) -> np.ndarray:
+    t = _c(t, np.int8)
+    N, K = t.shape
+    out = np.zeros(i2s_nbytes(N, K), np.uint8)
+    if lib().orc_i2s_pack_ternary(t, float(scale), out, N, K) == 0:
+        raise ValueError("i2_s needs N*K to be a multiple of 128")
+    return out
+
+
+def i2s_unpack_ternary(packed: np.ndarray, N: int, K: int):
+    t = np.zeros((N, K), np.int8)
+    s = lib().orc_i2s_unpack_ternary(_c(packed, np.uint8), t, N, K)
+    return t, float(s)
+
+
+def i2s_dequantize(packed: np.ndarray, N: int, K: int) -> np.ndarray:
+    out = np.zeros((N, K), np.float32)
+    lib().orc_i2s_dequantize(_c(packed, np.uint8), out, N, K)
+    return out
+
+
+def i2s_to_rowpadded(packed: np.ndarray, N: int, K: int) -> np.ndarray:
+    out = np.zeros(int(lib().orc_i2s_r_nbytes(N, K)), np.uint8)
+    lib().orc_i2s_to_rowpadded(_c(packed, np.uint8), out, N, K)
+    return out
+
+
+def act_quant(x: np.ndarray):
+    x = _c(x, np.float32)
+    M, K = x.shape
+    q = np.zeros((M, K), np.int8)
+    s = np.zeros(M, np.float32)
+    sums = np.zeros(M, np.int32)
+    lib().orc_act_quant(x, M, K, q, s, sums)
+    return q, s, sums
+
+
+def gemm_i32(t: np.ndarray, q: np.ndarray) -> np.ndarray:
+    t = _c(t, np.int8)
+    q = _c(q, np.int8)
+    N, K = t.shape
+    M = q.shape[0]
+    acc = np.zeros((M, N), np.int32)
+    lib().orc_gemm_i32(t, q, M, N, K, acc)
+    return acc
+
+
+def rescale(acc: np.ndarray, s: np.ndarray, w_scale: float) -> np.ndarray:
+    acc = _c(acc, np.int32)
+    M, N = acc.shape
+    y = np.zeros((M, N), np.float32)
+    lib().orc_rescale(acc, _c(s, np.float32), float(w_scale), M, N, y)
+    return y
+
+
+def mul_mat_i2s(packed: np.ndarray, x: np.ndarray, N: int) -> np.ndarray:
+    x = _c(x, np.float32)
+    M, K = x.shape
+    y = np.zeros((M, N), np.float32)
+    lib().orc_mul_mat_i2s(_c(packed, np.uint8), x, M, N, K, y)
+    return y
+
+
+def rms_norm(x: np.ndarray, g, eps: float) -> np.ndarray:
+    x = _c(x, np.float32)
+    M, K = x.shape
+    g = None if g is None else _c(g, np.float32)
+    y = np.zeros((M, K), np.float32)
+    lib().orc_rms_norm(x, _ptr(g), M, K, float(eps), y)
+    return y
+
+
+def sqrelu_mul(g: np.ndarray, u: np.ndarray) -> np.ndarray:
+    g = _c(g, np.float32)
+    u = _c(u, np.float32)
+    p = np.zeros_like(g)
+    lib().orc_sqrelu_mul(g.reshape(-1), u.reshape(-1), g.size, p.reshape(-1))
+    return p
+
+
+def soft_max_ext(x: np.ndarray, mask, scale: float) -> np.ndarray:
+    x = _c(x, np.float32)
+    M, N = x.shape
+    mask = None if mask is None else _c(mask, np.float32)
+    mrows = 1 if mask is None else mask.shape[0]
+    y = np.zeros((M, N), np.float32)
+    lib().orc_soft_max_ext(x, _ptr(mask), mrows, M, N, float(scale), y)
+    return y
+
+
+def ffn_block(x, g1, g2, eps, w_gate, w_up, w_down, H, F, want_p=False):
+    x = _c(x, np.float32)
+    M = x.shape[0]
+    y = np.zeros((M, H), np.float32)
+    p = np.zeros((M, F), np.float32) if want_p else None
+    lib().orc_ffn_block(x, M, H, F, _c(g1, np.float32), _c(g2, np.float32), float(eps),
+                        _c(w_gate, np.uint8), _c(w_up, np.uint8), _c(w_down, np.uint8), y, _ptr(p))
+    return (y, p) if want_p else y
+
+
+def fast_mul_mat_i2s(packed, x, N, nthreads):
+    x = _c(x, np.float32)
+    M, K = x.shape
+    y = np.zeros((M, N), np.float32)
+    lib().orc_fast_mul_mat_i2s(_c(packed, np.uint8), x, M, N, K, y, int(nthreads))
+    return y
+
+
+def fast_ffn_block(x, g1, g2, eps, w_gate, w_up, w_down, H, F, nthreads):
+    x = _c(x, np.float32)
+    M = x.shape[0]
+    y = np.zeros((M, H), np.float32)
+    lib().orc_fast_ffn_block(x, M, H, F, _c(g1, np.float32), _c(g2, np.float32), float(eps),
+                             _c(w_gate, np.uint8), _c(w_up, np.uint8), _c(w_down, np.uint8), y,
+                             int(nthreads))
+    return y
+
+
+def fast_isa() -> int:
+    return int(lib().orc_fast_isa())

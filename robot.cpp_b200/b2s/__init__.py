@@ -1,0 +1,230 @@
+"""Python binding of libb2s.so, the B200 ternary i2_s mul_mat library (C ABI in include/b2s.h).
+
+This is the ctypes path a Python caller of the reference uses for native ggml code (the quant tool binds
+libggml-base the same way, tools/quant/quantize-vla-gguf.py:47-53). Device buffers and streams come from
+torch (plumbing only); every op runs the library's own CUDA kernels. There is no fallback: if the shared
+library is missing or fails to load, ``lib()`` raises.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libb2s.so")
+
+B2S_OK = 0
+B2S_ERR_INVALID_ARG = -1
+B2S_ERR_UNSUPPORTED = -2
+B2S_ERR_WORKSPACE = -3
+B2S_ERR_CUDA = -4
+B2S_ERR_DEVICE = -5
+B2S_ERR_DEVICE_TIMEOUT = -6
+
+TYPE_F32 = 0
+TYPE_I8 = 24
+TYPE_I32 = 26
+TYPE_I2_S = 36
+TYPE_I2_S_R = 1036
+
+# Every symbol include/b2s.h declares (checked by the CPU test suite against the built library).
+EXPORTED = [
+    "b2s_version", "b2s_last_error", "b2s_device_check", "b2s_device_error",
+    "b2s_i2s_nbytes", "b2s_i2s_r_nbytes", "b2s_i2s_quantize", "b2s_i2s_dequantize",
+    "b2s_i2s_repack_rows", "b2s_act_quant", "b2s_rms_norm_act_quant", "b2s_mul_mat_workspace_size",
+    "b2s_mul_mat", "b2s_mul_mat_q8", "b2s_mul_mat_q8_ex", "b2s_ffn_gate_up_sqrelu_q8",
+    "b2s_ffn_block_workspace_size", "b2s_ffn_block", "b2s_soft_max_ext",
+]
+
+
+class B2SError(RuntimeError):
+    def __init__(self, status: int, msg: str):
+        super().__init__(f"b2s status {status}: {msg}")
+        self.status = status
+
+
+class Tensor(C.Structure):
+    """Mirror of ``b2s_tensor`` (= the ggml_tensor fields an op reads)."""
+    _fields_ = [("type", C.c_int32), ("ne", C.c_int64 * 4), ("nb", C.c_size_t * 4), ("data", C.c_void_p)]
+
+
+_lib = None
+_vp = C.c_void_p
+_i64 = C.c_int64
+_TP = C.POINTER(Tensor)
+
+
+def lib():
+    """Load libb2s.so (raises if it has not been built)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise RuntimeError(f"{LIB_PATH} is missing: build it with `make -C robot.cpp_b200/csrc` "
+                               "(or __graft_entry__.build()); there is no CPU fallback")
+        L = C.CDLL(LIB_PATH)
+        sig = {
+            "b2s_version": (C.c_char_p, []),
+            "b2s_last_error": (C.c_char_p, []),
+            "b2s_device_check": (C.c_int, []),
+            "b2s_device_error": (C.c_int, [C.POINTER(C.c_uint32), C.c_int]),
+            "b2s_i2s_nbytes": (C.c_size_t, [_i64, _i64]),
+            "b2s_i2s_r_nbytes": (C.c_size_t, [_i64, _i64]),
+            "b2s_i2s_quantize": (C.c_size_t, [_vp, _vp, _i64, _i64]),
+            "b2s_i2s_dequantize": (C.c_int, [_vp, _vp, _i64, _i64]),
+            "b2s_i2s_repack_rows": (C.c_int, [_vp, _vp, _i64, _i64, _vp]),
+            "b2s_act_quant": (C.c_int, [_vp, _i64, _i64, _i64, _vp, _i64, _vp, _vp, _vp]),
+            "b2s_rms_norm_act_quant": (C.c_int, [_vp, _vp, _i64, _i64, _i64, C.c_float, _vp, _i64, _vp, _vp, _vp]),
+            "b2s_mul_mat_workspace_size": (C.c_size_t, [_TP, _TP]),
+            "b2s_mul_mat": (C.c_int, [_TP, _TP, _TP, _vp, C.c_size_t, _vp]),
+            "b2s_mul_mat_q8": (C.c_int, [_TP, _vp, _i64, _vp, _vp, _i64, _vp, _i64, _vp]),
+            "b2s_mul_mat_q8_ex": (C.c_int, [_TP, _vp, _i64, _vp, _vp, _i64, _vp, _i64, C.c_int, _vp]),
+            "b2s_ffn_gate_up_sqrelu_q8": (C.c_int, [_TP, _TP, _vp, _i64, _vp, _vp, _i64, _vp, _i64, _vp]),
+            "b2s_ffn_block_workspace_size": (C.c_size_t, [_i64, _i64, _i64]),
+            "b2s_ffn_block": (C.c_int, [_vp, _i64, _vp, _vp, C.c_float, _TP, _TP, _TP, _vp, _vp, C.c_size_t, _vp]),
+            "b2s_soft_max_ext": (C.c_int, [_vp, _vp, _i64, _i64, _i64, C.c_float, _vp, _vp]),
+        }
+        for name, (res, args) in sig.items():
+            f = getattr(L, name)
+            f.restype = res
+            f.argtypes = args
+        _lib = L
+    return _lib
+
+
+def last_error() -> str:
+    return lib().b2s_last_error().decode()
+
+
+def check(status: int) -> None:
+    if status != B2S_OK:
+        raise B2SError(status, last_error())
+
+
+def version() -> str:
+    return lib().b2s_version().decode()
+
+
+def device_error(clear: bool = True) -> int:
+    v = C.c_uint32(0)
+    check(lib().b2s_device_error(C.byref(v), int(clear)))
+    return int(v.value)
+
+
+# ---------------------------------------------------------------------------------------------- tensors
+def _ptr(t) -> int | None:
+    if t is None:
+        return None
+    return int(t.data_ptr())
+
+
+def _stream(stream) -> int | None:
+    if stream is None:
+        import torch
+        return int(torch.cuda.current_stream().cuda_stream)
+    return int(stream.cuda_stream) if hasattr(stream, "cuda_stream") else int(stream)
+
+
+def i2s_tensor(buf, N: int, K: int, rowpadded: bool = False) -> Tensor:
+    """Descriptor of an i2_s weight (ne=[K,N]) stored in the device byte buffer ``buf``."""
+    t = Tensor()
+    t.type = TYPE_I2_S_R if rowpadded else TYPE_I2_S
+    t.ne[:] = [K, N, 1, 1]
+    rb = (((K + 127) // 128) * 128 // 4) if rowpadded else K // 4
+    t.nb[:] = [1, rb, rb * N, rb * N]
+    t.data = _ptr(buf)
+    return t
+
+
+def f32_tensor(x) -> Tensor:
+    """Descriptor of a 2-D float32 torch tensor [rows, cols] as ggml ne=[cols, rows]."""
+    assert x.dtype.is_floating_point and x.element_size() == 4 and x.dim() == 2 and x.stride(1) == 1
+    t = Tensor()
+    t.type = TYPE_F32
+    t.ne[:] = [x.shape[1], x.shape[0], 1, 1]
+    t.nb[:] = [4, x.stride(0) * 4, x.stride(0) * 4 * x.shape[0], x.stride(0) * 4 * x.shape[0]]
+    t.data = _ptr(x)
+    return t
+
+
+def i2s_nbytes(N: int, K: int) -> int:
+    return int(lib().b2s_i2s_nbytes(N, K))
+
+
+def i2s_r_nbytes(N: int, K: int) -> int:
+    return int(lib().b2s_i2s_r_nbytes(N, K))
+
+
+def i2s_quantize_host(w):
+    """from_float on the host: numpy float32 [N, K] -> numpy uint8 i2_s bytes."""
+    import numpy as np
+    w = np.ascontiguousarray(w, dtype=np.float32)
+    N, K = w.shape
+    out = np.zeros(i2s_nbytes(N, K), np.uint8)
+    n = lib().b2s_i2s_quantize(w.ctypes.data, out.ctypes.data, N, K)
+    if n == 0:
+        raise B2SError(B2S_ERR_UNSUPPORTED, last_error())
+    return out
+
+
+def i2s_dequantize_host(buf, N: int, K: int):
+    import numpy as np
+    buf = np.ascontiguousarray(buf, dtype=np.uint8)
+    out = np.zeros((N, K), np.float32)
+    check(lib().b2s_i2s_dequantize(buf.ctypes.data, out.ctypes.data, N, K))
+    return out
+
+
+# ---------------------------------------------------------------------------------------------- device ops
+def repack_rows(src, dst, N: int, K: int, stream=None) -> None:
+    check(lib().b2s_i2s_repack_rows(_ptr(src), _ptr(dst), N, K, _stream(stream)))
+
+
+def act_quant(x, q, s, sums=None, stream=None) -> None:
+    M, K = x.shape
+    check(lib().b2s_act_quant(_ptr(x), M, K, x.stride(0), _ptr(q), q.stride(0), _ptr(s), _ptr(sums), _stream(stream)))
+
+
+def rms_norm_act_quant(x, g, eps: float, q, s, sums=None, stream=None) -> None:
+    M, K = x.shape
+    check(lib().b2s_rms_norm_act_quant(_ptr(x), _ptr(g), M, K, x.stride(0), float(eps), _ptr(q), q.stride(0),
+                                       _ptr(s), _ptr(sums), _stream(stream)))
+
+
+def mul_mat_workspace_size(W: Tensor, X: Tensor) -> int:
+    return int(lib().b2s_mul_mat_workspace_size(C.byref(W), C.byref(X)))
+
+
+def mul_mat(W: Tensor, x, y, workspace, stream=None) -> None:
+    X = f32_tensor(x)
+    Y = f32_tensor(y)
+    check(lib().b2s_mul_mat(C.byref(W), C.byref(X), C.byref(Y), _ptr(workspace),
+                            workspace.numel() * workspace.element_size(), _stream(stream)))
+
+
+def mul_mat_q8(W: Tensor, q, s, sums, y, path: int = 0, stream=None) -> None:
+    M = q.shape[0]
+    check(lib().b2s_mul_mat_q8_ex(C.byref(W), _ptr(q), q.stride(0), _ptr(s), _ptr(sums), M, _ptr(y), y.stride(0),
+                                  int(path), _stream(stream)))
+
+
+def ffn_gate_up_sqrelu_q8(Wg: Tensor, Wu: Tensor, q, s, sums, p, stream=None) -> None:
+    M = q.shape[0]
+    check(lib().b2s_ffn_gate_up_sqrelu_q8(C.byref(Wg), C.byref(Wu), _ptr(q), q.stride(0), _ptr(s), _ptr(sums), M,
+                                          _ptr(p), p.stride(0), _stream(stream)))
+
+
+def ffn_block_workspace_size(M: int, H: int, F: int) -> int:
+    return int(lib().b2s_ffn_block_workspace_size(M, H, F))
+
+
+def ffn_block(x, g1, g2, eps: float, Wg: Tensor, Wu: Tensor, Wd: Tensor, y, workspace, stream=None) -> None:
+    M = x.shape[0]
+    check(lib().b2s_ffn_block(_ptr(x), M, _ptr(g1), _ptr(g2), float(eps), C.byref(Wg), C.byref(Wu), C.byref(Wd),
+                              _ptr(y), _ptr(workspace), workspace.numel() * workspace.element_size(),
+                              _stream(stream)))
+
+
+def soft_max_ext(x, mask, scale: float, y, stream=None) -> None:
+    M, N = x.shape
+    mrows = 1 if mask is None else mask.shape[0]
+    check(lib().b2s_soft_max_ext(_ptr(x), _ptr(mask), mrows, M, N, float(scale), _ptr(y), _stream(stream)))

@@ -1,0 +1,460 @@
+// b2s_api.cu -- the extern "C" boundary of libb2s.so (declared in include/b2s.h).
+//
+// Validates ggml-style tensor descriptors, owns no device memory (callers pass workspaces), builds the
+// TMA descriptors for the tensor-core path and dispatches between the decode GEMV and the tcgen05 GEMM.
+// Error convention follows the reference's bool/status-plus-message style
+// (src/models/gguf_loader.cpp:246-254, robot_server/session.cpp:132-135): negative status + message.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "b2s.h"
+#include "b2s_common.cuh"
+#include "b2s_internal.h"
+
+namespace {
+
+thread_local std::string t_last_error;
+
+int fail(int code, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    t_last_error = buf;
+    return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+    return fail(B2S_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
+// ---------------------------------------------------------------- device check (cached per device)
+int check_device() {
+    static int cache[128];  // 0 unknown, 1 ok, 2 bad
+    int dev = -1;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+    if (dev < 0 || dev >= 128) return fail(B2S_ERR_DEVICE, "device index %d out of range", dev);
+    if (cache[dev] == 0) {
+        int major = 0, minor = 0;
+        if ((e = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev)) != cudaSuccess)
+            return cuda_fail(e, "cudaDeviceGetAttribute");
+        if ((e = cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev)) != cudaSuccess)
+            return cuda_fail(e, "cudaDeviceGetAttribute");
+        cache[dev] = (major == 10 && minor == 0) ? 1 : 2;
+        if (cache[dev] == 2) return fail(B2S_ERR_DEVICE, "device %d is sm_%d%d; this library is built for sm_100a", dev,
+                                         major, minor);
+    }
+    return cache[dev] == 1 ? B2S_OK : fail(B2S_ERR_DEVICE, "device %d is not sm_100", dev);
+}
+
+// ---------------------------------------------------------------- TMA descriptor encoding
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    });
+    return fn;
+}
+
+// 2D u8 tensor map: inner dim `cols` bytes, `rows` rows of stride `ld` bytes, box box_c x box_r.
+int make_tmap_u8(CUtensorMap* m, const void* ptr, uint64_t cols, uint64_t rows, uint64_t ld, uint32_t box_c,
+                 uint32_t box_r, bool swizzle128) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return fail(B2S_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+    if ((reinterpret_cast<uintptr_t>(ptr) & 15) != 0) return fail(B2S_ERR_UNSUPPORTED, "TMA base not 16-byte aligned");
+    if (ld % 16 != 0) return fail(B2S_ERR_UNSUPPORTED, "TMA row stride %llu not a multiple of 16 bytes",
+                                  (unsigned long long)ld);
+    cuuint64_t dims[2] = {cols, rows};
+    cuuint64_t strides[1] = {ld};
+    cuuint32_t box[2] = {box_c, box_r};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(B2S_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return B2S_OK;
+}
+
+// ---------------------------------------------------------------- descriptor validation
+int weight_view(const b2s_tensor* W, b2s::I2sWeight* out, const char* name) {
+    if (!W) return fail(B2S_ERR_INVALID_ARG, "%s is NULL", name);
+    if (!W->data) return fail(B2S_ERR_INVALID_ARG, "%s->data is NULL", name);
+    const int64_t K = W->ne[0], N = W->ne[1];
+    if (K <= 0 || N <= 0 || W->ne[2] != 1 || W->ne[3] != 1)
+        return fail(B2S_ERR_INVALID_ARG, "%s must be 2-D with positive ne0/ne1 (got %lld x %lld x %lld x %lld)", name,
+                    (long long)W->ne[0], (long long)W->ne[1], (long long)W->ne[2], (long long)W->ne[3]);
+    if ((reinterpret_cast<uintptr_t>(W->data) & 15) != 0)
+        return fail(B2S_ERR_UNSUPPORTED, "%s->data must be 16-byte aligned", name);
+    if (K % 16 != 0) return fail(B2S_ERR_UNSUPPORTED, "%s: ne0 (K=%lld) must be a multiple of 16", name, (long long)K);
+    const int64_t Kp = b2s::round_up(K, b2s::kQK);
+    if (W->type == B2S_TYPE_I2_S) {
+        if (K % b2s::kQK != 0)
+            return fail(B2S_ERR_UNSUPPORTED,
+                        "%s: i2_s with ne0 %% 128 != 0 (K=%lld) must be repacked with b2s_i2s_repack_rows first", name,
+                        (long long)K);
+    } else if (W->type != B2S_TYPE_I2_S_R) {
+        return fail(B2S_ERR_UNSUPPORTED, "%s: type %d is not i2_s", name, (int)W->type);
+    }
+    out->codes = static_cast<const uint8_t*>(W->data);
+    out->scale = reinterpret_cast<const float*>(static_cast<const uint8_t*>(W->data) + N * Kp / 4);
+    out->N = N;
+    out->K = K;
+    out->Kp = Kp;
+    return B2S_OK;
+}
+
+// Rows of a ggml f32 tensor as a 2-D [rows x ne0] view with row stride ld (elements).
+int f32_rows(const b2s_tensor* T, const char* name, int64_t* rows, int64_t* cols, int64_t* ld) {
+    if (!T) return fail(B2S_ERR_INVALID_ARG, "%s is NULL", name);
+    if (!T->data) return fail(B2S_ERR_INVALID_ARG, "%s->data is NULL", name);
+    if (T->type != B2S_TYPE_F32) return fail(B2S_ERR_UNSUPPORTED, "%s must be f32 (type %d)", name, (int)T->type);
+    if (T->nb[0] != sizeof(float)) return fail(B2S_ERR_UNSUPPORTED, "%s rows must be contiguous (nb0=4)", name);
+    if (T->ne[0] <= 0 || T->ne[1] <= 0 || T->ne[2] <= 0 || T->ne[3] <= 0)
+        return fail(B2S_ERR_INVALID_ARG, "%s has a non-positive dimension", name);
+    if (T->nb[1] % sizeof(float) != 0 || T->nb[1] < T->ne[0] * sizeof(float))
+        return fail(B2S_ERR_INVALID_ARG, "%s: nb1 (%zu) inconsistent with ne0 (%lld)", name, T->nb[1], (long long)T->ne[0]);
+    // Higher dims must collapse into rows with a uniform stride.
+    if ((T->ne[2] > 1 && T->nb[2] != T->nb[1] * T->ne[1]) || (T->ne[3] > 1 && T->nb[3] != T->nb[2] * T->ne[2]))
+        return fail(B2S_ERR_UNSUPPORTED, "%s: dims 2/3 must be contiguous over rows", name);
+    *rows = T->ne[1] * T->ne[2] * T->ne[3];
+    *cols = T->ne[0];
+    *ld = (int64_t)(T->nb[1] / sizeof(float));
+    return B2S_OK;
+}
+
+struct WsLayout {
+    size_t q_off, s_off, sum_off, total;
+    int64_t ldq;
+};
+size_t a256(size_t v) { return (v + 255) & ~size_t(255); }
+WsLayout act_ws(int64_t M, int64_t K, size_t base = 0) {
+    WsLayout l;
+    l.ldq = b2s::round_up(K, 16);
+    l.q_off = a256(base);
+    l.s_off = a256(l.q_off + (size_t)(M * l.ldq));
+    l.sum_off = a256(l.s_off + sizeof(float) * (size_t)M);
+    l.total = a256(l.sum_off + sizeof(int32_t) * (size_t)M);
+    return l;
+}
+
+int launched(cudaError_t e, const char* what) {
+    if (e != cudaSuccess) return cuda_fail(e, what);
+    return B2S_OK;
+}
+
+// Tensor-core token tile: split M into the fewest tiles of at most max_bn, rounded up to 16.
+int pick_bn(int64_t M, int max_bn) {
+    const int64_t tiles = b2s::ceil_div(M, max_bn);
+    int64_t bn = b2s::round_up(b2s::ceil_div(M, tiles), 16);
+    if (bn > max_bn) bn = max_bn;
+    if (bn < 16) bn = 16;
+    return (int)bn;
+}
+
+int run_tc(const b2s::I2sWeight& w0, const b2s::I2sWeight* w1, const int8_t* q, int64_t ldq, const float* s,
+           int64_t M, float* Y, int64_t ldy, int mode, cudaStream_t st) {
+    if ((reinterpret_cast<uintptr_t>(q) & 15) != 0 || ldq % 16 != 0)
+        return fail(B2S_ERR_UNSUPPORTED, "tensor-core path needs 16-byte aligned q with ldq %% 16 == 0");
+    if (M > (int64_t)0x7fffffff || w0.N > (int64_t)0x7fffffff) return fail(B2S_ERR_UNSUPPORTED, "size exceeds int32");
+    b2s::TcGemmArgs a;
+    memset(&a, 0, sizeof(a));
+    a.bn = pick_bn(M, mode == 1 ? 192 : 256);
+    int rc;
+    if ((rc = make_tmap_u8(&a.tmap_q, q, (uint64_t)w0.K, (uint64_t)M, (uint64_t)ldq, 128, (uint32_t)a.bn, true)))
+        return rc;
+    if ((rc = make_tmap_u8(&a.tmap_w0, w0.codes, (uint64_t)(w0.Kp / 4), (uint64_t)w0.N, (uint64_t)(w0.Kp / 4), 32,
+                           128, false)))
+        return rc;
+    if (mode == 1) {
+        if ((rc = make_tmap_u8(&a.tmap_w1, w1->codes, (uint64_t)(w1->Kp / 4), (uint64_t)w1->N, (uint64_t)(w1->Kp / 4),
+                               32, 128, false)))
+            return rc;
+    } else {
+        a.tmap_w1 = a.tmap_w0;
+    }
+    a.w0_scale = w0.scale;
+    a.w1_scale = (mode == 1) ? w1->scale : w0.scale;
+    a.s = s;
+    a.y = Y;
+    a.ldy = ldy;
+    a.M = (int)M;
+    a.N = (int)w0.N;
+    a.K = (int)w0.K;
+    a.Kp = (int)w0.Kp;
+    a.mode = mode;
+    return launched(b2s::launch_gemm_i2s_tc(a, st), "gemm_i2s_tc launch");
+}
+
+// path: 0 auto, 1 GEMV, 2 tensor cores
+int mul_mat_q8_impl(const b2s::I2sWeight& w, const int8_t* q, int64_t ldq, const float* s, const int32_t* sums,
+                    int64_t M, float* Y, int64_t ldy, int path, cudaStream_t st) {
+    if (M <= 0) return B2S_OK;
+    if (path == 0) path = (M <= 8) ? 1 : 2;
+    if (path == 1) {
+        b2s::Q8Act a{q, s, sums, M, w.K, ldq};
+        return launched(b2s::launch_gemv_i2s(w, a, Y, ldy, st), "gemv_i2s launch");
+    }
+    return run_tc(w, nullptr, q, ldq, s, M, Y, ldy, 0, st);
+}
+
+}  // namespace
+
+// ==================================================================================================
+extern "C" {
+
+const char* b2s_version(void) { return "b2s 0.1 (sm_100a)"; }
+
+const char* b2s_last_error(void) { return t_last_error.c_str(); }
+
+int b2s_device_check(void) { return check_device(); }
+
+int b2s_device_error(uint32_t* out_bits, int clear) {
+    if (!out_bits) return fail(B2S_ERR_INVALID_ARG, "out_bits is NULL");
+    int rc = check_device();
+    if (rc) return rc;
+    unsigned int v = 0;
+    cudaError_t e = cudaMemcpyFromSymbol(&v, b2s::g_device_error, sizeof(v));
+    if (e != cudaSuccess) return cuda_fail(e, "read device error word");
+    if (clear) {
+        const unsigned int z = 0;
+        e = cudaMemcpyToSymbol(b2s::g_device_error, &z, sizeof(z));
+        if (e != cudaSuccess) return cuda_fail(e, "clear device error word");
+    }
+    *out_bits = v;
+    return B2S_OK;
+}
+
+size_t b2s_i2s_nbytes(int64_t nrow, int64_t n_per_row) {
+    if (nrow <= 0 || n_per_row <= 0) return 0;
+    return (size_t)(nrow * n_per_row / 4) + 32;
+}
+
+size_t b2s_i2s_r_nbytes(int64_t nrow, int64_t n_per_row) {
+    if (nrow <= 0 || n_per_row <= 0) return 0;
+    return (size_t)(nrow * b2s::round_up(n_per_row, b2s::kQK) / 4) + 32;
+}
+
+size_t b2s_i2s_quantize(const float* src, void* dst, int64_t nrow, int64_t n_per_row) {
+    if (!src || !dst || nrow <= 0 || n_per_row <= 0) {
+        fail(B2S_ERR_INVALID_ARG, "b2s_i2s_quantize: bad arguments");
+        return 0;
+    }
+    const int64_t n = nrow * n_per_row;
+    if (n % b2s::kQK != 0) {
+        fail(B2S_ERR_UNSUPPORTED, "b2s_i2s_quantize: nrow*n_per_row must be a multiple of 128");
+        return 0;
+    }
+    uint8_t* out = static_cast<uint8_t*>(dst);
+    double amax = 0.0;
+    for (int64_t i = 0; i < n; ++i) {
+        const double a = src[i] < 0 ? -(double)src[i] : (double)src[i];
+        if (a > amax) amax = a;
+    }
+    memset(out, 0, (size_t)(n / 4) + 32);
+    for (int64_t blk = 0; blk < n / b2s::kQK; ++blk) {
+        for (int j = 0; j < b2s::kQK; ++j) {
+            const float v = src[blk * b2s::kQK + j];
+            const double av = v < 0 ? -(double)v : (double)v;
+            const unsigned code = (av < 1e-6) ? 1u : ((double)v * amax > 0 ? 2u : 0u);
+            out[32 * blk + (j & 31)] |= (uint8_t)(code << (6 - 2 * (j >> 5)));
+        }
+    }
+    const float sc = (float)amax;
+    memcpy(out + n / 4, &sc, sizeof(float));
+    return (size_t)(n / 4) + 32;
+}
+
+int b2s_i2s_dequantize(const void* src, float* dst, int64_t nrow, int64_t n_per_row) {
+    if (!src || !dst || nrow <= 0 || n_per_row <= 0) return fail(B2S_ERR_INVALID_ARG, "b2s_i2s_dequantize: bad arguments");
+    const int64_t n = nrow * n_per_row;
+    if (n % b2s::kQK != 0) return fail(B2S_ERR_UNSUPPORTED, "b2s_i2s_dequantize: n must be a multiple of 128");
+    const uint8_t* in = static_cast<const uint8_t*>(src);
+    float sc;
+    memcpy(&sc, in + n / 4, sizeof(float));
+    for (int64_t g = 0; g < n; ++g) {
+        const int64_t blk = g / b2s::kQK;
+        const int j = (int)(g % b2s::kQK);
+        const int code = (in[32 * blk + (j & 31)] >> (6 - 2 * (j >> 5))) & 3;
+        dst[g] = (float)(code - 1) * sc;
+    }
+    return B2S_OK;
+}
+
+int b2s_i2s_repack_rows(const void* src, void* dst, int64_t nrow, int64_t n_per_row, void* stream) {
+    int rc = check_device();
+    if (rc) return rc;
+    if (!src || !dst || nrow <= 0 || n_per_row <= 0) return fail(B2S_ERR_INVALID_ARG, "b2s_i2s_repack_rows: bad arguments");
+    if ((nrow * n_per_row) % b2s::kQK != 0) return fail(B2S_ERR_UNSUPPORTED, "i2_s needs n %% 128 == 0");
+    return launched(b2s::launch_repack_rows(static_cast<const uint8_t*>(src), static_cast<uint8_t*>(dst), nrow,
+                                            n_per_row, static_cast<cudaStream_t>(stream)),
+                    "repack_rows launch");
+}
+
+static int act_quant_common(const float* x, const float* g, bool norm, float eps, int64_t M, int64_t K, int64_t ldx,
+                            int8_t* q, int64_t ldq, float* s, int32_t* sums, void* stream) {
+    int rc = check_device();
+    if (rc) return rc;
+    if (!x || !q || !s) return fail(B2S_ERR_INVALID_ARG, "act_quant: x, q and s must be non-NULL");
+    if (M < 0 || K <= 0 || ldx < K || ldq < K) return fail(B2S_ERR_INVALID_ARG, "act_quant: bad shape/strides");
+    if (K > (int64_t)0x7fffffff || M > (int64_t)0x7fffffff) return fail(B2S_ERR_UNSUPPORTED, "act_quant: size exceeds int32");
+    return launched(b2s::launch_act_quant(x, ldx, g, norm, eps, M, K, q, ldq, s, sums, static_cast<cudaStream_t>(stream)),
+                    "act_quant launch");
+}
+
+int b2s_act_quant(const float* x, int64_t M, int64_t K, int64_t ldx, int8_t* q, int64_t ldq, float* s, int32_t* sums,
+                  void* stream) {
+    return act_quant_common(x, nullptr, false, 0.0f, M, K, ldx, q, ldq, s, sums, stream);
+}
+
+int b2s_rms_norm_act_quant(const float* x, const float* g, int64_t M, int64_t K, int64_t ldx, float eps, int8_t* q,
+                           int64_t ldq, float* s, int32_t* sums, void* stream) {
+    return act_quant_common(x, g, true, eps, M, K, ldx, q, ldq, s, sums, stream);
+}
+
+size_t b2s_mul_mat_workspace_size(const b2s_tensor* W, const b2s_tensor* X) {
+    if (!W || !X) return 0;
+    const int64_t M = X->ne[1] * (X->ne[2] > 0 ? X->ne[2] : 1) * (X->ne[3] > 0 ? X->ne[3] : 1);
+    return act_ws(M, W->ne[0]).total;
+}
+
+int b2s_mul_mat_q8_ex(const b2s_tensor* W, const int8_t* q, int64_t ldq, const float* s, const int32_t* sums,
+                      int64_t M, float* Y, int64_t ldy, int path, void* stream) {
+    int rc = check_device();
+    if (rc) return rc;
+    b2s::I2sWeight w;
+    if ((rc = weight_view(W, &w, "W"))) return rc;
+    if (!q || !s || !sums || !Y) return fail(B2S_ERR_INVALID_ARG, "mul_mat_q8: q, s, sums and Y must be non-NULL");
+    if (M < 0 || ldq < w.K || ldy < w.N) return fail(B2S_ERR_INVALID_ARG, "mul_mat_q8: bad M/ldq/ldy");
+    if (path < 0 || path > 2) return fail(B2S_ERR_INVALID_ARG, "mul_mat_q8: path must be 0, 1 or 2");
+    return mul_mat_q8_impl(w, q, ldq, s, sums, M, Y, ldy, path, static_cast<cudaStream_t>(stream));
+}
+
+int b2s_mul_mat_q8(const b2s_tensor* W, const int8_t* q, int64_t ldq, const float* s, const int32_t* sums, int64_t M,
+                   float* Y, int64_t ldy, void* stream) {
+    return b2s_mul_mat_q8_ex(W, q, ldq, s, sums, M, Y, ldy, 0, stream);
+}
+
+int b2s_mul_mat(const b2s_tensor* W, const b2s_tensor* X, b2s_tensor* Y, void* workspace, size_t workspace_bytes,
+                void* stream) {
+    int rc = check_device();
+    if (rc) return rc;
+    b2s::I2sWeight w;
+    if ((rc = weight_view(W, &w, "W"))) return rc;
+    int64_t M, Kx, ldx, My, Ny, ldy;
+    if ((rc = f32_rows(X, "X", &M, &Kx, &ldx))) return rc;
+    if ((rc = f32_rows(Y, "Y", &My, &Ny, &ldy))) return rc;
+    if (Kx != w.K) return fail(B2S_ERR_INVALID_ARG, "X ne0 (%lld) != W ne0 (%lld)", (long long)Kx, (long long)w.K);
+    if (Ny != w.N || My != M)
+        return fail(B2S_ERR_INVALID_ARG, "Y must be ne=[%lld,%lld], got [%lld,%lld]", (long long)w.N, (long long)M,
+                    (long long)Ny, (long long)My);
+    const WsLayout l = act_ws(M, w.K);
+    if (!workspace || workspace_bytes < l.total)
+        return fail(B2S_ERR_WORKSPACE, "mul_mat needs %zu workspace bytes, got %zu", l.total, workspace_bytes);
+    if ((reinterpret_cast<uintptr_t>(workspace) & 255) != 0) return fail(B2S_ERR_WORKSPACE, "workspace must be 256-byte aligned");
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    int8_t* q = reinterpret_cast<int8_t*>(ws + l.q_off);
+    float* s = reinterpret_cast<float*>(ws + l.s_off);
+    int32_t* sums = reinterpret_cast<int32_t*>(ws + l.sum_off);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if ((rc = launched(b2s::launch_act_quant(static_cast<const float*>(X->data), ldx, nullptr, false, 0.0f, M, w.K, q,
+                                             l.ldq, s, sums, st),
+                       "act_quant launch")))
+        return rc;
+    return mul_mat_q8_impl(w, q, l.ldq, s, sums, M, static_cast<float*>(Y->data), ldy, 0, st);
+}
+
+int b2s_ffn_gate_up_sqrelu_q8(const b2s_tensor* W_gate, const b2s_tensor* W_up, const int8_t* q, int64_t ldq,
+                              const float* s, const int32_t* sums, int64_t M, float* P, int64_t ldp, void* stream) {
+    int rc = check_device();
+    if (rc) return rc;
+    b2s::I2sWeight wg, wu;
+    if ((rc = weight_view(W_gate, &wg, "W_gate"))) return rc;
+    if ((rc = weight_view(W_up, &wu, "W_up"))) return rc;
+    if (wg.N != wu.N || wg.K != wu.K) return fail(B2S_ERR_INVALID_ARG, "W_gate and W_up shapes differ");
+    if (!q || !s || !sums || !P) return fail(B2S_ERR_INVALID_ARG, "gate_up: q, s, sums and P must be non-NULL");
+    if (M < 0 || ldq < wg.K || ldp < wg.N) return fail(B2S_ERR_INVALID_ARG, "gate_up: bad M/ldq/ldp");
+    if (M == 0) return B2S_OK;
+    return run_tc(wg, &wu, q, ldq, s, M, P, ldp, 1, static_cast<cudaStream_t>(stream));
+}
+
+static void ffn_layout(int64_t M, int64_t H, int64_t F, WsLayout* l1, size_t* p_off, WsLayout* l2) {
+    *l1 = act_ws(M, H);
+    *p_off = a256(l1->total);
+    *l2 = act_ws(M, F, *p_off + sizeof(float) * (size_t)(M * F));
+}
+
+size_t b2s_ffn_block_workspace_size(int64_t M, int64_t H, int64_t F) {
+    if (M <= 0 || H <= 0 || F <= 0) return 0;
+    WsLayout l1, l2;
+    size_t p_off;
+    ffn_layout(M, H, F, &l1, &p_off, &l2);
+    return l2.total;
+}
+
+int b2s_ffn_block(const float* X, int64_t M, const float* g1, const float* g2, float eps, const b2s_tensor* W_gate,
+                  const b2s_tensor* W_up, const b2s_tensor* W_down, float* Y, void* workspace, size_t workspace_bytes,
+                  void* stream) {
+    int rc = check_device();
+    if (rc) return rc;
+    b2s::I2sWeight wg, wu, wd;
+    if ((rc = weight_view(W_gate, &wg, "W_gate"))) return rc;
+    if ((rc = weight_view(W_up, &wu, "W_up"))) return rc;
+    if ((rc = weight_view(W_down, &wd, "W_down"))) return rc;
+    const int64_t H = wg.K, F = wg.N;
+    if (wu.K != H || wu.N != F || wd.K != F || wd.N != H)
+        return fail(B2S_ERR_INVALID_ARG, "FFN weights must be gate/up [H->F] and down [F->H]");
+    if (!X || !Y) return fail(B2S_ERR_INVALID_ARG, "ffn_block: X and Y must be non-NULL");
+    if (M <= 0) return M == 0 ? B2S_OK : fail(B2S_ERR_INVALID_ARG, "ffn_block: M < 0");
+    WsLayout l1, l2;
+    size_t p_off;
+    ffn_layout(M, H, F, &l1, &p_off, &l2);
+    if (!workspace || workspace_bytes < l2.total)
+        return fail(B2S_ERR_WORKSPACE, "ffn_block needs %zu workspace bytes, got %zu", l2.total, workspace_bytes);
+    if ((reinterpret_cast<uintptr_t>(workspace) & 255) != 0) return fail(B2S_ERR_WORKSPACE, "workspace must be 256-byte aligned");
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    int8_t* q1 = reinterpret_cast<int8_t*>(ws + l1.q_off);
+    float* s1 = reinterpret_cast<float*>(ws + l1.s_off);
+    int32_t* u1 = reinterpret_cast<int32_t*>(ws + l1.sum_off);
+    float* P = reinterpret_cast<float*>(ws + p_off);
+    int8_t* q2 = reinterpret_cast<int8_t*>(ws + l2.q_off);
+    float* s2 = reinterpret_cast<float*>(ws + l2.s_off);
+    int32_t* u2 = reinterpret_cast<int32_t*>(ws + l2.sum_off);
+    if ((rc = launched(b2s::launch_act_quant(X, H, g1, true, eps, M, H, q1, l1.ldq, s1, u1, st), "rms_norm_act_quant 1")))
+        return rc;
+    if ((rc = run_tc(wg, &wu, q1, l1.ldq, s1, M, P, F, 1, st))) return rc;
+    if ((rc = launched(b2s::launch_act_quant(P, F, g2, true, eps, M, F, q2, l2.ldq, s2, u2, st), "rms_norm_act_quant 2")))
+        return rc;
+    return mul_mat_q8_impl(wd, q2, l2.ldq, s2, u2, M, Y, H, 0, st);
+}
+
+int b2s_soft_max_ext(const float* x, const float* mask, int64_t mask_rows, int64_t M, int64_t N, float scale, float* y,
+                     void* stream) {
+    int rc = check_device();
+    if (rc) return rc;
+    if (!x || !y) return fail(B2S_ERR_INVALID_ARG, "soft_max_ext: x and y must be non-NULL");
+    if (M < 0 || N <= 0 || N > (int64_t)0x7fffffff) return fail(B2S_ERR_INVALID_ARG, "soft_max_ext: bad shape");
+    if (mask && mask_rows <= 0) return fail(B2S_ERR_INVALID_ARG, "soft_max_ext: mask_rows must be positive");
+    return launched(b2s::launch_softmax(x, mask, mask ? mask_rows : 1, M, N, scale, y, static_cast<cudaStream_t>(stream)),
+                    "softmax launch");
+}
+
+}  // extern "C"

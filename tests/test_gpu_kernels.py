@@ -1,0 +1,264 @@
+"""Parity of the CUDA path (through the C ABI) against the oracle, on a B200.
+
+Bars: int8 activations, scales, sums and int32 accumulators bit-exact; fp32 outputs compared with
+max-abs-rel <= 1e-5 (max |y - y_ref| / max |y_ref|) and, because every fp32 step is restated with the
+same IEEE operations in the same order, also checked for exact equality where stated. Softmax uses libm
+expf on the host and CUDA expf on the device: tolerance 2e-6 absolute on probabilities.
+"""
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+pytestmark = pytest.mark.gpu
+
+from b2s import workloads as wl  # noqa: E402
+
+TOL = 1e-5
+
+
+def max_abs_rel(y, ref):
+    ref = np.asarray(ref, np.float64)
+    return float(np.max(np.abs(np.asarray(y, np.float64) - ref)) / max(np.max(np.abs(ref)), 1e-30))
+
+
+def dev(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def weight_dev(b2s, w):
+    buf = dev(w.packed)
+    return buf, b2s.i2s_tensor(buf, w.N, w.K)
+
+
+def q8_buffers(M, K):
+    ldq = (K + 15) // 16 * 16
+    q = torch.zeros((M, ldq), dtype=torch.int8, device="cuda")[:, :K]
+    s = torch.zeros(M, dtype=torch.float32, device="cuda")
+    u = torch.zeros(M, dtype=torch.int32, device="cuda")
+    return q, s, u
+
+
+def sync_ok(b2s):
+    torch.cuda.synchronize()
+    assert b2s.device_error() == 0
+
+
+# ------------------------------------------------------------------------------------------ act-quant
+@pytest.mark.parametrize("M,K", [(1, 2560), (37, 2560), (5, 6912), (3, 99), (4, 4304)])
+def test_act_quant_bit_exact(b2s, orc, M, K):
+    g = wl.rng(100 + M + K)
+    x = wl.activations(g, M, K)
+    x[0, :] = 0.0                      # all-zero row: the 1e-5 amax floor
+    if M > 2:
+        x[1, :] *= 1e-7                # every |x| below the floor
+        x[2, 3] = 127.0 * 3            # ties: amax 381 -> s = 1/3 ...
+    q, s, u = q8_buffers(M, K)
+    xd = dev(x)
+    b2s.act_quant(xd, q, s, u)
+    sync_ok(b2s)
+    q_ref, s_ref, u_ref = orc.act_quant(x)
+    assert np.array_equal(q.cpu().numpy(), q_ref)
+    assert np.array_equal(s.cpu().numpy(), s_ref)
+    assert np.array_equal(u.cpu().numpy(), u_ref)
+
+
+def test_act_quant_kat(b2s):
+    import os
+    kat = np.load(os.path.join(os.path.dirname(__file__), "golden", "kat.npz"))
+    x = kat["x_actq"]
+    q, s, u = q8_buffers(*x.shape)
+    b2s.act_quant(dev(x), q, s, u)
+    sync_ok(b2s)
+    assert np.array_equal(q.cpu().numpy(), kat["q_actq"])
+    assert np.array_equal(s.cpu().numpy(), kat["s_actq"])
+    assert np.array_equal(u.cpu().numpy(), kat["sum_actq"])
+
+
+@pytest.mark.parametrize("M,K", [(3, 2560), (300, 2560), (17, 6912), (2, 1152)])
+def test_rms_norm_act_quant_bit_exact(b2s, orc, M, K):
+    g = wl.rng(200 + M + K)
+    x = wl.activations(g, M, K) * 3.0
+    w = wl.norm_weight(g, K)
+    q, s, u = q8_buffers(M, K)
+    b2s.rms_norm_act_quant(dev(x), dev(w), 1e-5, q, s, u)
+    sync_ok(b2s)
+    xn = orc.rms_norm(x, w, 1e-5)
+    q_ref, s_ref, u_ref = orc.act_quant(xn)
+    assert np.array_equal(s.cpu().numpy(), s_ref)
+    assert np.array_equal(q.cpu().numpy(), q_ref)
+    assert np.array_equal(u.cpu().numpy(), u_ref)
+
+
+# ------------------------------------------------------------------------------------------ GEMM / GEMV
+def run_q8(b2s, orc, M, K, N, path, seed):
+    g = wl.rng(seed)
+    w = wl.weight(g, N, K)
+    x = wl.activations(g, M, K)
+    buf, W = weight_dev(b2s, w)
+    q, s, u = q8_buffers(M, K)
+    b2s.act_quant(dev(x), q, s, u)
+    y = torch.full((M, N), float("nan"), dtype=torch.float32, device="cuda")
+    b2s.mul_mat_q8(W, q, s, u, y, path=path)
+    sync_ok(b2s)
+    q_ref, s_ref, _ = orc.act_quant(x)
+    if M * N * K <= 64 * 1024 * 1024:
+        acc = orc.gemm_i32(w.t, q_ref)
+        y_ref = orc.rescale(acc, s_ref, float(w.scale))
+    else:
+        y_ref = orc.fast_mul_mat_i2s(w.packed, x, N, 8)
+    return y.cpu().numpy(), y_ref
+
+
+@pytest.mark.parametrize("M", [1, 2, 3, 5, 8, 13])
+@pytest.mark.parametrize("K,N", [(2560, 2560), (1152, 4304), (256, 40), (6912, 2560)])
+def test_gemv_path(b2s, orc, M, K, N):
+    y, y_ref = run_q8(b2s, orc, M, K, N, path=1, seed=M * 7 + K + N)
+    assert max_abs_rel(y, y_ref) <= TOL
+    assert np.array_equal(y, y_ref)
+
+
+@pytest.mark.parametrize("M", [1, 16, 37, 256, 300])
+@pytest.mark.parametrize("K,N", [(128, 128), (384, 200), (2560, 2560), (1152, 4304), (6912, 2560)])
+def test_tensor_core_path(b2s, orc, M, K, N):
+    y, y_ref = run_q8(b2s, orc, M, K, N, path=2, seed=M * 11 + K + N)
+    assert max_abs_rel(y, y_ref) <= TOL
+    assert np.array_equal(y, y_ref)
+
+
+@pytest.mark.parametrize("M,K,N", [(4096, 2560, 2560), (600, 2560, 6912), (513, 6912, 2560)])
+def test_tensor_core_large(b2s, orc, M, K, N):
+    y, y_ref = run_q8(b2s, orc, M, K, N, path=2, seed=M + K + N)
+    assert max_abs_rel(y, y_ref) <= TOL
+    assert np.array_equal(y, y_ref)
+
+
+@pytest.mark.parametrize("M", [1, 16, 256])
+def test_mul_mat_op_config0(b2s, orc, M):
+    """The MUL_MAT node through ggml-style descriptors (f32 X in, f32 Y out), 2560x2560 weight."""
+    K = N = 2560
+    g = wl.rng(300 + M)
+    w = wl.weight(g, N, K)
+    x = wl.activations(g, M, K)
+    buf, W = weight_dev(b2s, w)
+    xd = dev(x)
+    y = torch.empty((M, N), dtype=torch.float32, device="cuda")
+    X = b2s.f32_tensor(xd)
+    ws = torch.empty(b2s.mul_mat_workspace_size(W, X), dtype=torch.uint8, device="cuda")
+    b2s.mul_mat(W, xd, y, ws)
+    sync_ok(b2s)
+    y_ref = orc.fast_mul_mat_i2s(w.packed, x, N, 8)
+    assert max_abs_rel(y.cpu().numpy(), y_ref) <= TOL
+    assert np.array_equal(y.cpu().numpy(), y_ref)
+
+
+def test_repack_rows_and_mul_mat(b2s, orc):
+    """K % 128 != 0 (ViT FFN down 4304 -> 1152 shape, fewer rows): flattened i2_s -> row-padded."""
+    K, N, M = 4304, 64, 20
+    g = wl.rng(400)
+    w = wl.weight(g, N, K)
+    src = dev(w.packed)
+    dst = torch.zeros(b2s.i2s_r_nbytes(N, K), dtype=torch.uint8, device="cuda")
+    b2s.repack_rows(src, dst, N, K)
+    sync_ok(b2s)
+    assert np.array_equal(dst.cpu().numpy(), orc.i2s_to_rowpadded(w.packed, N, K))
+    W = b2s.i2s_tensor(dst, N, K, rowpadded=True)
+    x = wl.activations(g, M, K)
+    for path in (1, 2):
+        q, s, u = q8_buffers(M, K)
+        b2s.act_quant(dev(x), q, s, u)
+        y = torch.empty((M, N), dtype=torch.float32, device="cuda")
+        b2s.mul_mat_q8(W, q, s, u, y, path=path)
+        sync_ok(b2s)
+        assert np.array_equal(y.cpu().numpy(), orc.mul_mat_i2s(w.packed, x, N))
+
+
+# ------------------------------------------------------------------------------------------ FFN
+def test_gate_up_sqrelu(b2s, orc):
+    M, H, F = 45, 2560, 640
+    g = wl.rng(500)
+    wg, wu = wl.weight(g, F, H), wl.weight(g, F, H)
+    x = wl.activations(g, M, H)
+    bg, Wg = weight_dev(b2s, wg)
+    bu, Wu = weight_dev(b2s, wu)
+    q, s, u = q8_buffers(M, H)
+    b2s.act_quant(dev(x), q, s, u)
+    p = torch.empty((M, F), dtype=torch.float32, device="cuda")
+    b2s.ffn_gate_up_sqrelu_q8(Wg, Wu, q, s, u, p)
+    sync_ok(b2s)
+    p_ref = orc.sqrelu_mul(orc.mul_mat_i2s(wg.packed, x, F), orc.mul_mat_i2s(wu.packed, x, F))
+    assert np.array_equal(p.cpu().numpy(), p_ref)
+
+
+@pytest.mark.parametrize("M", [300, 7])
+def test_ffn_block_config1(b2s, orc, M):
+    """BitNet-b1.58-2B FFN block (H=2560, F=6912), prefill M=300 and a decode-size M."""
+    f = wl.ffn_block(seed=600 + M, M=M)
+    bufs = [weight_dev(b2s, w) for w in (f.w_gate, f.w_up, f.w_down)]
+    y = torch.empty((M, f.H), dtype=torch.float32, device="cuda")
+    ws = torch.empty(b2s.ffn_block_workspace_size(M, f.H, f.F), dtype=torch.uint8, device="cuda")
+    b2s.ffn_block(dev(f.x), dev(f.g1), dev(f.g2), f.eps, bufs[0][1], bufs[1][1], bufs[2][1], y, ws)
+    sync_ok(b2s)
+    y_ref = orc.fast_ffn_block(f.x, f.g1, f.g2, f.eps, f.w_gate.packed, f.w_up.packed, f.w_down.packed, f.H, f.F, 8)
+    assert max_abs_rel(y.cpu().numpy(), y_ref) <= TOL
+    assert np.array_equal(y.cpu().numpy(), y_ref)
+
+
+def test_ffn_tiny_golden(b2s):
+    import os
+    d = np.load(os.path.join(os.path.dirname(__file__), "golden", "ffn_tiny.npz"))
+    M, H = d["x"].shape
+    F = d["g2"].shape[0]
+    Ws = []
+    for k, (n, kk) in (("w_gate", (F, H)), ("w_up", (F, H)), ("w_down", (H, F))):
+        buf = dev(d[k])
+        Ws.append((buf, b2s.i2s_tensor(buf, n, kk)))
+    y = torch.empty((M, H), dtype=torch.float32, device="cuda")
+    ws = torch.empty(b2s.ffn_block_workspace_size(M, H, F), dtype=torch.uint8, device="cuda")
+    b2s.ffn_block(dev(d["x"]), dev(d["g1"]), dev(d["g2"]), float(d["eps"]), Ws[0][1], Ws[1][1], Ws[2][1], y, ws)
+    sync_ok(b2s)
+    assert np.array_equal(y.cpu().numpy(), d["y"])
+
+
+# ------------------------------------------------------------------------------------------ softmax
+@pytest.mark.parametrize("M,N,masked", [(16 * 256, 256, False), (20 * 288, 288, True), (7, 1000, True)])
+def test_soft_max_ext(b2s, orc, M, N, masked):
+    g = wl.rng(700 + N)
+    x = (g.standard_normal((M, N)) * 4).astype(np.float32)
+    mask = None
+    if masked:  # causal mask rows, as in a decoder prefill
+        r = min(M, N)
+        mask = np.triu(np.full((r, N), -np.inf, np.float32), k=1)
+    y = torch.empty((M, N), dtype=torch.float32, device="cuda")
+    b2s.soft_max_ext(dev(x), None if mask is None else dev(mask), 0.125, y)
+    sync_ok(b2s)
+    y_ref = orc.soft_max_ext(x, mask, 0.125)
+    yy = y.cpu().numpy()
+    assert np.max(np.abs(yy - y_ref)) <= 2e-6
+    if masked:
+        assert np.all(yy[np.isneginf(np.broadcast_to(mask[np.arange(M) % mask.shape[0]], (M, N)))] == 0.0)
+
+
+# ------------------------------------------------------------------------------------------ errors
+def test_errors_before_launch(b2s):
+    K, N = 4304, 64
+    buf = torch.zeros(b2s.i2s_nbytes(N, K), dtype=torch.uint8, device="cuda")
+    W = b2s.i2s_tensor(buf, N, K)  # flattened i2_s with K % 128 != 0 needs a repack
+    x = torch.zeros((4, K), dtype=torch.float32, device="cuda")
+    y = torch.zeros((4, N), dtype=torch.float32, device="cuda")
+    ws = torch.zeros(1 << 20, dtype=torch.uint8, device="cuda")
+    with pytest.raises(b2s.B2SError) as e:
+        b2s.mul_mat(W, x, y, ws)
+    assert e.value.status == b2s.B2S_ERR_UNSUPPORTED
+    K = N = 256
+    buf = torch.zeros(b2s.i2s_nbytes(N, K), dtype=torch.uint8, device="cuda")
+    W = b2s.i2s_tensor(buf, N, K)
+    x = torch.zeros((4, K), dtype=torch.float32, device="cuda")
+    y = torch.zeros((4, N), dtype=torch.float32, device="cuda")
+    with pytest.raises(b2s.B2SError) as e:
+        b2s.mul_mat(W, x, y, ws[:16])
+    assert e.value.status == b2s.B2S_ERR_WORKSPACE
+    with pytest.raises(b2s.B2SError) as e:
+        b2s.mul_mat(W, torch.zeros((4, K + 16), dtype=torch.float32, device="cuda"), y, ws)
+    assert e.value.status == b2s.B2S_ERR_INVALID_ARG
+    sync_ok(b2s)
