@@ -156,7 +156,10 @@ WsLayout act_ws(int64_t M, int64_t K, size_t base = 0) {
 }
 
 int launched(cudaError_t e, const char* what) {
-    if (e != cudaSuccess) return cuda_fail(e, what);
+    if (e != cudaSuccess) {
+        (void)cudaGetLastError();  // a failed launch must not leak into the next call's error check
+        return cuda_fail(e, what);
+    }
     return B2S_OK;
 }
 

@@ -148,9 +148,12 @@ static cudaError_t launch_mt(const I2sWeight& w, const int8_t* q, int64_t ldq, c
                              float* y, int64_t ldy, cudaStream_t st) {
     const size_t smem = (size_t)MT * (size_t)w.Kp;
     auto kfn = gemv_i2s_kernel<MT>;
-    if (smem > 48 * 1024) {
+    // Dynamic + static shared memory above 48 KB needs the opt-in attribute (raised once per size).
+    static int opted_in = 0;
+    if (smem + sizeof(int) * kGemvWarps * kGemvRows * MT > 48 * 1024 && (int)smem > opted_in) {
         cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
+        opted_in = (int)smem;
     }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)ceil_div(w.N, kGemvRows));
