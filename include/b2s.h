@@ -119,6 +119,18 @@ size_t b2s_mul_mat_workspace_size(const b2s_tensor *W, const b2s_tensor *X);
 int b2s_mul_mat(const b2s_tensor *W, const b2s_tensor *X, b2s_tensor *Y, void *workspace, size_t workspace_bytes,
                 void *stream);
 
+/* The MUL_MAT node of b2s_mul_mat for callers that cannot allocate: no workspace argument, and the call
+ * allocates nothing. This entry point has no counterpart in the reference. It serves code that owns no
+ * device workspace and must not call cudaMalloc while it runs: an op inside a ggml backend's compute step
+ * (the scheduler has already allocated every buffer and hands the op no allocator), or a robot control
+ * loop past start-up (cudaMalloc can synchronize the device and adds latency jitter). The quantized
+ * activations go to a library-owned 4 MiB static device array instead (held by every GPU that loads the
+ * library until the process exits). Limit: the call's scratch need, b2s_mul_mat_workspace_size(W, X)
+ * (about M*roundup(K,16) + 8*M bytes), must be at most 4 MiB, else B2S_ERR_WORKSPACE and nothing is
+ * launched. The first call on a device looks up the array's address; make it before any stream capture.
+ * All calls on a device share the array: calls that overlap on the GPU race, so serialize them. */
+int b2s_mul_mat_static(const b2s_tensor *W, const b2s_tensor *X, b2s_tensor *Y, void *stream);
+
 /* MUL_MAT on already-quantized activations (producer-fused path): q [M x ldq] int8 (ldq % 16 == 0,
  * 16-byte aligned), s [M], sums [M] from b2s_act_quant / b2s_rms_norm_act_quant. Y [M x ldy] f32. */
 int b2s_mul_mat_q8(const b2s_tensor *W, const int8_t *q, int64_t ldq, const float *s, const int32_t *sums,

@@ -33,7 +33,7 @@ EXPORTED = [
     "b2s_i2s_nbytes", "b2s_i2s_r_nbytes", "b2s_i2s_quantize", "b2s_i2s_dequantize",
     "b2s_i2s_repack_rows", "b2s_act_quant", "b2s_rms_norm_act_quant", "b2s_mul_mat_workspace_size",
     "b2s_mul_mat", "b2s_mul_mat_q8", "b2s_mul_mat_q8_ex", "b2s_ffn_gate_up_sqrelu_q8",
-    "b2s_ffn_block_workspace_size", "b2s_ffn_block", "b2s_soft_max_ext",
+    "b2s_ffn_block_workspace_size", "b2s_ffn_block", "b2s_soft_max_ext", "b2s_mul_mat_static",
 ]
 
 
@@ -82,6 +82,7 @@ def lib():
             "b2s_ffn_block_workspace_size": (C.c_size_t, [_i64, _i64, _i64]),
             "b2s_ffn_block": (C.c_int, [_vp, _i64, _vp, _vp, C.c_float, _TP, _TP, _TP, _vp, _vp, C.c_size_t, _vp]),
             "b2s_soft_max_ext": (C.c_int, [_vp, _vp, _i64, _i64, _i64, C.c_float, _vp, _vp]),
+            "b2s_mul_mat_static": (C.c_int, [_TP, _TP, _TP, _vp]),
         }
         for name, (res, args) in sig.items():
             f = getattr(L, name)
@@ -199,6 +200,13 @@ def mul_mat(W: Tensor, x, y, workspace, stream=None) -> None:
     Y = f32_tensor(y)
     check(lib().b2s_mul_mat(C.byref(W), C.byref(X), C.byref(Y), _ptr(workspace),
                             workspace.numel() * workspace.element_size(), _stream(stream)))
+
+
+def mul_mat_static(W: Tensor, x, y, stream=None) -> None:
+    """MUL_MAT without a workspace: for callers that may not allocate (the library's 4 MiB static scratch)."""
+    X = f32_tensor(x)
+    Y = f32_tensor(y)
+    check(lib().b2s_mul_mat_static(C.byref(W), C.byref(X), C.byref(Y), _stream(stream)))
 
 
 def mul_mat_q8(W: Tensor, q, s, sums, y, path: int = 0, stream=None) -> None:

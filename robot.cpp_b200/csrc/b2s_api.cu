@@ -220,6 +220,50 @@ int mul_mat_q8_impl(const b2s::I2sWeight& w, const int8_t* q, int64_t ldq, const
 
 }  // namespace
 
+namespace b2s {
+
+int set_last_error(int code, const char* msg) { return fail(code, "%s", msg); }
+
+size_t mul_mat_scratch_bytes(const void* Wv, const void* Xv) {
+    const b2s_tensor* W = static_cast<const b2s_tensor*>(Wv);
+    const b2s_tensor* X = static_cast<const b2s_tensor*>(Xv);
+    b2s::I2sWeight w{};
+    int64_t M = 0, Kx = 0, ldx = 0;
+    if (weight_view(W, &w, "W") != B2S_OK) return 0;
+    if (f32_rows(X, "X", &M, &Kx, &ldx) != B2S_OK) return 0;
+    return act_ws(M, w.K).total;
+}
+
+int mul_mat_into_scratch(const void* Wv, const void* Xv, void* Yv, void* scratch, size_t capacity, cudaStream_t st) {
+    const b2s_tensor* W = static_cast<const b2s_tensor*>(Wv);
+    const b2s_tensor* X = static_cast<const b2s_tensor*>(Xv);
+    const b2s_tensor* Y = static_cast<const b2s_tensor*>(Yv);
+    b2s::I2sWeight w{};
+    int rc;
+    if ((rc = weight_view(W, &w, "W"))) return rc;
+    int64_t M = 0, Kx = 0, ldx = 0, My = 0, Ny = 0, ldy = 0;
+    if ((rc = f32_rows(X, "X", &M, &Kx, &ldx))) return rc;
+    if ((rc = f32_rows(Y, "Y", &My, &Ny, &ldy))) return rc;
+    if (Kx != w.K) return fail(B2S_ERR_INVALID_ARG, "X ne0 (%lld) != W ne0 (%lld)", (long long)Kx, (long long)w.K);
+    if (Ny != w.N || My != M)
+        return fail(B2S_ERR_INVALID_ARG, "Y must be ne=[%lld,%lld], got [%lld,%lld]", (long long)w.N, (long long)M,
+                    (long long)Ny, (long long)My);
+    const WsLayout l = act_ws(M, w.K);
+    if (!scratch || capacity < l.total)
+        return fail(B2S_ERR_WORKSPACE, "mul_mat needs %zu scratch bytes, %zu available", l.total, capacity);
+    uint8_t* ws = static_cast<uint8_t*>(scratch);
+    int8_t* q = reinterpret_cast<int8_t*>(ws + l.q_off);
+    float* s = reinterpret_cast<float*>(ws + l.s_off);
+    int32_t* sums = reinterpret_cast<int32_t*>(ws + l.sum_off);
+    if ((rc = launched(b2s::launch_act_quant(static_cast<const float*>(X->data), ldx, nullptr, false, 0.0f, M, w.K, q,
+                                             l.ldq, s, sums, st),
+                       "act_quant launch")))
+        return rc;
+    return mul_mat_q8_impl(w, q, l.ldq, s, sums, M, static_cast<float*>(Y->data), ldy, 0, st);
+}
+
+}  // namespace b2s
+
 // ==================================================================================================
 extern "C" {
 

@@ -50,4 +50,15 @@ cudaError_t launch_repack_rows(const uint8_t* src, uint8_t* dst, int64_t N, int6
 cudaError_t launch_softmax(const float* x, const float* mask, int64_t mask_rows, int64_t M, int64_t N, float scale,
                            float* y, cudaStream_t st);
 
+// Records `msg` as the calling thread's b2s_last_error() and returns `code`.
+int set_last_error(int code, const char* msg);
+
+// Scratch bytes the MUL_MAT node needs for its int8 activations, scales and sums (same layout as the
+// caller workspace of b2s_mul_mat); 0 with the error set if W or X is malformed.
+size_t mul_mat_scratch_bytes(const void* W, const void* X);
+
+// The MUL_MAT node of b2s_mul_mat run into a scratch region the caller already owns
+// (`scratch` device pointer, `capacity` bytes, 256-byte aligned). Validates exactly like b2s_mul_mat.
+int mul_mat_into_scratch(const void* W, const void* X, void* Y, void* scratch, size_t capacity, cudaStream_t st);
+
 }  // namespace b2s
