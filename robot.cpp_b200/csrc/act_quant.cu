@@ -75,6 +75,8 @@ act_quant_kernel(const float* __restrict__ x, int64_t ldx, const float* __restri
     const int64_t m = blockIdx.x;
     const float* xr = x + m * ldx;
     int8_t* qr = q + m * ldq;
+    griddep_wait();    // x is written by the preceding kernel
+    griddep_launch();  // the consuming GEMM may start now: it waits for this grid before reading q
 
     float nscale = 1.0f;
     if (NORM) {
@@ -151,15 +153,22 @@ cudaError_t launch_act_quant(const float* x, int64_t ldx, const float* g, bool n
     if (M <= 0) return cudaSuccess;
     const bool vec = (K % 4 == 0) && (ldx % 4 == 0) && (ldq % 4 == 0) &&
                      ((reinterpret_cast<uintptr_t>(x) & 15) == 0) && ((reinterpret_cast<uintptr_t>(q) & 3) == 0);
-    dim3 grid((unsigned)M), block(kActThreads);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)M);
+    cfg.blockDim = dim3(kActThreads);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const int k = (int)K;
     if (norm) {
-        if (vec) act_quant_kernel<true, true><<<grid, block, 0, st>>>(x, ldx, g, eps, (int)K, q, ldq, s, sums);
-        else act_quant_kernel<true, false><<<grid, block, 0, st>>>(x, ldx, g, eps, (int)K, q, ldq, s, sums);
-    } else {
-        if (vec) act_quant_kernel<false, true><<<grid, block, 0, st>>>(x, ldx, g, eps, (int)K, q, ldq, s, sums);
-        else act_quant_kernel<false, false><<<grid, block, 0, st>>>(x, ldx, g, eps, (int)K, q, ldq, s, sums);
+        if (vec) return cudaLaunchKernelEx(&cfg, act_quant_kernel<true, true>, x, ldx, g, eps, k, q, ldq, s, sums);
+        return cudaLaunchKernelEx(&cfg, act_quant_kernel<true, false>, x, ldx, g, eps, k, q, ldq, s, sums);
     }
-    return cudaGetLastError();
+    if (vec) return cudaLaunchKernelEx(&cfg, act_quant_kernel<false, true>, x, ldx, g, eps, k, q, ldq, s, sums);
+    return cudaLaunchKernelEx(&cfg, act_quant_kernel<false, false>, x, ldx, g, eps, k, q, ldq, s, sums);
 }
 
 }  // namespace b2s

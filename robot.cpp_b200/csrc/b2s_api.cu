@@ -163,32 +163,67 @@ int launched(cudaError_t e, const char* what) {
     return B2S_OK;
 }
 
-// Tensor-core token tile: split M into the fewest tiles of at most max_bn, rounded up to 16.
-int pick_bn(int64_t M, int max_bn) {
-    const int64_t tiles = b2s::ceil_div(M, max_bn);
-    int64_t bn = b2s::round_up(b2s::ceil_div(M, tiles), 16);
-    if (bn > max_bn) bn = max_bn;
-    if (bn < 16) bn = 16;
-    return (int)bn;
+// Tensor-core tiling. A CTA covers up to 320 tokens as one (<= 256) or two MMA sub-tiles; M is split into
+// the fewest such spans (fewer CTA waves beat full-width 256-token MMAs on a non-persistent grid). When
+// the output tiles cannot fill the GPU's SMs, the K loop is split across the CTAs of a cluster (up to 8,
+// each keeping at least two 128-wide K steps).
+struct TcTiling {
+    int T, bn_sub, nsub, m_tiles, n_tiles, splits;
+};
+TcTiling pick_tiling(int64_t M, int64_t n_out, int rows_per_cta, int64_t Kp, int num_sms) {
+    TcTiling t;
+    t.m_tiles = (int)b2s::ceil_div(M, 320);
+    const int64_t t0 = b2s::ceil_div(M, t.m_tiles);
+    if (t0 <= 256) {
+        t.nsub = 1;
+        t.bn_sub = (int)b2s::round_up(t0 < 16 ? 16 : t0, 16);
+    } else {
+        t.nsub = 2;
+        t.bn_sub = (int)b2s::round_up(b2s::ceil_div(t0, 2), 16);
+    }
+    t.T = t.nsub * t.bn_sub;
+    t.n_tiles = (int)b2s::ceil_div(n_out, rows_per_cta);
+    const int64_t tiles = (int64_t)t.n_tiles * t.m_tiles;
+    int s = 1;
+    if (tiles < num_sms) s = (int)(num_sms / tiles);
+    const int64_t nkt = Kp / b2s::kQK;
+    if (s > nkt / 2) s = (int)(nkt / 2);
+    if (s > 8) s = 8;
+    if (s < 1) s = 1;
+    t.splits = s;
+    return t;
+}
+
+int num_sms_current() {
+    static int cache[128];
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 128) return 148;
+    if (!cache[dev]) {
+        int n = 0;
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+        cache[dev] = n;
+    }
+    return cache[dev];
 }
 
 int run_tc(const b2s::I2sWeight& w0, const b2s::I2sWeight* w1, const int8_t* q, int64_t ldq, const float* s,
-           int64_t M, float* Y, int64_t ldy, int mode, cudaStream_t st) {
+           const int32_t* sums, int64_t M, float* Y, int64_t ldy, int mode, cudaStream_t st) {
     if ((reinterpret_cast<uintptr_t>(q) & 15) != 0 || ldq % 16 != 0)
         return fail(B2S_ERR_UNSUPPORTED, "tensor-core path needs 16-byte aligned q with ldq %% 16 == 0");
     if (M > (int64_t)0x7fffffff || w0.N > (int64_t)0x7fffffff) return fail(B2S_ERR_UNSUPPORTED, "size exceeds int32");
+    const int rows = (mode == 1) ? 64 : 128;
+    const TcTiling t = pick_tiling(M, w0.N, rows, w0.Kp, num_sms_current());
     b2s::TcGemmArgs a;
     memset(&a, 0, sizeof(a));
-    a.bn = pick_bn(M, mode == 1 ? 192 : 256);
     int rc;
-    if ((rc = make_tmap_u8(&a.tmap_q, q, (uint64_t)w0.K, (uint64_t)M, (uint64_t)ldq, 128, (uint32_t)a.bn, true)))
+    if ((rc = make_tmap_u8(&a.tmap_q, q, (uint64_t)w0.K, (uint64_t)M, (uint64_t)ldq, 128, (uint32_t)t.bn_sub, true)))
         return rc;
     if ((rc = make_tmap_u8(&a.tmap_w0, w0.codes, (uint64_t)(w0.Kp / 4), (uint64_t)w0.N, (uint64_t)(w0.Kp / 4), 32,
-                           128, false)))
+                           (uint32_t)rows, false)))
         return rc;
     if (mode == 1) {
         if ((rc = make_tmap_u8(&a.tmap_w1, w1->codes, (uint64_t)(w1->Kp / 4), (uint64_t)w1->N, (uint64_t)(w1->Kp / 4),
-                               32, 128, false)))
+                               32, (uint32_t)rows, false)))
             return rc;
     } else {
         a.tmap_w1 = a.tmap_w0;
@@ -196,12 +231,19 @@ int run_tc(const b2s::I2sWeight& w0, const b2s::I2sWeight* w1, const int8_t* q, 
     a.w0_scale = w0.scale;
     a.w1_scale = (mode == 1) ? w1->scale : w0.scale;
     a.s = s;
+    a.sums = sums;
     a.y = Y;
     a.ldy = ldy;
     a.M = (int)M;
     a.N = (int)w0.N;
     a.K = (int)w0.K;
     a.Kp = (int)w0.Kp;
+    a.T = t.T;
+    a.bn_sub = t.bn_sub;
+    a.nsub = t.nsub;
+    a.n_tiles = t.n_tiles;
+    a.m_tiles = t.m_tiles;
+    a.splits = t.splits;
     a.mode = mode;
     return launched(b2s::launch_gemm_i2s_tc(a, st), "gemm_i2s_tc launch");
 }
@@ -215,7 +257,7 @@ int mul_mat_q8_impl(const b2s::I2sWeight& w, const int8_t* q, int64_t ldq, const
         b2s::Q8Act a{q, s, sums, M, w.K, ldq};
         return launched(b2s::launch_gemv_i2s(w, a, Y, ldy, st), "gemv_i2s launch");
     }
-    return run_tc(w, nullptr, q, ldq, s, M, Y, ldy, 0, st);
+    return run_tc(w, nullptr, q, ldq, s, sums, M, Y, ldy, 0, st);
 }
 
 }  // namespace
@@ -439,7 +481,7 @@ int b2s_ffn_gate_up_sqrelu_q8(const b2s_tensor* W_gate, const b2s_tensor* W_up, 
     if (!q || !s || !sums || !P) return fail(B2S_ERR_INVALID_ARG, "gate_up: q, s, sums and P must be non-NULL");
     if (M < 0 || ldq < wg.K || ldp < wg.N) return fail(B2S_ERR_INVALID_ARG, "gate_up: bad M/ldq/ldp");
     if (M == 0) return B2S_OK;
-    return run_tc(wg, &wu, q, ldq, s, M, P, ldp, 1, static_cast<cudaStream_t>(stream));
+    return run_tc(wg, &wu, q, ldq, s, sums, M, P, ldp, 1, static_cast<cudaStream_t>(stream));
 }
 
 static void ffn_layout(int64_t M, int64_t H, int64_t F, WsLayout* l1, size_t* p_off, WsLayout* l2) {
@@ -487,7 +529,7 @@ int b2s_ffn_block(const float* X, int64_t M, const float* g1, const float* g2, f
     int32_t* u2 = reinterpret_cast<int32_t*>(ws + l2.sum_off);
     if ((rc = launched(b2s::launch_act_quant(X, H, g1, true, eps, M, H, q1, l1.ldq, s1, u1, st), "rms_norm_act_quant 1")))
         return rc;
-    if ((rc = run_tc(wg, &wu, q1, l1.ldq, s1, M, P, F, 1, st))) return rc;
+    if ((rc = run_tc(wg, &wu, q1, l1.ldq, s1, u1, M, P, F, 1, st))) return rc;
     if ((rc = launched(b2s::launch_act_quant(P, F, g2, true, eps, M, F, q2, l2.ldq, s2, u2, st), "rms_norm_act_quant 2")))
         return rc;
     return mul_mat_q8_impl(wd, q2, l2.ldq, s2, u2, M, Y, H, 0, st);

@@ -55,6 +55,13 @@ __device__ __forceinline__ float warp_sum_f(float v) {
     return v;
 }
 
+// ---------------------------------------------------------------- programmatic dependent launch
+// griddep_wait(): block until the preceding kernel in the stream (launched before this one with
+// programmatic stream serialization allowed) has completed and its memory is visible; a no-op otherwise.
+// griddep_launch(): allow the next such kernel to start launching its CTAs now.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // ---------------------------------------------------------------- shared-memory addresses
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));

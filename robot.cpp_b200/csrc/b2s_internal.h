@@ -31,16 +31,20 @@ cudaError_t launch_gemv_i2s(const I2sWeight& w, const Q8Act& a, float* y, int64_
 // Tensor-core path. mode 0: Y = W*q. mode 1 (gate/up): P = relu(Wg*q)^2 * (Wu*q).
 // tmap_* are built by the caller (host) for these exact buffers.
 struct TcGemmArgs {
-    CUtensorMap tmap_w0;  // packed codes of W (or W_gate), 2D u8 [N rows][Kp/4 bytes], box 32 x 128
-    CUtensorMap tmap_w1;  // packed codes of W_up (mode 1)
-    CUtensorMap tmap_q;   // int8 activations 2D [M rows][K], box 128 x BN, 128B swizzle
+    CUtensorMap tmap_w0;  // packed codes of W (or W_gate), 2D u8 [N rows][Kp/4 bytes], box 32 x 128 (64 in mode 1)
+    CUtensorMap tmap_w1;  // packed codes of W_up (mode 1), box 32 x 64
+    CUtensorMap tmap_q;   // int8 activations 2D [M rows][K], box 128 x bn_sub, 128B swizzle
     const float* w0_scale;
     const float* w1_scale;
     const float* s;       // act scales [M]
+    const int32_t* sums;  // act sums [M]
     float* y;
     int64_t ldy;
-    int M, N, K, Kp;
-    int bn;               // token tile (multiple of 16, <= 256; <= 192 in mode 1)
+    int M, N, K, Kp;      // N = output columns (F in mode 1)
+    int T;                // tokens per CTA = nsub * bn_sub (<= 320)
+    int bn_sub;           // MMA N per sub-tile (multiple of 16, <= 256)
+    int nsub;             // 1 or 2 sub-tiles
+    int n_tiles, m_tiles, splits;  // grid; splits = K-split CTAs per cluster (1..8)
     int mode;
 };
 cudaError_t launch_gemm_i2s_tc(const TcGemmArgs& args, cudaStream_t st);

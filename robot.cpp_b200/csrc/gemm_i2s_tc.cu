@@ -1,45 +1,62 @@
 // gemm_i2s_tc.cu -- prefill-size i2_s x int8 GEMM on the sm_100a tensor cores (tcgen05 kind::i8).
 //
-// Output tile: 128 weight rows (n) x BN tokens (m), BN a multiple of 16 up to 256.
-// The weights are the MMA's A operand and live in tensor memory; the activations are the B operand
-// in shared memory:
-//   * warp 4 (producer) TMA-loads, per 128-wide K step, the packed weight tile (128 rows x 32 bytes,
-//     local HBM, no multicast) and the int8 activation tile (BN rows x 128 bytes, 128B swizzle) into a
-//     ring of shared-memory stages;
-//   * warps 0-3 (converters) each own 32 TMEM lanes = 32 weight rows: a thread reads its row's
-//     32 packed bytes from shared memory, decodes the 2-bit codes to signed int8 {-1,0,1} in
-//     registers ((c + 0x7F) ^ 0x80 per byte) and stores the 128 int8 values with one
-//     tcgen05.st.32x32b.x32 into a ring of TMEM A stages, so the unpacked weights never touch
-//     shared-memory bandwidth;
-//   * warp 5 (MMA) issues, per K step, four tcgen05.mma.cta_group::1.kind::i8 (M=128, N=BN, K=32)
-//     reading A from TMEM and B through a K-major SW128 descriptor, accumulating int32 in TMEM;
-//   * warps 0-3 then read the accumulator back (tcgen05.ld) and write fp32
-//     y = (float)acc * (w_scale / s[m]) with coalesced 128-byte stores (32 consecutive n per warp).
-// Mode 1 (FFN gate/up) runs two weight matrices against the same activation tile into two
-// accumulators and writes p = relu(g)^2 * u, fusing the squared-ReLU gate product into the epilogue.
+// A CTA owns 128 weight rows and T tokens (T <= 320, as one or two MMA sub-tiles of bn_sub tokens).
+// The weights are the MMA's A operand and live in tensor memory; the activations are the B operand in
+// shared memory:
+//   * warp 4 (producer) TMA-loads, per 128-wide K step, the packed weight tile (128 rows x 32 bytes from
+//     local HBM, no multicast) and the int8 activation tile(s) (bn_sub rows x 128 bytes, 128B swizzle)
+//     into a 4-stage shared-memory ring. The weight tiles of the first ring round are requested before
+//     the kernel waits for its producer kernel (programmatic dependent launch), so their HBM latency
+//     overlaps the end of the preceding kernel;
+//   * warps 0-3 (converters) each own 32 TMEM lanes. A thread reads one weight row's 32 packed bytes and
+//     extracts the unsigned 2-bit codes {0,1,2} of each bit-plane with one shift and one mask per 4
+//     weights, then stores the 128 codes with one tcgen05.st.32x32b.x32 into the TMEM A stage that
+//     pairs with the shared-memory stage: the unpacked weights never touch shared memory;
+//   * warp 5 (MMA) issues, per 32-wide K slice and sub-tile, tcgen05.mma.cta_group::1.kind::i8 with
+//     A = unsigned codes from TMEM and B = signed int8 activations (K-major SW128 descriptor), M=128,
+//     N=bn_sub, int32 accumulators in TMEM. Since code = t + 1, acc = sum_k t_k q_k + sum_k q_k; the
+//     epilogue subtracts the per-token activation sum (the method of the fork's ggml_vec_dot_i2_i8_s);
+//   * warps 0-3 read the accumulators back (tcgen05.ld, two 16-token chunks per wait) and write fp32
+//     y = (float)(acc - sum_q[m]) * (w_scale / s[m]) with coalesced stores.
+// Mode 1 (FFN gate/up): in every converter warp, lanes 0-15 hold 16 gate rows and lanes 16-31 the 16 up
+// rows of the same output columns, so one accumulator set holds both and the epilogue pairs them with
+// one warp shuffle, writing p = relu(g)^2 * u (the squared-ReLU gate product fused into the GEMM).
 //
-// All waits are bounded; on a timeout the kernel records the error in g_device_error, drains what it
-// issued (bounded), frees its TMEM and returns.
+// Split-K across a thread-block cluster: when the output tiles alone cannot fill the GPU, the grid's
+// z dimension splits the K loop over the S CTAs of a cluster (1 x 1 x S). Each CTA stores its int32
+// partial tile from TMEM into its own shared memory; after a cluster barrier, CTA z reduces every S-th
+// 16-token chunk by reading the S partials through distributed shared memory (each rank's 16 loads in
+// flight at once, two ranks at a time). The int32 sum is exact, so the result is bit-identical to the
+// unsplit loop.
+//
+// All mbarrier waits are bounded (about one second); on a timeout the kernel records the error in
+// g_device_error, drains what it issued (bounded), still takes part in the cluster barriers, frees its
+// TMEM and returns.
 #include "b2s_common.cuh"
 #include "b2s_internal.h"
 
 namespace b2s {
 
 namespace tc {
-constexpr int kStages = 4;           // shared-memory ring (TMA)
-constexpr int kAStages = 4;          // TMEM A ring, 32 columns each
-constexpr int kBK = 128;             // K per stage (one 128-byte swizzle row of int8)
-constexpr int kActStageBytes = 256 * 128;
+constexpr int kStages = 4;             // shared-memory ring (TMA) = TMEM A ring
+constexpr int kBK = 128;               // K per stage: one 128-byte swizzle row of int8
+constexpr int kMaxT = 320;             // tokens per CTA
+constexpr int kActStageBytes = kMaxT * 128;
 constexpr int kWStageBytes = 128 * 32;
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;  // warps 0-3 converters+epilogue, 4 TMA, 5 MMA, 6-9 set-up+epilogue
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kAccCol = 128;    // accumulators start after the A ring
 
+// One ring index s serves the shared-memory stage and the TMEM A stage of the same K step:
+//   full[s]     TMA bytes of stage s landed (expect_tx; producer arrives once)
+//   afull[s]    the converters wrote TMEM A stage s (one arrival per converter warp)
+//   consumed[s] the MMAs of stage s completed (one tcgen05.commit): frees both the shared-memory
+//               stage (producer may refill it) and the TMEM A stage (converters may overwrite it); the
+//               converters read stage s's packed weights before arriving on afull[s], i.e. before
+//               those MMAs were issued.
 struct alignas(8) Bars {
     uint64_t full[kStages];
-    uint64_t empty[kStages];
-    uint64_t afull[kAStages];
-    uint64_t aempty[kAStages];
+    uint64_t afull[kStages];
+    uint64_t consumed[kStages];
     uint64_t accfull;
     uint64_t drain;
     uint32_t tmem_slot;
@@ -47,8 +64,9 @@ struct alignas(8) Bars {
 };
 
 constexpr size_t kSmemAct = (size_t)kStages * kActStageBytes;
-constexpr size_t kSmemW = (size_t)kStages * 2 * kWStageBytes;
-constexpr size_t kSmemBytes = 1024 /*align slack*/ + kSmemAct + kSmemW + 2 * 256 * sizeof(float) + sizeof(Bars);
+constexpr size_t kSmemW = (size_t)kStages * kWStageBytes;
+constexpr size_t kSmemBytes = 1024 /*align slack*/ + kSmemAct + kSmemW + 3 * kMaxT * sizeof(float) + sizeof(Bars);
+static_assert((size_t)128 * kMaxT * 4 <= kSmemAct, "split-K partial tile must fit in the stage ring");
 }  // namespace tc
 
 __device__ __forceinline__ void tmem_ld_32x32b_x16(uint32_t taddr, uint32_t (&r)[16]) {
@@ -61,60 +79,113 @@ __device__ __forceinline__ void tmem_ld_32x32b_x16(uint32_t taddr, uint32_t (&r)
         : "memory");
 }
 
-// Packed word (4 bytes = 4 consecutive k of each bit-plane) -> signed int8 {-1,0,1} for plane g.
-__device__ __forceinline__ uint32_t decode_plane(uint32_t w, int g) {
-    const uint32_t c = (w >> (6 - 2 * g)) & 0x03030303u;
-    return (c + 0x7F7F7F7Fu) ^ 0x80808080u;
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+    asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+// 16 int32 of CTA `rank`'s shared memory, 512 bytes apart (16 token columns of one row of the
+// column-major partial tile), starting where `local_addr` points locally. All 16 loads are issued before
+// any result is used; across the warp each load reads 32 consecutive rows = one 128-byte line.
+__device__ __forceinline__ void dsmem_ld_col16(uint32_t local_addr, uint32_t rank, int32_t (&v)[16]) {
+    uint32_t remote;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(local_addr), "r"(rank));
+    asm volatile(
+        "ld.shared::cluster.b32 %0, [%16];\n\t"
+        "ld.shared::cluster.b32 %1, [%16+512];\n\t"
+        "ld.shared::cluster.b32 %2, [%16+1024];\n\t"
+        "ld.shared::cluster.b32 %3, [%16+1536];\n\t"
+        "ld.shared::cluster.b32 %4, [%16+2048];\n\t"
+        "ld.shared::cluster.b32 %5, [%16+2560];\n\t"
+        "ld.shared::cluster.b32 %6, [%16+3072];\n\t"
+        "ld.shared::cluster.b32 %7, [%16+3584];\n\t"
+        "ld.shared::cluster.b32 %8, [%16+4096];\n\t"
+        "ld.shared::cluster.b32 %9, [%16+4608];\n\t"
+        "ld.shared::cluster.b32 %10, [%16+5120];\n\t"
+        "ld.shared::cluster.b32 %11, [%16+5632];\n\t"
+        "ld.shared::cluster.b32 %12, [%16+6144];\n\t"
+        "ld.shared::cluster.b32 %13, [%16+6656];\n\t"
+        "ld.shared::cluster.b32 %14, [%16+7168];\n\t"
+        "ld.shared::cluster.b32 %15, [%16+7680];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+        : "r"(remote)
+        : "memory");
+}
+
+// Instruction descriptor, kind::i8: D s32, A unsigned 8-bit (weight codes), B signed 8-bit
+// (activations), both K-major, shape 128 x N.
+__host__ __device__ constexpr uint32_t umma_idesc_u8s8(int M, int N) {
+    return (2u << 4) | (0u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 
 __global__ void __launch_bounds__(tc::kThreads, 1)
 gemm_i2s_tc_kernel(const __grid_constant__ CUtensorMap tmap_w0, const __grid_constant__ CUtensorMap tmap_w1,
                    const __grid_constant__ CUtensorMap tmap_q, const float* __restrict__ w0_scale,
-                   const float* __restrict__ w1_scale, const float* __restrict__ s_act, float* __restrict__ y,
-                   int64_t ldy, int M, int N, int Kp, int bn, int mode) {
+                   const float* __restrict__ w1_scale, const float* __restrict__ s_act,
+                   const int32_t* __restrict__ sum_act, float* __restrict__ y, int64_t ldy, int M, int N, int Kp,
+                   int T, int bn_sub, int nsub, int mode) {
     using namespace tc;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* act_sm = base;
     uint8_t* w_sm = base + kSmemAct;
-    float* rfac = reinterpret_cast<float*>(w_sm + kSmemW);  // [2][256]
-    Bars* bars = reinterpret_cast<Bars*>(rfac + 2 * 256);
+    float* rfac = reinterpret_cast<float*>(w_sm + kSmemW);         // [2][kMaxT]
+    int32_t* sumq = reinterpret_cast<int32_t*>(rfac + 2 * kMaxT);  // [kMaxT]
+    Bars* bars = reinterpret_cast<Bars*>(sumq + kMaxT);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int n0 = blockIdx.x * 128;
-    const int m0 = blockIdx.y * bn;
+    const int S = (int)gridDim.z;
+    const int zr = (int)blockIdx.z;
+    const int rows_per_w = (mode == 1) ? 64 : 128;          // weight rows of one matrix per CTA
+    const int nb = blockIdx.x * rows_per_w;                 // first output column of this CTA
+    const int m0 = blockIdx.y * T;
     const int nkt = Kp / kBK;
-    const int nw = mode == 1 ? 2 : 1;
-    const uint32_t acc_stride = (uint32_t)((bn + 31) / 32 * 32);
+    const int kt0 = (int)((int64_t)nkt * zr / S), kt1 = (int)((int64_t)nkt * (zr + 1) / S);
+    const int nk = kt1 - kt0;
+    const int npre = nk < kStages ? nk : kStages;
+    const uint32_t acc_stride = (uint32_t)((bn_sub + 31) / 32 * 32);
+    const uint32_t a_col0 = acc_stride * (uint32_t)nsub;    // TMEM A ring after the accumulators (<= 320)
+    const uint32_t tx = (uint32_t)T * 128u + (uint32_t)kWStageBytes;
 
-    if (threadIdx.x == 0) {
+    auto load_w = [&](int s, int kt) {
+        uint8_t* wst = w_sm + (size_t)s * kWStageBytes;
+        if (mode == 1) {
+            tma_load_2d(wst, &tmap_w0, &bars->full[s], kt * 32, nb);
+            tma_load_2d(wst + 64 * 32, &tmap_w1, &bars->full[s], kt * 32, nb);
+        } else {
+            tma_load_2d(wst, &tmap_w0, &bars->full[s], kt * 32, nb);
+        }
+    };
+
+    if (threadIdx.x == 128) {  // producer thread: barriers, descriptors, weights of the first ring round
         for (int i = 0; i < kStages; ++i) {
             mbar_init(&bars->full[i], 1);
-            mbar_init(&bars->empty[i], 1 + 128);
-        }
-        for (int i = 0; i < kAStages; ++i) {
-            mbar_init(&bars->afull[i], 128);
-            mbar_init(&bars->aempty[i], 1);
+            mbar_init(&bars->afull[i], 4);  // one arrival per converter warp
+            mbar_init(&bars->consumed[i], 1);
         }
         mbar_init(&bars->accfull, 1);
         mbar_init(&bars->drain, 1);
         bars->abort = 0;
         fence_mbar_init();
-    }
-    if (warp == 4 && lane == 0) {
         tma_prefetch_desc(&tmap_q);
         tma_prefetch_desc(&tmap_w0);
         if (mode == 1) tma_prefetch_desc(&tmap_w1);
+        for (int i = 0; i < npre; ++i) {  // weights do not depend on the preceding kernel
+            mbar_arrive_expect_tx(&bars->full[i], tx);
+            load_w(i, kt0 + i);
+        }
     }
     if (warp == 0) {
         tmem_alloc(&bars->tmem_slot, kTmemCols);
         tmem_relinquish();
-    }
-    // Per-token rescale factors w_scale / s[m] (one IEEE division per token and matrix).
-    for (int i = threadIdx.x; i < nw * bn; i += blockDim.x) {
-        const int j = i / bn, t = i - j * bn, m = m0 + t;
-        const float ws = __ldg(j == 0 ? w0_scale : w1_scale);
-        rfac[j * 256 + t] = (m < M) ? __fdiv_rn(ws, s_act[m]) : 0.0f;
     }
     tc_fence_before();
     __syncthreads();
@@ -122,56 +193,77 @@ gemm_i2s_tc_kernel(const __grid_constant__ CUtensorMap tmap_w0, const __grid_con
     const uint32_t tmem_base = bars->tmem_slot;
     volatile uint32_t* abort_flag = &bars->abort;
 
-    if (warp == 4) {
+    if (warp >= 6) {
+        // ------------------------------------------------------------------ epilogue group B: set-up
+        // Per-token rescale factors w_scale / s[m] (one IEEE division per token and matrix) and the
+        // activation sums, computed while the main loop runs.
+        griddep_wait();  // scales and sums come from the preceding kernel
+        const int nmat = (mode == 1) ? 2 : 1;
+        const int tid = threadIdx.x - 192;
+        for (int i = tid; i < nmat * T; i += 128) {
+            const int j = i / T, t = i - j * T, m = m0 + t;
+            const float ws = __ldg(j == 0 ? w0_scale : w1_scale);
+            rfac[j * kMaxT + t] = (m < M) ? __fdiv_rn(ws, s_act[m]) : 0.0f;
+        }
+        for (int t = tid; t < T; t += 128) sumq[t] = (m0 + t < M) ? sum_act[m0 + t] : 0;
+        int good = 1;
+        if (lane == 0) good = mbar_wait(&bars->accfull, 0);
+        if (!__shfl_sync(0xffffffffu, good, 0) && lane == 0) *abort_flag = 1;
+        __syncwarp();
+        tc_fence_after();
+    } else if (warp == 4) {
         // ------------------------------------------------------------------ TMA producer
         if (lane == 0) {
-            const uint32_t tx = (uint32_t)bn * 128u + (uint32_t)nw * kWStageBytes;
+            griddep_wait();  // the activation tiles are written by the preceding kernel
             int issued = 0;
-            for (int kt = 0; kt < nkt; ++kt) {
-                const int s = kt % kStages;
-                const uint32_t ph = (uint32_t)(kt / kStages) & 1u;
-                if (*abort_flag || !mbar_wait(&bars->empty[s], ph ^ 1u)) { *abort_flag = 1; break; }
-                mbar_arrive_expect_tx(&bars->full[s], tx);
-                tma_load_2d(act_sm + (size_t)s * kActStageBytes, &tmap_q, &bars->full[s], kt * kBK, m0);
-                tma_load_2d(w_sm + (size_t)(s * 2 + 0) * kWStageBytes, &tmap_w0, &bars->full[s], kt * 32, n0);
-                if (mode == 1)
-                    tma_load_2d(w_sm + (size_t)(s * 2 + 1) * kWStageBytes, &tmap_w1, &bars->full[s], kt * 32, n0);
+            int s = 0;
+            uint32_t ph = 0;
+            for (int it = 0; it < nk; ++it) {
+                const int kt = kt0 + it;
+                if (it >= kStages) {  // first-round stages were armed before the setup barrier
+                    if (!mbar_wait(&bars->consumed[s], ph ^ 1u) || *abort_flag) { *abort_flag = 1; break; }
+                    mbar_arrive_expect_tx(&bars->full[s], tx);
+                    load_w(s, kt);
+                }
+                uint8_t* act = act_sm + (size_t)s * kActStageBytes;
+                for (int u = 0; u < nsub; ++u)
+                    tma_load_2d(act + (size_t)u * bn_sub * 128, &tmap_q, &bars->full[s], kt * kBK, m0 + u * bn_sub);
                 ++issued;
+                if (++s == kStages) { s = 0; ph ^= 1u; }
             }
             if (*abort_flag) {  // drain copies still in flight before the CTA's shared memory goes away
-                for (int kt = (issued > kStages ? issued - kStages : 0); kt < issued; ++kt)
-                    mbar_wait(&bars->full[kt % kStages], (uint32_t)(kt / kStages) & 1u, 2u);
+                for (int it = (issued > kStages ? issued - kStages : 0); it < issued; ++it)
+                    mbar_wait(&bars->full[it % kStages], (uint32_t)(it / kStages) & 1u, 2u);
             }
         }
     } else if (warp == 5) {
         // ------------------------------------------------------------------ MMA issuer
         if (lane == 0) {
-            const uint32_t idesc = umma_idesc_i8(128, bn);
-            int ai = 0;
+            const uint32_t idesc = umma_idesc_u8s8(128, bn_sub);
+            const uint32_t act_base = smem_u32(act_sm);
+            const uint32_t sub_bytes = (uint32_t)bn_sub * 128u;
             bool issued_any = false;
-            for (int kt = 0; kt < nkt && !*abort_flag; ++kt) {
-                const int s = kt % kStages;
-                const uint32_t ph = (uint32_t)(kt / kStages) & 1u;
-                if (!mbar_wait(&bars->full[s], ph)) { *abort_flag = 1; break; }
-                const uint32_t b_base = smem_u32(act_sm + (size_t)s * kActStageBytes);
-                bool ok = true;
-                for (int j = 0; j < nw; ++j, ++ai) {
-                    const int a = ai % kAStages;
-                    const uint32_t aph = (uint32_t)(ai / kAStages) & 1u;
-                    if (!mbar_wait(&bars->afull[a], aph)) { ok = false; break; }
-                    tc_fence_after();
-                    const uint32_t d_tmem = tmem_base + kAccCol + (uint32_t)j * acc_stride;
+            uint32_t acc_flag = 0;  // first MMA of each accumulator overwrites it
+            int s = 0;
+            uint32_t ph = 0;
+            for (int it = 0; it < nk; ++it) {
+                // afull[s] is arrived only after the converters observed full[s]; waiting on full[s] as
+                // well makes the TMA bytes of the activation tile visible to this thread's MMAs.
+                if (!mbar_wait(&bars->afull[s], ph) || !mbar_wait(&bars->full[s], ph)) { *abort_flag = 1; break; }
+                tc_fence_after();
+                const uint32_t b_base = act_base + (uint32_t)s * kActStageBytes;
+                const uint32_t a_base = tmem_base + a_col0 + (uint32_t)s * 32u;
 #pragma unroll
-                    for (int kk = 0; kk < kBK / 32; ++kk) {
-                        const uint64_t bdesc = umma_desc_k_sw128(b_base + kk * 32);
-                        const uint32_t a_tmem = tmem_base + (uint32_t)(a * 32 + kk * 8);
-                        tc_mma_i8_ts(d_tmem, a_tmem, bdesc, idesc, (kt > 0 || kk > 0) ? 1u : 0u);
-                    }
-                    issued_any = true;
-                    tc_commit(&bars->aempty[a]);
+                for (int kk = 0; kk < kBK / 32; ++kk) {
+                    tc_mma_i8_ts(tmem_base, a_base + kk * 8, umma_desc_k_sw128(b_base + kk * 32), idesc, acc_flag);
+                    if (nsub == 2)
+                        tc_mma_i8_ts(tmem_base + acc_stride, a_base + kk * 8,
+                                     umma_desc_k_sw128(b_base + sub_bytes + kk * 32), idesc, acc_flag);
+                    acc_flag = 1;
                 }
-                if (!ok) { *abort_flag = 1; break; }
-                tc_commit(&bars->empty[s]);
+                issued_any = true;
+                tc_commit(&bars->consumed[s]);
+                if (++s == kStages) { s = 0; ph ^= 1u; }
             }
             if (!*abort_flag) {
                 tc_commit(&bars->accfull);
@@ -182,65 +274,170 @@ gemm_i2s_tc_kernel(const __grid_constant__ CUtensorMap tmap_w0, const __grid_con
         }
     } else {
         // ------------------------------------------------------------------ converters (warps 0-3)
-        const int row = threadIdx.x;  // TMEM lane == weight row within the tile
+        // TMEM lane L = threadIdx.x holds weight row r_sm of the stage: in mode 1, lanes 0-15 of each warp
+        // take gate rows 16w..16w+15 (stage rows 0-63) and lanes 16-31 the up rows of the same output
+        // columns (stage rows 64-127).
+        const int r_sm = (mode == 1) ? ((lane < 16) ? (16 * warp + lane) : (64 + 16 * warp + lane - 16))
+                                     : (int)threadIdx.x;
         const uint32_t lane_base = tmem_base + ((uint32_t)(warp * 32) << 16);
-        int ai = 0;
-        for (int kt = 0; kt < nkt && !*abort_flag; ++kt) {
-            const int s = kt % kStages;
-            const uint32_t ph = (uint32_t)(kt / kStages) & 1u;
-            if (!mbar_wait(&bars->full[s], ph)) { *abort_flag = 1; break; }
-            uint4 pk[2][2];
-            for (int j = 0; j < nw; ++j) {
-                const uint4* src = reinterpret_cast<const uint4*>(w_sm + (size_t)(s * 2 + j) * kWStageBytes + row * 32);
-                pk[j][0] = src[0];
-                pk[j][1] = src[1];
-            }
-            mbar_arrive(&bars->empty[s]);
-            bool ok = true;
-            for (int j = 0; j < nw; ++j, ++ai) {
-                const int a = ai % kAStages;
-                const uint32_t aph = (uint32_t)(ai / kAStages) & 1u;
-                if (!mbar_wait(&bars->aempty[a], aph ^ 1u)) { ok = false; break; }
-                const uint32_t w[8] = {pk[j][0].x, pk[j][0].y, pk[j][0].z, pk[j][0].w,
-                                       pk[j][1].x, pk[j][1].y, pk[j][1].z, pk[j][1].w};
-                uint32_t out[32];
+        // Lane 0 waits on the barriers and the warp follows (a timed-out wait is broadcast with
+        // __shfl_sync), so control flow stays warp-uniform for the .sync.aligned tcgen05.st.
+        bool ok = true;
+        int s = 0;
+        uint32_t ph = 0;
+        for (int it = 0; it < nk; ++it) {
+            int good = 1;
+            if (lane == 0) good = (*abort_flag == 0) && mbar_wait(&bars->full[s], ph);
+            if (!__shfl_sync(0xffffffffu, good, 0)) { ok = false; break; }
+            // Every lane acquires the completed phase itself before reading the TMA-written bytes (the
+            // phase cannot advance: stage s is refilled only after this warp arrives on afull[s]).
+            (void)mbar_try_wait(&bars->full[s], ph);
+            const uint4* src = reinterpret_cast<const uint4*>(w_sm + (size_t)s * kWStageBytes + r_sm * 32);
+            const uint4 p0 = src[0], p1 = src[1];
+            if (lane == 0) good = mbar_wait(&bars->consumed[s], ph ^ 1u);  // TMEM A stage s is free
+            if (!__shfl_sync(0xffffffffu, good, 0)) { ok = false; break; }
+            const uint32_t w[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
+            uint32_t out[32];
 #pragma unroll
-                for (int g = 0; g < 4; ++g)
-#pragma unroll
-                    for (int p = 0; p < 8; ++p) out[8 * g + p] = decode_plane(w[p], g);
-                tmem_st_32x32b_x32(lane_base + (uint32_t)(a * 32), out);
-                tc_wait_st();
-                tc_fence_before();
-                mbar_arrive(&bars->afull[a]);
+            for (int p = 0; p < 8; ++p) {
+                out[p] = (w[p] >> 6) & 0x03030303u;       // k = 4p..4p+3
+                out[8 + p] = (w[p] >> 4) & 0x03030303u;   // k = 32+4p..
+                out[16 + p] = (w[p] >> 2) & 0x03030303u;  // k = 64+4p..
+                out[24 + p] = w[p] & 0x03030303u;         // k = 96+4p..
             }
-            if (!ok) { *abort_flag = 1; break; }
+            tmem_st_32x32b_x32(lane_base + a_col0 + (uint32_t)(s * 32), out);
+            tc_wait_st();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bars->afull[s]);
+            if (++s == kStages) { s = 0; ph ^= 1u; }
         }
-        // ------------------------------------------------------------------ epilogue (warps 0-3)
-        if (!*abort_flag && mbar_wait(&bars->accfull, 0)) {
-            tc_fence_after();
-            const int n = n0 + row;
-            for (int c = 0; c < bn / 16; ++c) {
-                uint32_t a0[16], a1[16];
-                tmem_ld_32x32b_x16(lane_base + kAccCol + (uint32_t)(c * 16), a0);
-                if (mode == 1) tmem_ld_32x32b_x16(lane_base + kAccCol + acc_stride + (uint32_t)(c * 16), a1);
-                tc_wait_ld();
+        if (!ok && lane == 0) *abort_flag = 1;
+        int good = ok ? 1 : 0;
+        if (lane == 0 && good) good = mbar_wait(&bars->accfull, 0);
+        if (!__shfl_sync(0xffffffffu, good, 0) && lane == 0) *abort_flag = 1;
+        __syncwarp();
+        tc_fence_after();
+    }
+    griddep_launch();  // the next kernel may start its prologue while this one writes its outputs
+
+    // ---------------------------------------------------------------------- epilogue
+    // Two epilogue groups: warps 0-3 (group 0) and warps 6-9 (group 1). Warp w reads TMEM lane quadrant
+    // w % 4, so each quadrant has one warp per group; the groups take alternate token chunk pairs.
+    const bool split = S > 1;
+    const int nchunk = T / 16;
+    const bool epi = (warp < 4) || (warp >= 6);
+    const int egrp = (warp < 4) ? 0 : 1;
+    const int q = warp & 3;                                                  // TMEM lane quadrant
+    const int row = 32 * q + lane;                                           // TMEM lane
+    int32_t* part = reinterpret_cast<int32_t*>(act_sm);  // [T tokens][128 rows] int32 (column-major)
+    auto chunk_col = [&](int ch) -> uint32_t {           // TMEM column of 16-token chunk ch
+        const int t0 = ch * 16, u = t0 / bn_sub;
+        return (uint32_t)u * acc_stride + (uint32_t)(t0 - u * bn_sub);
+    };
+    // Loads the raw accumulators of chunks ch and ch+1 (if hb) for this thread's TMEM lane.
+    auto load_pair = [&](int ch, bool hb, bool good, int32_t (&ra)[16], int32_t (&rb)[16]) {
+        uint32_t a[16], b[16];
+        const uint32_t lane_base = tmem_base + ((uint32_t)(q * 32) << 16);
+        if (good) {
+            tmem_ld_32x32b_x16(lane_base + chunk_col(ch), a);
+            if (hb) tmem_ld_32x32b_x16(lane_base + chunk_col(ch + 1), b);
+            tc_wait_ld();
+        }
 #pragma unroll
-                for (int j = 0; j < 16; ++j) {
-                    const int t = c * 16 + j, m = m0 + t;
-                    float v = __fmul_rn((float)(int32_t)a0[j], rfac[t]);
-                    if (mode == 1) {
-                        const float u = __fmul_rn((float)(int32_t)a1[j], rfac[256 + t]);
-                        const float r = v > 0.0f ? v : 0.0f;
-                        v = __fmul_rn(__fmul_rn(r, r), u);
-                    }
-                    if (m < M && n < N) y[(int64_t)m * ldy + n] = v;
+        for (int j = 0; j < 16; ++j) {
+            ra[j] = good ? (int32_t)a[j] : 0;
+            rb[j] = (good && hb) ? (int32_t)b[j] : 0;
+        }
+    };
+
+    if (split) {
+        __syncthreads();  // every role has left the main loop: the rings are free; rfac/sumq are ready
+        if (epi) {
+            const bool good = __all_sync(0xffffffffu, *abort_flag == 0);
+            for (int ch = 2 * egrp; ch < nchunk; ch += 4) {
+                int32_t ra[16], rb[16];
+                const bool hb = ch + 1 < nchunk;
+                load_pair(ch, hb, good, ra, rb);
+                int32_t* dst = part + (ch * 16) * 128 + row;
+#pragma unroll
+                for (int j = 0; j < 16; ++j) dst[j * 128] = ra[j];
+                if (hb) {
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) dst[(16 + j) * 128] = rb[j];
                 }
             }
+        }
+        cluster_sync_all();
+    } else if (epi) {
+        named_bar_sync(2, 256);  // group 1's rfac/sumq are visible to group 0
+    }
+
+    if (epi) {
+        const bool good = __all_sync(0xffffffffu, *abort_flag == 0);
+        const int gu = (mode == 1) ? (lane >> 4) : 0;                     // 0 gate / 1 up lane (mode 1)
+        const int n = (mode == 1) ? nb + 16 * q + (lane & 15) : nb + row;  // output column
+
+        auto finish = [&](int ch, const int32_t (&raw)[16]) {
+            const int t0 = ch * 16;
+            if (mode == 0) {
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    const int t = t0 + j, m = m0 + t;
+                    const float v = __fmul_rn((float)(raw[j] - sumq[t]), rfac[t]);
+                    if (good && m < M && n < N) y[(int64_t)m * ldy + n] = v;
+                }
+            } else {
+                float p[16];
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    const int t = t0 + j;
+                    const float v = __fmul_rn((float)(raw[j] - sumq[t]), rfac[gu * kMaxT + t]);
+                    const float o = __shfl_xor_sync(0xffffffffu, v, 16);
+                    const float g = gu ? o : v, u = gu ? v : o;
+                    const float rg = g > 0.0f ? g : 0.0f;
+                    p[j] = __fmul_rn(__fmul_rn(rg, rg), u);
+                }
+                // gate lanes store tokens 0-7 of the chunk, up lanes tokens 8-15 (same 16 columns)
+#pragma unroll
+                for (int jj = 0; jj < 8; ++jj) {
+                    const float v = gu ? p[8 + jj] : p[jj];
+                    const int m = m0 + t0 + gu * 8 + jj;
+                    if (good && m < M && n < N) y[(int64_t)m * ldy + n] = v;
+                }
+            }
+        };
+
+        if (split) {
+            const int rank = (int)cluster_ctarank();
+            int i = 0;
+            for (int ch = rank; ch < nchunk; ch += S, ++i) {
+                if ((i & 1) != egrp) continue;
+                int32_t raw[16];
+#pragma unroll
+                for (int j = 0; j < 16; ++j) raw[j] = 0;
+                const uint32_t addr = smem_u32(part + (ch * 16) * 128 + row);
+                for (int r = 0; r < S; r += 2) {
+                    int32_t a[16], b[16];
+                    if (good) dsmem_ld_col16(addr, (uint32_t)r, a);
+                    if (good && r + 1 < S) dsmem_ld_col16(addr, (uint32_t)(r + 1), b);
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) raw[j] += (good ? a[j] : 0) + ((good && r + 1 < S) ? b[j] : 0);
+                }
+                finish(ch, raw);
+            }
         } else {
-            *abort_flag = 1;
+            for (int ch = 2 * egrp; ch < nchunk; ch += 4) {
+                int32_t ra[16], rb[16];
+                const bool hb = ch + 1 < nchunk;
+                load_pair(ch, hb, good, ra, rb);
+                finish(ch, ra);
+                if (hb) finish(ch + 1, rb);
+            }
         }
     }
 
+    if (split) cluster_sync_all();  // partials stay readable until every CTA of the cluster is done
     tc_fence_before();
     __syncthreads();
     if (warp == 0) {
@@ -257,11 +454,22 @@ cudaError_t launch_gemm_i2s_tc(const TcGemmArgs& a, cudaStream_t st) {
         if (e != cudaSuccess) return e;
         attr_set = true;
     }
-    dim3 grid((unsigned)ceil_div(a.N, 128), (unsigned)ceil_div(a.M, a.bn));
-    gemm_i2s_tc_kernel<<<grid, tc::kThreads, tc::kSmemBytes, st>>>(a.tmap_w0, a.tmap_w1, a.tmap_q, a.w0_scale,
-                                                                     a.w1_scale, a.s, a.y, a.ldy, a.M, a.N, a.Kp,
-                                                                     a.bn, a.mode);
-    return cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)a.n_tiles, (unsigned)a.m_tiles, (unsigned)a.splits);
+    cfg.blockDim = dim3(tc::kThreads);
+    cfg.dynamicSmemBytes = tc::kSmemBytes;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = (unsigned)a.splits;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    return cudaLaunchKernelEx(&cfg, gemm_i2s_tc_kernel, a.tmap_w0, a.tmap_w1, a.tmap_q, a.w0_scale, a.w1_scale, a.s,
+                              a.sums, a.y, a.ldy, a.M, a.N, a.Kp, a.T, a.bn_sub, a.nsub, a.mode);
 }
 
 }  // namespace b2s
