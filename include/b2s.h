@@ -114,7 +114,7 @@ size_t b2s_mul_mat_workspace_size(const b2s_tensor *W, const b2s_tensor *X);
 
 /* The MUL_MAT node: Y = mul_mat(W, X). W: I2_S (ne0 % 128 == 0) or I2_S_R, ne=[K,N], contiguous;
  * X: F32 ne=[K,M], rows contiguous (nb[0] = 4); Y: F32 ne=[N,M], rows contiguous. Uses the caller's
- * workspace for the quantized activations; allocates nothing. Decode sizes (M <= 8) run the dp4a GEMV,
+ * workspace for the quantized activations; allocates nothing. Decode sizes (M <= 16) run the dp4a GEMV,
  * larger M the tcgen05 tensor-core GEMM. */
 int b2s_mul_mat(const b2s_tensor *W, const b2s_tensor *X, b2s_tensor *Y, void *workspace, size_t workspace_bytes,
                 void *stream);

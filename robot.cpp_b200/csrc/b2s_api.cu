@@ -252,7 +252,7 @@ int run_tc(const b2s::I2sWeight& w0, const b2s::I2sWeight* w1, const int8_t* q, 
 int mul_mat_q8_impl(const b2s::I2sWeight& w, const int8_t* q, int64_t ldq, const float* s, const int32_t* sums,
                     int64_t M, float* Y, int64_t ldy, int path, cudaStream_t st) {
     if (M <= 0) return B2S_OK;
-    if (path == 0) path = (M <= 8) ? 1 : 2;
+    if (path == 0) path = (M <= 16) ? 1 : 2;
     if (path == 1) {
         b2s::Q8Act a{q, s, sums, M, w.K, ldq};
         return launched(b2s::launch_gemv_i2s(w, a, Y, ldy, st), "gemv_i2s launch");

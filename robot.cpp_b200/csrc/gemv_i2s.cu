@@ -1,4 +1,4 @@
-// gemv_i2s.cu -- decode-size (M <= 8) i2_s x int8 GEMV with dp4a.
+// gemv_i2s.cu -- decode-size (M <= 16) i2_s x int8 GEMV with dp4a.
 //
 // Streams the packed 2-bit weights once from HBM with 128-bit loads and decodes them in registers:
 // a 16-byte half of a 32-byte i2_s block holds, for each of its 4 bit-planes g, 16 consecutive
@@ -41,9 +41,9 @@ __device__ __forceinline__ int dp4a_us(uint32_t a, int b, int c) {
 template <int MT>
 __global__ void __launch_bounds__(kGemvWarps * 32)
 gemv_i2s_kernel(const uint8_t* __restrict__ codes, const float* __restrict__ wscale, int N, int Kp,
-                const int8_t* __restrict__ q, int64_t ldq, int K, const float* __restrict__ s,
+                const int8_t* __restrict__ q, int64_t ldq, int K, int mrows, const float* __restrict__ s,
                 const int32_t* __restrict__ sums, float* __restrict__ y, int64_t ldy) {
-    extern __shared__ __align__(16) uint8_t q_sm[];  // MT x Kp int8, zero beyond K
+    extern __shared__ __align__(16) uint8_t q_sm[];  // MT x Kp int8, zero beyond K and beyond mrows
     __shared__ int red[kGemvWarps][kGemvRows][MT];
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -62,7 +62,8 @@ gemv_i2s_kernel(const uint8_t* __restrict__ codes, const float* __restrict__ wsc
     for (int u = 0; u < kGemvUnroll; ++u)
         if (u < cnt && row_ok) wv[u] = ld_stream_v4(wr + 32 * (b + u));
 
-    griddep_wait();  // activations are produced by the preceding kernel
+    griddep_launch();  // the next kernel may start streaming its own weights now
+    griddep_wait();    // activations are produced by the preceding kernel
 
     // Stage q (MT rows of K int8) into shared memory, zero-filling [K, Kp).
     const int cpr = Kp / 16;  // 16-byte chunks per token row
@@ -71,7 +72,9 @@ gemv_i2s_kernel(const uint8_t* __restrict__ codes, const float* __restrict__ wsc
         const int m = i / cpr, c = i - m * cpr, k0 = c * 16;
         uint4 v = make_uint4(0, 0, 0, 0);
         const int8_t* src = q + (int64_t)m * ldq + k0;
-        if (q_vec && k0 + 16 <= K) {
+        if (m >= mrows) {
+            // token rows beyond M stay zero (their outputs are not stored)
+        } else if (q_vec && k0 + 16 <= K) {
             v = *reinterpret_cast<const uint4*>(src);
         } else {
             uint8_t tmp[16];
@@ -120,8 +123,6 @@ gemv_i2s_kernel(const uint8_t* __restrict__ codes, const float* __restrict__ wsc
             if (u < cnt && row_ok) wv[u] = ld_stream_v4(wr + 32 * (b + u));
     }
 
-    griddep_launch();
-
 #pragma unroll
     for (int m = 0; m < MT; ++m) {
         const int v = acc[m] + __shfl_xor_sync(0xffffffffu, acc[m], 1);
@@ -131,7 +132,7 @@ gemv_i2s_kernel(const uint8_t* __restrict__ codes, const float* __restrict__ wsc
     for (int t = threadIdx.x; t < kGemvRows * MT; t += blockDim.x) {
         const int rr = t / MT, m = t - rr * MT;
         const int n = blockIdx.x * kGemvRows + rr;
-        if (n < N) {
+        if (n < N && m < mrows) {
             int tot = 0;
 #pragma unroll
             for (int w = 0; w < kGemvWarps; ++w) tot += red[w][rr][m];
@@ -142,8 +143,8 @@ gemv_i2s_kernel(const uint8_t* __restrict__ codes, const float* __restrict__ wsc
 }
 
 template <int MT>
-static cudaError_t launch_mt(const I2sWeight& w, const int8_t* q, int64_t ldq, const float* s, const int32_t* sums,
-                             float* y, int64_t ldy, cudaStream_t st) {
+static cudaError_t launch_mt(const I2sWeight& w, const int8_t* q, int64_t ldq, int mrows, const float* s,
+                             const int32_t* sums, float* y, int64_t ldy, cudaStream_t st) {
     const size_t smem = (size_t)MT * (size_t)w.Kp;
     auto kfn = gemv_i2s_kernel<MT>;
     // Dynamic + static shared memory above 48 KB needs the opt-in attribute (raised once per size).
@@ -163,26 +164,25 @@ static cudaError_t launch_mt(const I2sWeight& w, const int8_t* q, int64_t ldq, c
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, kfn, w.codes, w.scale, (int)w.N, (int)w.Kp, q, ldq, (int)w.K, s, sums, y, ldy);
+    return cudaLaunchKernelEx(&cfg, kfn, w.codes, w.scale, (int)w.N, (int)w.Kp, q, ldq, (int)w.K, mrows, s, sums, y,
+                              ldy);
 }
 
 cudaError_t launch_gemv_i2s(const I2sWeight& w, const Q8Act& a, float* y, int64_t ldy, cudaStream_t st) {
-    // Token groups of up to 8; each group is one launch over all rows.
-    for (int64_t m0 = 0; m0 < a.M; m0 += 8) {
-        const int64_t mt = (a.M - m0) < 8 ? (a.M - m0) : 8;
+    // Token groups of up to 16, each one pass over the weights; a group of m tokens runs the smallest
+    // power-of-two variant >= m with the extra token rows zero.
+    for (int64_t m0 = 0; m0 < a.M; m0 += 16) {
+        const int mt = (int)((a.M - m0) < 16 ? (a.M - m0) : 16);
         const int8_t* q = a.q + m0 * a.ldq;
         const float* s = a.s + m0;
         const int32_t* sums = a.sums + m0;
         float* yy = y + m0 * ldy;
         cudaError_t e;
-        if (mt == 1) e = launch_mt<1>(w, q, a.ldq, s, sums, yy, ldy, st);
-        else if (mt == 2) e = launch_mt<2>(w, q, a.ldq, s, sums, yy, ldy, st);
-        else if (mt <= 4) e = (mt == 4) ? launch_mt<4>(w, q, a.ldq, s, sums, yy, ldy, st)
-                                        : launch_mt<3>(w, q, a.ldq, s, sums, yy, ldy, st);
-        else if (mt == 8) e = launch_mt<8>(w, q, a.ldq, s, sums, yy, ldy, st);
-        else if (mt == 5) e = launch_mt<5>(w, q, a.ldq, s, sums, yy, ldy, st);
-        else if (mt == 6) e = launch_mt<6>(w, q, a.ldq, s, sums, yy, ldy, st);
-        else e = launch_mt<7>(w, q, a.ldq, s, sums, yy, ldy, st);
+        if (mt == 1) e = launch_mt<1>(w, q, a.ldq, mt, s, sums, yy, ldy, st);
+        else if (mt == 2) e = launch_mt<2>(w, q, a.ldq, mt, s, sums, yy, ldy, st);
+        else if (mt <= 4) e = launch_mt<4>(w, q, a.ldq, mt, s, sums, yy, ldy, st);
+        else if (mt <= 8) e = launch_mt<8>(w, q, a.ldq, mt, s, sums, yy, ldy, st);
+        else e = launch_mt<16>(w, q, a.ldq, mt, s, sums, yy, ldy, st);
         if (e != cudaSuccess) return e;
     }
     return cudaGetLastError();

@@ -110,7 +110,7 @@ def run_q8(b2s, orc, M, K, N, path, seed):
     return y.cpu().numpy(), y_ref
 
 
-@pytest.mark.parametrize("M", [1, 2, 3, 5, 8, 13])
+@pytest.mark.parametrize("M", [1, 2, 3, 5, 8, 13, 16, 21])
 @pytest.mark.parametrize("K,N", [(2560, 2560), (1152, 4304), (256, 40), (6912, 2560)])
 def test_gemv_path(b2s, orc, M, K, N):
     y, y_ref = run_q8(b2s, orc, M, K, N, path=1, seed=M * 7 + K + N)
