@@ -156,6 +156,49 @@ int b2s_ffn_block(const float *X, int64_t M, const float *g1, const float *g2, f
                   const b2s_tensor *W_up, const b2s_tensor *W_down, float *Y, void *workspace,
                   size_t workspace_bytes, void *stream);
 
+/* MUL_MAT on quantized activations with a fused epilogue, applied in this order to y = acc*w_scale/s[m]:
+ * y += bias[n] (bias may be NULL); y = gelu_tanh(y) if act == 1 (ggml_gelu, tanh approximation);
+ * y = residual[m*ld_res + n] + y (residual may be NULL; it may alias Y). Covers the ggml_add(bias),
+ * ggml_gelu and residual ggml_add nodes that follow a linear layer (src/models/smolvla/vision.cpp:314-345). */
+int b2s_mul_mat_q8_epi(const b2s_tensor *W, const int8_t *q, int64_t ldq, const float *s, const int32_t *sums,
+                       int64_t M, float *Y, int64_t ldy, const float *bias, const float *residual, int64_t ld_res,
+                       int act, void *stream);
+
+/* Normalization of M rows of K floats, written as fp32: kind 0 = ggml_rms_norm, kind 1 = ggml_norm
+ * (LayerNorm), then * g (ggml_mul, g may be NULL) and + b (ggml_add, b may be NULL). eps as in ggml. */
+int b2s_norm(const float *x, const float *g, const float *b, int64_t M, int64_t K, int64_t ldx, float eps, int kind,
+             float *y, int64_t ldy, void *stream);
+/* The same normalization followed by the per-token act-quant (b2s_act_quant semantics). */
+int b2s_norm_act_quant(const float *x, const float *g, const float *b, int64_t M, int64_t K, int64_t ldx, float eps,
+                       int kind, int8_t *q, int64_t ldq, float *s, int32_t *sums, void *stream);
+
+/* In-place NEOX rotary embedding (ggml_rope_ext, mode NEOX; src/models/pi0/vlm.cpp:223-235) of M rows of
+ * n_heads heads of head_dim floats at row stride ld; token m has position pos0 + m. */
+int b2s_rope_neox(float *x, int64_t M, int n_heads, int head_dim, int64_t ld, float theta_base, int pos0, void *stream);
+
+/* Multi-head attention softmax(Q K^T * scale [+ causal mask]) V over M tokens, fp32, with n_heads query
+ * heads sharing n_kv_heads key/value heads (GQA; n_heads % n_kv_heads == 0). Q/K/V/O rows hold the heads
+ * side by side (head h at columns [h*head_dim, (h+1)*head_dim)). The ggml sequence mul_mat(K, Q) ->
+ * soft_max_ext -> mul_mat(V, KQ) (src/models/smolvla/action_expert.cpp:771-774) as one fused kernel with a
+ * fixed fp32 operation order: scores = fma-accumulated dot products (d ascending) times scale, the
+ * b2s_soft_max_ext softmax, outputs = fma-accumulated sums over keys (ascending). Needs head_dim % 8 == 0,
+ * head_dim <= 128, leading dimensions % 4 == 0, 16-byte aligned tensors and
+ * 4 * (128 * head_dim + 64 * (roundup(M, 64) + 4)) <= 227 KB of shared memory (M <= 576 at head_dim 128);
+ * B2S_ERR_UNSUPPORTED otherwise. */
+int b2s_attention(const float *q, int64_t ldq, const float *k, int64_t ldk, const float *v, int64_t ldv, int64_t M,
+                  int n_heads, int n_kv_heads, int head_dim, float scale, int causal, float *o, int64_t ldo,
+                  void *stream);
+
+/* Patch embedding of a CHW fp32 image: non-overlapping P x P patches (row-major patch order) times the
+ * [D][C*P*P] weight, plus bias[D] and the position embedding pos[n_patches][D] (either may be NULL):
+ * y = (bias + pos) + acc, acc fma-accumulated over k = c*P*P + ky*P + kx ascending. */
+int b2s_patch_embed(const float *img, int C, int H, int W, int P, const float *w, const float *bias, const float *pos,
+                    int D, float *y, int64_t ldy, void *stream);
+
+/* Random-init token embeddings: y[i][c] = -0.02 + 0.04 * ((b2s_bitvla_param_bits(seed, 0x80000000 | tokens[i], c)
+ * >> 8) * 2^-24) for c < dim, fp32 (the BitVLA engine's text embedding; no 128256-row table is materialized). */
+int b2s_embed_tokens_hash(const int32_t *tokens, int n, int dim, uint32_t seed, float *y, int64_t ldy, void *stream);
+
 /* ggml_soft_max_ext(x, mask, scale, 0.0f): y[m,:] = softmax(x[m,:]*scale + mask[m % mask_rows,:]).
  * mask may be NULL. Rows contiguous, N columns (src/models/smolvla/action_expert.cpp:773). */
 int b2s_soft_max_ext(const float *x, const float *mask, int64_t mask_rows, int64_t M, int64_t N, float scale,

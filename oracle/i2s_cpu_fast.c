@@ -23,7 +23,7 @@
 typedef void (*range_fn)(void *ctx, int64_t begin, int64_t end);
 typedef struct { range_fn fn; void *ctx; int64_t begin, end; } range_job;
 static void *range_thunk(void *p) { range_job *j = (range_job *)p; j->fn(j->ctx, j->begin, j->end); return NULL; }
-static void parallel_for(int64_t n, int nthreads, range_fn fn, void *ctx) {
+void orc_parallel_for(int64_t n, int nthreads, range_fn fn, void *ctx) {
     if (nthreads < 1) nthreads = 1;
     if (nthreads > 256) nthreads = 256;
     if (n < nthreads) nthreads = (int)(n > 0 ? n : 1);
@@ -125,6 +125,7 @@ static void block_dot_scalar(const uint8_t *codes, int nr, const int8_t *q, int 
 typedef struct {
     const uint8_t *Wr; int64_t N, Kp; const int8_t *q; const float *s; const int32_t *sums;
     float ws; int64_t M; float *Y; int isa;
+    const float *tile_scales; int64_t ldy; /* NULL: ws for every row; else row n uses tile_scales[n/128] */
 } gemm_ctx;
 
 static void gemm_range(void *p, int64_t g0, int64_t g1) {
@@ -145,10 +146,11 @@ static void gemm_range(void *p, int64_t g0, int64_t g1) {
             if (c->isa == 2) block_dot_vnni(codes, nr, c->q + m0 * Kp, nt, Kp, raw);
             else if (c->isa == 1) block_dot_avx2(codes, nr, c->q + m0 * Kp, nt, Kp, raw);
             else block_dot_scalar(codes, nr, c->q + m0 * Kp, nt, Kp, raw);
+            const float ws = c->tile_scales ? c->tile_scales[n0 / QK] : c->ws;
             for (int t = 0; t < nt; ++t) {
-                const float rs = c->ws / c->s[m0 + t];
+                const float rs = ws / c->s[m0 + t];
                 for (int r = 0; r < nr; ++r)
-                    c->Y[(m0 + t) * N + n0 + r] = (float)(raw[t * RB + r] - c->sums[m0 + t]) * rs;
+                    c->Y[(m0 + t) * c->ldy + n0 + r] = (float)(raw[t * RB + r] - c->sums[m0 + t]) * rs;
             }
         }
     }
@@ -182,10 +184,22 @@ void orc_fast_mul_mat_i2s(const uint8_t *W, const float *X, int64_t M, int64_t N
     float *s = (float *)malloc(sizeof(float) * (size_t)M);
     int32_t *sums = (int32_t *)malloc(sizeof(int32_t) * (size_t)M);
     actq_ctx ac = {X, K, Kp, q, s, sums};
-    parallel_for(M, nthreads, actq_range, &ac);
-    gemm_ctx gc = {Wr, N, Kp, q, s, sums, ws, M, Y, isa};
-    parallel_for((N + RB - 1) / RB, nthreads, gemm_range, &gc);
+    orc_parallel_for(M, nthreads, actq_range, &ac);
+    gemm_ctx gc = {Wr, N, Kp, q, s, sums, ws, M, Y, isa, NULL, N};
+    orc_parallel_for((N + RB - 1) / RB, nthreads, gemm_range, &gc);
     free(q); free(s); free(sums); free(tmp);
+}
+
+void orc_fast_gemm_q8_rp(const uint8_t *Wr, const float *tile_scales, int64_t N, int64_t K, const int8_t *q,
+                         const float *s, const int32_t *sums, int64_t M, float *Y, int64_t ldy, int nthreads) {
+    gemm_ctx gc = {Wr, N, rup128(K), q, s, sums, 0.0f, M, Y, orc_fast_isa(), tile_scales, ldy};
+    orc_parallel_for((N + RB - 1) / RB, nthreads, gemm_range, &gc);
+}
+
+void orc_fast_act_quant_padded(const float *X, int64_t M, int64_t K, int8_t *q, float *s, int32_t *sums,
+                               int nthreads) {
+    actq_ctx ac = {X, K, rup128(K), q, s, sums};
+    orc_parallel_for(M, nthreads, actq_range, &ac);
 }
 
 typedef struct { const float *x; const float *g; int64_t K; float eps; float *y; } rms_ctx;
@@ -210,13 +224,13 @@ void orc_fast_ffn_block(const float *X, int64_t M, int64_t H, int64_t F,
     float *gt = (float *)malloc(sizeof(float) * (size_t)(M * F));
     float *up = (float *)malloc(sizeof(float) * (size_t)(M * F));
     rms_ctx r1 = {X, g_norm1, H, eps, xn};
-    parallel_for(M, nthreads, rms_range, &r1);
+    orc_parallel_for(M, nthreads, rms_range, &r1);
     orc_fast_mul_mat_i2s(W_gate, xn, M, F, H, gt, nthreads);
     orc_fast_mul_mat_i2s(W_up, xn, M, F, H, up, nthreads);
     sq_ctx sq = {gt, up, F, gt};
-    parallel_for(M, nthreads, sq_range, &sq);
+    orc_parallel_for(M, nthreads, sq_range, &sq);
     rms_ctx r2 = {gt, g_norm2, F, eps, gt};
-    parallel_for(M, nthreads, rms_range, &r2);
+    orc_parallel_for(M, nthreads, rms_range, &r2);
     orc_fast_mul_mat_i2s(W_down, gt, M, H, F, Y, nthreads);
     free(xn); free(gt); free(up);
 }

@@ -190,6 +190,52 @@ void orc_sqrelu_mul(const float *g, const float *u, int64_t n, float *p) {
     }
 }
 
+/* exp by Cody-Waite range reduction (x = n ln2 + r, ln2 split into a 16-bit head and a tail) and the
+ * degree-7 Taylor polynomial of e^r in Horner form with fused multiply-adds, scaled by 2^n; inputs below
+ * -86 give 0, above 88 saturate. The same IEEE operation sequence as the device's det_expf. */
+float orc_det_expf(float x) {
+    if (!(x >= -86.0f)) return 0.0f;
+    if (x > 88.0f) x = 88.0f;
+    const float n = rintf(x * 1.44269502162933349609375f);
+    float r = fmaf(-n, 0.693145751953125f, x);
+    r = fmaf(-n, 1.428606765330187045e-06f, r);
+    float p = 1.98412698412698412698e-04f;
+    p = fmaf(p, r, 1.38888888888888888889e-03f);
+    p = fmaf(p, r, 8.33333333333333333333e-03f);
+    p = fmaf(p, r, 4.16666666666666666667e-02f);
+    p = fmaf(p, r, 1.66666666666666666667e-01f);
+    p = fmaf(p, r, 0.5f);
+    p = fmaf(p, r, 1.0f);
+    p = fmaf(p, r, 1.0f);
+    const uint32_t bits = (uint32_t)((int)n + 127) << 23;
+    float two_n;
+    memcpy(&two_n, &bits, sizeof two_n);
+    return p * two_n;
+}
+
+/* tanh(u) = sign(u) (1 - 2 / (e^{2|u|} + 1)), |u| > 9 -> +-1 (the device's det_tanhf). */
+float orc_det_tanhf(float u) {
+    const float a = fabsf(u);
+    const float t = (a > 9.0f) ? 1.0f : 1.0f - 2.0f / (orc_det_expf(2.0f * a) + 1.0f);
+    return copysignf(t, u);
+}
+
+/* Sum of e[0..n) in the device's warp order: lane l adds e[j], j = l mod 32, for increasing j; then
+ * an xor butterfly over the 32 lane sums (offsets 16, 8, 4, 2, 1); the result is lane 0's value. */
+float orc_warp_order_sum(const float *e, int64_t n) {
+    float lanes[32], nxt[32];
+    for (int l = 0; l < 32; ++l) {
+        float acc = 0.0f;
+        for (int64_t j = l; j < n; j += 32) acc = acc + e[j];
+        lanes[l] = acc;
+    }
+    for (int off = 16; off > 0; off >>= 1) {
+        for (int l = 0; l < 32; ++l) nxt[l] = lanes[l] + lanes[l ^ off];
+        memcpy(lanes, nxt, sizeof lanes);
+    }
+    return lanes[0];
+}
+
 void orc_soft_max_ext(const float *x, const float *mask, int64_t mask_rows, int64_t M, int64_t N,
                       float scale, float *y) {
     float *w = (float *)malloc(sizeof(float) * (size_t)N);
@@ -203,13 +249,9 @@ void orc_soft_max_ext(const float *x, const float *mask, int64_t mask_rows, int6
             w[n] = v;
             if (v > mx) mx = v;
         }
-        double sum = 0.0;
-        for (int64_t n = 0; n < N; ++n) {
-            const float e = (w[n] == -INFINITY) ? 0.0f : expf(w[n] - mx);
-            w[n] = e;
-            sum += (double)e;
-        }
-        const float inv = (float)(1.0 / sum);
+        for (int64_t n = 0; n < N; ++n) w[n] = (w[n] == -INFINITY) ? 0.0f : orc_det_expf(w[n] - mx);
+        const float sum = orc_warp_order_sum(w, N);
+        const float inv = (sum > 0.0f) ? 1.0f / sum : 0.0f;
         for (int64_t n = 0; n < N; ++n) y[m * N + n] = w[n] * inv;
     }
     free(w);

@@ -18,7 +18,9 @@
  *     scale = 1/sqrtf(mean + eps)) followed by ggml_mul with the norm weight, as used at
  *     src/models/smolvla/action_expert.cpp:731-736 and src/models/pi0/vlm.cpp:216.
  *   - Softmax follows ggml_soft_max_ext(x, mask, scale, 0.0f) as used at
- *     src/models/smolvla/action_expert.cpp:773.
+ *     src/models/smolvla/action_expert.cpp:773, with a pinned fp32 evaluation: e = orc_det_expf(l - max)
+ *     (Cody-Waite reduction + degree-7 Taylor polynomial, fused multiply-adds), the sum in the device's
+ *     warp order (orc_warp_order_sum), p = e * (1/sum).
  *
  * i2_s byte layout ("layout v1", flattened over the whole tensor, n = N*K, n % 128 == 0):
  *   weight g = r*K + k (row r, column k) lives in block b = g/128 at position j = g%128;
@@ -87,6 +89,11 @@ void orc_ffn_block(const float *X, int64_t M, int64_t H, int64_t F,
                    const uint8_t *W_gate, const uint8_t *W_up, const uint8_t *W_down,
                    float *Y, float *P_dbg);
 
+/* ---- deterministic fp32 transcendental functions shared with the device kernels ---- */
+float orc_det_expf(float x);
+float orc_det_tanhf(float u);
+float orc_warp_order_sum(const float *e, int64_t n);
+
 /* ---- threaded SIMD variant of the integer path (timed CPU baseline only) ---- */
 /* Same results, bit for bit, as orc_act_quant + orc_gemm_i32 + orc_rescale. */
 void orc_fast_mul_mat_i2s(const uint8_t *W, const float *X, int64_t M, int64_t N, int64_t K, float *Y,
@@ -96,6 +103,15 @@ void orc_fast_ffn_block(const float *X, int64_t M, int64_t H, int64_t F,
                         const uint8_t *W_gate, const uint8_t *W_up, const uint8_t *W_down,
                         float *Y, int nthreads);
 int orc_fast_isa(void); /* 2 = AVX512-VNNI, 1 = AVX2, 0 = scalar */
+/* Y[m][n] (row stride ldy) = (float)(acc - sums[m]) * (ws_n / s[m]) from row-padded codes Wr (Kp/4 bytes
+ * per row) and pre-quantized activations q [M][Kp] (zero-padded past K); ws_n = tile_scales[n/128]. */
+void orc_fast_gemm_q8_rp(const uint8_t *Wr, const float *tile_scales, int64_t N, int64_t K, const int8_t *q,
+                         const float *s, const int32_t *sums, int64_t M, float *Y, int64_t ldy, int nthreads);
+/* orc_act_quant of M rows of K floats into q [M][Kp] (zero-padded), s [M], sums [M]. */
+void orc_fast_act_quant_padded(const float *X, int64_t M, int64_t K, int8_t *q, float *s, int32_t *sums,
+                               int nthreads);
+/* Static parallel-for over [0, n) on nthreads pthreads. */
+void orc_parallel_for(int64_t n, int nthreads, void (*fn)(void *ctx, int64_t begin, int64_t end), void *ctx);
 
 #ifdef __cplusplus
 }

@@ -73,6 +73,28 @@ def lib():
                                          _u8p, _u8p, _u8p, _f32p, C.c_int]
         L.orc_fast_isa.restype = C.c_int
         L.orc_fast_isa.argtypes = []
+        L.orc_bv_param_bits.restype = C.c_uint32
+        L.orc_bv_param_bits.argtypes = [C.c_uint32, C.c_uint32, C.c_uint32]
+        L.orc_bv_ternary_scale.restype = C.c_float
+        L.orc_bv_ternary_scale.argtypes = [C.c_uint32, C.c_uint32, _i64]
+        L.orc_bv_gen_ternary.restype = None
+        L.orc_bv_gen_ternary.argtypes = [_u8p, _i64, _i64, C.c_uint32, C.c_uint32, C.c_int]
+        L.orc_bv_gen_uniform.restype = None
+        L.orc_bv_gen_uniform.argtypes = [_f32p, _i64, C.c_uint32, C.c_uint32, C.c_float, C.c_float]
+        L.orc_layer_norm.restype = None
+        L.orc_layer_norm.argtypes = [_f32p, C.c_void_p, C.c_void_p, _i64, _i64, C.c_float, _f32p]
+        L.orc_gelu_tanh.restype = C.c_float
+        L.orc_gelu_tanh.argtypes = [C.c_float]
+        L.orc_rope_table.restype = None
+        L.orc_rope_table.argtypes = [C.c_float, C.c_int, C.c_int, _f32p]
+        L.orc_rope_neox.restype = None
+        L.orc_rope_neox.argtypes = [_f32p, _i64, C.c_int, C.c_int, _i64, _f32p, C.c_int, C.c_int]
+        L.orc_attention.restype = None
+        L.orc_attention.argtypes = [_f32p, _i64, _i64, _i64, _i64, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
+                                    C.c_int, C.c_float, _f32p, _i64, C.c_int]
+        L.orc_bitvla_forward.restype = C.c_int
+        L.orc_bitvla_forward.argtypes = [C.c_void_p, C.c_uint32, C.c_int, _f32p, C.c_void_p, C.c_void_p,
+                                         C.c_void_p, C.c_int]
         _lib = L
     return _lib
 
@@ -219,3 +241,97 @@ def fast_ffn_block(x, g1, g2, eps, w_gate, w_up, w_down, H, F, nthreads):
 
 def fast_isa() -> int:
     return int(lib().orc_fast_isa())
+
+
+# ------------------------------------------------------------------------------ BitVLA-shape forward
+class BitVLAConfig(C.Structure):
+    """Field-for-field mirror of b2s_bitvla_config (include/b2s_bitvla.h)."""
+    _fields_ = [("image_size", C.c_int), ("patch", C.c_int), ("vit_layers", C.c_int), ("vit_hidden", C.c_int),
+                ("vit_ffn", C.c_int), ("vit_heads", C.c_int), ("vit_eps", C.c_float), ("conn_hidden", C.c_int),
+                ("dec_layers", C.c_int), ("dec_hidden", C.c_int), ("dec_ffn", C.c_int), ("dec_heads", C.c_int),
+                ("dec_kv_heads", C.c_int), ("head_dim", C.c_int), ("rope_theta", C.c_float), ("dec_eps", C.c_float),
+                ("vocab", C.c_int), ("n_text", C.c_int), ("action_chunk", C.c_int), ("action_dim", C.c_int)]
+
+
+def bitvla_config(**over) -> BitVLAConfig:
+    """The BitVLA shape (224px/14 ViT 27x1152/4304/16h, connector 2560, decoder 30x2560/6912, 20/5 heads)."""
+    d = dict(image_size=224, patch=14, vit_layers=27, vit_hidden=1152, vit_ffn=4304, vit_heads=16, vit_eps=1e-6,
+             conn_hidden=2560, dec_layers=30, dec_hidden=2560, dec_ffn=6912, dec_heads=20, dec_kv_heads=5,
+             head_dim=128, rope_theta=500000.0, dec_eps=1e-5, vocab=128256, n_text=32, action_chunk=8,
+             action_dim=7)
+    d.update(over)
+    return BitVLAConfig(**d)
+
+
+def bitvla_seq_len(cfg: BitVLAConfig) -> int:
+    g = cfg.image_size // cfg.patch
+    return g * g + cfg.n_text
+
+
+def bitvla_forward(cfg: BitVLAConfig, seed: int, images: np.ndarray, tokens: np.ndarray, nthreads: int = 0):
+    """(hidden [B*seq, dec_hidden], actions [B, chunk*dim]) of the oracle forward."""
+    images = _c(images, np.float32)
+    tokens = _c(tokens, np.int32)
+    B = images.shape[0]
+    seq = bitvla_seq_len(cfg)
+    hidden = np.zeros((B * seq, cfg.dec_hidden), np.float32)
+    actions = np.zeros((B, cfg.action_chunk * cfg.action_dim), np.float32)
+    nth = nthreads or (os.cpu_count() or 1)
+    rc = lib().orc_bitvla_forward(C.byref(cfg), seed & 0xFFFFFFFF, B, images, tokens.ctypes.data_as(C.c_void_p),
+                                  hidden.ctypes.data_as(C.c_void_p), actions.ctypes.data_as(C.c_void_p), nth)
+    assert rc == 0
+    return hidden, actions
+
+
+def bv_param_bits(seed: int, tensor: int, idx: int) -> int:
+    return int(lib().orc_bv_param_bits(seed & 0xFFFFFFFF, tensor & 0xFFFFFFFF, idx & 0xFFFFFFFF))
+
+
+def bv_ternary_rowpadded(rows: int, K: int, seed: int, tensor: int) -> np.ndarray:
+    Kp = (K + 127) // 128 * 128
+    out = np.zeros(rows * Kp // 4, np.uint8)
+    lib().orc_bv_gen_ternary(out, rows, K, seed, tensor, os.cpu_count() or 1)
+    return out
+
+
+def bv_ternary_scale(seed: int, tensor: int, K: int) -> float:
+    return float(lib().orc_bv_ternary_scale(seed, tensor, K))
+
+
+def layer_norm(x, g, b, eps: float) -> np.ndarray:
+    x = _c(x, np.float32)
+    M, K = x.shape
+    g = None if g is None else _c(g, np.float32)
+    b = None if b is None else _c(b, np.float32)
+    y = np.zeros((M, K), np.float32)
+    lib().orc_layer_norm(x, _ptr(g), _ptr(b), M, K, float(eps), y)
+    return y
+
+
+def gelu_tanh(x: np.ndarray) -> np.ndarray:
+    f = lib().orc_gelu_tanh
+    return np.array([f(float(v)) for v in np.asarray(x, np.float32).reshape(-1)], np.float32).reshape(np.shape(x))
+
+
+def rope_table(base: float, hd: int, n_pos: int) -> np.ndarray:
+    cs = np.zeros((n_pos, hd // 2, 2), np.float32)
+    lib().orc_rope_table(float(base), hd, n_pos, cs)
+    return cs
+
+
+def rope_neox(x: np.ndarray, n_heads: int, hd: int, base: float, pos0: int = 0, period: int = 0) -> np.ndarray:
+    x = _c(x, np.float32).copy()
+    M = x.shape[0]
+    npos = pos0 + (period if period > 0 else M)
+    cs = rope_table(base, hd, npos)
+    lib().orc_rope_neox(x, M, n_heads, hd, x.shape[1], cs, period, pos0)
+    return x
+
+
+def attention(qkv: np.ndarray, q_off: int, k_off: int, v_off: int, batch: int, heads: int, kv_heads: int, hd: int,
+              T: int, causal: bool, scale: float) -> np.ndarray:
+    qkv = _c(qkv, np.float32)
+    o = np.zeros((batch * T, heads * hd), np.float32)
+    lib().orc_attention(qkv, qkv.shape[1], q_off, k_off, v_off, batch, heads, kv_heads, hd, T, int(causal),
+                        float(scale), o, heads * hd, os.cpu_count() or 1)
+    return o

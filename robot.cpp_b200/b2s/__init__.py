@@ -34,6 +34,8 @@ EXPORTED = [
     "b2s_i2s_repack_rows", "b2s_act_quant", "b2s_rms_norm_act_quant", "b2s_mul_mat_workspace_size",
     "b2s_mul_mat", "b2s_mul_mat_q8", "b2s_mul_mat_q8_ex", "b2s_ffn_gate_up_sqrelu_q8",
     "b2s_ffn_block_workspace_size", "b2s_ffn_block", "b2s_soft_max_ext", "b2s_mul_mat_static",
+    "b2s_mul_mat_q8_epi", "b2s_norm", "b2s_norm_act_quant", "b2s_rope_neox", "b2s_attention",
+    "b2s_patch_embed", "b2s_embed_tokens_hash",
 ]
 
 
@@ -83,6 +85,17 @@ def lib():
             "b2s_ffn_block": (C.c_int, [_vp, _i64, _vp, _vp, C.c_float, _TP, _TP, _TP, _vp, _vp, C.c_size_t, _vp]),
             "b2s_soft_max_ext": (C.c_int, [_vp, _vp, _i64, _i64, _i64, C.c_float, _vp, _vp]),
             "b2s_mul_mat_static": (C.c_int, [_TP, _TP, _TP, _vp]),
+            "b2s_mul_mat_q8_epi": (C.c_int, [_TP, _vp, _i64, _vp, _vp, _i64, _vp, _i64, _vp, _vp, _i64, C.c_int,
+                                             _vp]),
+            "b2s_norm": (C.c_int, [_vp, _vp, _vp, _i64, _i64, _i64, C.c_float, C.c_int, _vp, _i64, _vp]),
+            "b2s_norm_act_quant": (C.c_int, [_vp, _vp, _vp, _i64, _i64, _i64, C.c_float, C.c_int, _vp, _i64, _vp,
+                                             _vp, _vp]),
+            "b2s_rope_neox": (C.c_int, [_vp, _i64, C.c_int, C.c_int, _i64, C.c_float, C.c_int, _vp]),
+            "b2s_attention": (C.c_int, [_vp, _i64, _vp, _i64, _vp, _i64, _i64, C.c_int, C.c_int, C.c_int, C.c_float,
+                                        C.c_int, _vp, _i64, _vp]),
+            "b2s_patch_embed": (C.c_int, [_vp, C.c_int, C.c_int, C.c_int, C.c_int, _vp, _vp, _vp, C.c_int, _vp, _i64,
+                                          _vp]),
+            "b2s_embed_tokens_hash": (C.c_int, [_vp, C.c_int, C.c_int, C.c_uint32, _vp, _i64, _vp]),
         }
         for name, (res, args) in sig.items():
             f = getattr(L, name)
@@ -236,3 +249,54 @@ def soft_max_ext(x, mask, scale: float, y, stream=None) -> None:
     M, N = x.shape
     mrows = 1 if mask is None else mask.shape[0]
     check(lib().b2s_soft_max_ext(_ptr(x), _ptr(mask), mrows, M, N, float(scale), _ptr(y), _stream(stream)))
+
+
+def mul_mat_q8_epi(W: Tensor, q, s, sums, y, bias=None, residual=None, act: int = 0, stream=None) -> None:
+    """y = W*q then + bias, GELU (act=1), + residual (residual may be y itself)."""
+    M = q.shape[0]
+    ld_res = residual.stride(0) if residual is not None else 0
+    check(lib().b2s_mul_mat_q8_epi(C.byref(W), _ptr(q), q.stride(0), _ptr(s), _ptr(sums), M, _ptr(y), y.stride(0),
+                                   _ptr(bias), _ptr(residual), ld_res, int(act), _stream(stream)))
+
+
+NORM_RMS = 0
+NORM_LAYER = 1
+
+
+def norm(x, g, b, eps: float, kind: int, y, stream=None) -> None:
+    M, K = x.shape
+    check(lib().b2s_norm(_ptr(x), _ptr(g), _ptr(b), M, K, x.stride(0), float(eps), int(kind), _ptr(y), y.stride(0),
+                         _stream(stream)))
+
+
+def norm_act_quant(x, g, b, eps: float, kind: int, q, s, sums, stream=None) -> None:
+    M, K = x.shape
+    check(lib().b2s_norm_act_quant(_ptr(x), _ptr(g), _ptr(b), M, K, x.stride(0), float(eps), int(kind), _ptr(q),
+                                   q.stride(0), _ptr(s), _ptr(sums), _stream(stream)))
+
+
+def rope_neox(x, n_heads: int, head_dim: int, theta_base: float, pos0: int = 0, stream=None) -> None:
+    M = x.shape[0]
+    check(lib().b2s_rope_neox(_ptr(x), M, int(n_heads), int(head_dim), x.stride(0), float(theta_base), int(pos0),
+                              _stream(stream)))
+
+
+def attention(q, k, v, n_heads: int, n_kv_heads: int, head_dim: int, scale: float, causal: bool, o,
+              stream=None) -> None:
+    M = q.shape[0]
+    check(lib().b2s_attention(_ptr(q), q.stride(0), _ptr(k), k.stride(0), _ptr(v), v.stride(0), M, int(n_heads),
+                              int(n_kv_heads), int(head_dim), float(scale), int(bool(causal)), _ptr(o), o.stride(0),
+                              _stream(stream)))
+
+
+def patch_embed(img, P: int, w, bias, pos, y, stream=None) -> None:
+    C_, H, W = img.shape
+    D = w.shape[0]
+    check(lib().b2s_patch_embed(_ptr(img), C_, H, W, int(P), _ptr(w), _ptr(bias), _ptr(pos), D, _ptr(y), y.stride(0),
+                                _stream(stream)))
+
+
+def embed_tokens_hash(tokens, dim: int, seed: int, y, stream=None) -> None:
+    n = tokens.shape[0]
+    check(lib().b2s_embed_tokens_hash(_ptr(tokens), n, int(dim), int(seed) & 0xFFFFFFFF, _ptr(y), y.stride(0),
+                                      _stream(stream)))

@@ -1,0 +1,125 @@
+"""Python binding of the BitVLA-shape engine in libb2s.so (C ABI in include/b2s_bitvla.h).
+
+A ``Model`` owns a random-init BitVLA-shape network on one GPU (weights generated on the device from a
+seed) and runs whole-observation forwards through the library's CUDA graph. ``predict`` mirrors
+``robotcpp::Model::predict`` (src/models/model.h:65-71): host images and tokens in, host actions out.
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+from . import check, lib as _lib, _ptr, _stream
+
+
+class Config(C.Structure):
+    """Mirror of b2s_bitvla_config."""
+    _fields_ = [("image_size", C.c_int), ("patch", C.c_int), ("vit_layers", C.c_int), ("vit_hidden", C.c_int),
+                ("vit_ffn", C.c_int), ("vit_heads", C.c_int), ("vit_eps", C.c_float), ("conn_hidden", C.c_int),
+                ("dec_layers", C.c_int), ("dec_hidden", C.c_int), ("dec_ffn", C.c_int), ("dec_heads", C.c_int),
+                ("dec_kv_heads", C.c_int), ("head_dim", C.c_int), ("rope_theta", C.c_float), ("dec_eps", C.c_float),
+                ("vocab", C.c_int), ("n_text", C.c_int), ("action_chunk", C.c_int), ("action_dim", C.c_int)]
+
+
+_bound = False
+
+
+def _bind():
+    global _bound
+    L = _lib()
+    if _bound:
+        return L
+    vp, i64 = C.c_void_p, C.c_int64
+    P = C.POINTER(Config)
+    sig = {
+        "b2s_bitvla_default_config": (None, [P]),
+        "b2s_bitvla_seq_len": (C.c_int, [P]),
+        "b2s_bitvla_ternary_ops": (C.c_double, [P]),
+        "b2s_bitvla_param_bits": (C.c_uint32, [C.c_uint32, C.c_uint32, C.c_uint32]),
+        "b2s_bitvla_create": (C.c_int, [P, C.c_uint32, C.c_int, C.POINTER(vp)]),
+        "b2s_bitvla_free": (None, [vp]),
+        "b2s_bitvla_ternary_bytes": (C.c_size_t, [vp]),
+        "b2s_bitvla_weight_bytes": (C.c_size_t, [vp]),
+        "b2s_bitvla_activation_bytes": (C.c_size_t, [vp]),
+        "b2s_bitvla_forward": (C.c_int, [vp, C.c_int, vp, vp, vp, vp, vp]),
+        "b2s_bitvla_predict": (C.c_int, [vp, C.c_int, vp, vp, vp, vp]),
+    }
+    for name, (res, args) in sig.items():
+        f = getattr(L, name)
+        f.restype = res
+        f.argtypes = args
+    _bound = True
+    return L
+
+
+EXPORTED = ["b2s_bitvla_default_config", "b2s_bitvla_seq_len", "b2s_bitvla_ternary_ops", "b2s_bitvla_param_bits",
+            "b2s_bitvla_create", "b2s_bitvla_free", "b2s_bitvla_ternary_bytes", "b2s_bitvla_weight_bytes",
+            "b2s_bitvla_activation_bytes", "b2s_bitvla_forward", "b2s_bitvla_predict"]
+
+
+def default_config(**over) -> Config:
+    c = Config()
+    _bind().b2s_bitvla_default_config(C.byref(c))
+    for k, v in over.items():
+        setattr(c, k, v)
+    return c
+
+
+def seq_len(cfg: Config) -> int:
+    return int(_bind().b2s_bitvla_seq_len(C.byref(cfg)))
+
+
+def ternary_ops(cfg: Config) -> float:
+    return float(_bind().b2s_bitvla_ternary_ops(C.byref(cfg)))
+
+
+def param_bits(seed: int, tensor: int, idx: int) -> int:
+    return int(_bind().b2s_bitvla_param_bits(seed & 0xFFFFFFFF, tensor & 0xFFFFFFFF, idx & 0xFFFFFFFF))
+
+
+class Model:
+    """A BitVLA-shape model on the current CUDA device."""
+
+    def __init__(self, cfg: Config, seed: int, max_batch: int = 1):
+        L = _bind()
+        self.cfg = cfg
+        self.seed = seed
+        self.max_batch = max_batch
+        h = C.c_void_p()
+        check(L.b2s_bitvla_create(C.byref(cfg), seed & 0xFFFFFFFF, max_batch, C.byref(h)))
+        self._h = h
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            _bind().b2s_bitvla_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    @property
+    def seq_len(self) -> int:
+        return seq_len(self.cfg)
+
+    def ternary_bytes(self) -> int:
+        return int(_bind().b2s_bitvla_ternary_bytes(self._h))
+
+    def weight_bytes(self) -> int:
+        return int(_bind().b2s_bitvla_weight_bytes(self._h))
+
+    def activation_bytes(self) -> int:
+        return int(_bind().b2s_bitvla_activation_bytes(self._h))
+
+    def forward(self, images, tokens, hidden=None, actions=None, stream=None) -> None:
+        """Device tensors: images [B,3,S,S] f32, tokens [B,n_text] i32 -> hidden [B*seq, H], actions [B, A]."""
+        B = images.shape[0]
+        check(_bind().b2s_bitvla_forward(self._h, B, _ptr(images), _ptr(tokens), _ptr(hidden), _ptr(actions),
+                                         _stream(stream)))
+
+    def predict(self, images_hwc, tokens, actions, stream=None) -> None:
+        """Host numpy arrays: images [B,S,S,3] uint8, tokens [B,n_text] int32 -> actions [B, A] float32."""
+        B = images_hwc.shape[0]
+        check(_bind().b2s_bitvla_predict(self._h, B, images_hwc.ctypes.data, tokens.ctypes.data,
+                                         actions.ctypes.data, _stream(stream)))

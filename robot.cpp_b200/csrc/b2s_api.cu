@@ -207,7 +207,8 @@ int num_sms_current() {
 }
 
 int run_tc(const b2s::I2sWeight& w0, const b2s::I2sWeight* w1, const int8_t* q, int64_t ldq, const float* s,
-           const int32_t* sums, int64_t M, float* Y, int64_t ldy, int mode, cudaStream_t st) {
+           const int32_t* sums, int64_t M, float* Y, int64_t ldy, int mode, cudaStream_t st,
+           const b2s::Epilogue& epi = b2s::Epilogue{}) {
     if ((reinterpret_cast<uintptr_t>(q) & 15) != 0 || ldq % 16 != 0)
         return fail(B2S_ERR_UNSUPPORTED, "tensor-core path needs 16-byte aligned q with ldq %% 16 == 0");
     if (M > (int64_t)0x7fffffff || w0.N > (int64_t)0x7fffffff) return fail(B2S_ERR_UNSUPPORTED, "size exceeds int32");
@@ -245,24 +246,39 @@ int run_tc(const b2s::I2sWeight& w0, const b2s::I2sWeight* w1, const int8_t* q, 
     a.m_tiles = t.m_tiles;
     a.splits = t.splits;
     a.mode = mode;
+    a.epi = epi;
     return launched(b2s::launch_gemm_i2s_tc(a, st), "gemm_i2s_tc launch");
 }
 
 // path: 0 auto, 1 GEMV, 2 tensor cores
 int mul_mat_q8_impl(const b2s::I2sWeight& w, const int8_t* q, int64_t ldq, const float* s, const int32_t* sums,
-                    int64_t M, float* Y, int64_t ldy, int path, cudaStream_t st) {
+                    int64_t M, float* Y, int64_t ldy, int path, cudaStream_t st,
+                    const b2s::Epilogue& epi = b2s::Epilogue{}) {
     if (M <= 0) return B2S_OK;
     if (path == 0) path = (M <= 16) ? 1 : 2;
     if (path == 1) {
         b2s::Q8Act a{q, s, sums, M, w.K, ldq};
-        return launched(b2s::launch_gemv_i2s(w, a, Y, ldy, st), "gemv_i2s launch");
+        return launched(b2s::launch_gemv_i2s(w, a, Y, ldy, epi, st), "gemv_i2s launch");
     }
-    return run_tc(w, nullptr, q, ldq, s, sums, M, Y, ldy, 0, st);
+    return run_tc(w, nullptr, q, ldq, s, sums, M, Y, ldy, 0, st, epi);
 }
 
 }  // namespace
 
 namespace b2s {
+
+int dispatch_mul_mat_q8(const I2sWeight& w, const int8_t* q, int64_t ldq, const float* s, const int32_t* sums,
+                        int64_t M, float* y, int64_t ldy, int path, const Epilogue& epi, cudaStream_t st) {
+    if (epi.scale_rows < 0 || (epi.scale_rows % 128 != 0 && path != 1))
+        return fail(B2S_ERR_UNSUPPORTED, "stacked weight scales need scale_rows %% 128 == 0");
+    return mul_mat_q8_impl(w, q, ldq, s, sums, M, y, ldy, path, st, epi);
+}
+
+int dispatch_gate_up(const I2sWeight& wg, const I2sWeight& wu, const int8_t* q, int64_t ldq, const float* s,
+                     const int32_t* sums, int64_t M, float* p, int64_t ldp, cudaStream_t st) {
+    if (M <= 0) return B2S_OK;
+    return run_tc(wg, &wu, q, ldq, s, sums, M, p, ldp, 1, st);
+}
 
 int set_last_error(int code, const char* msg) { return fail(code, "%s", msg); }
 
@@ -441,6 +457,21 @@ int b2s_mul_mat_q8(const b2s_tensor* W, const int8_t* q, int64_t ldq, const floa
     return b2s_mul_mat_q8_ex(W, q, ldq, s, sums, M, Y, ldy, 0, stream);
 }
 
+int b2s_mul_mat_q8_epi(const b2s_tensor* W, const int8_t* q, int64_t ldq, const float* s, const int32_t* sums,
+                       int64_t M, float* Y, int64_t ldy, const float* bias, const float* residual, int64_t ld_res,
+                       int act, void* stream) {
+    int rc = check_device();
+    if (rc) return rc;
+    b2s::I2sWeight w;
+    if ((rc = weight_view(W, &w, "W"))) return rc;
+    if (!q || !s || !sums || !Y) return fail(B2S_ERR_INVALID_ARG, "mul_mat_q8_epi: q, s, sums and Y must be non-NULL");
+    if (M < 0 || ldq < w.K || ldy < w.N) return fail(B2S_ERR_INVALID_ARG, "mul_mat_q8_epi: bad M/ldq/ldy");
+    if (act != 0 && act != 1) return fail(B2S_ERR_INVALID_ARG, "mul_mat_q8_epi: act must be 0 (none) or 1 (gelu)");
+    if (residual && ld_res < w.N) return fail(B2S_ERR_INVALID_ARG, "mul_mat_q8_epi: ld_res < N");
+    b2s::Epilogue epi{bias, residual, ld_res, act};
+    return mul_mat_q8_impl(w, q, ldq, s, sums, M, Y, ldy, 0, static_cast<cudaStream_t>(stream), epi);
+}
+
 int b2s_mul_mat(const b2s_tensor* W, const b2s_tensor* X, b2s_tensor* Y, void* workspace, size_t workspace_bytes,
                 void* stream) {
     int rc = check_device();
@@ -533,6 +564,80 @@ int b2s_ffn_block(const float* X, int64_t M, const float* g1, const float* g2, f
     if ((rc = launched(b2s::launch_act_quant(P, F, g2, true, eps, M, F, q2, l2.ldq, s2, u2, st), "rms_norm_act_quant 2")))
         return rc;
     return mul_mat_q8_impl(wd, q2, l2.ldq, s2, u2, M, Y, H, 0, st);
+}
+
+int b2s_norm(const float* x, const float* g, const float* b, int64_t M, int64_t K, int64_t ldx, float eps, int kind,
+             float* y, int64_t ldy, void* stream) {
+    int rc = check_device();
+    if (rc) return rc;
+    if (!x || !y) return fail(B2S_ERR_INVALID_ARG, "norm: x and y must be non-NULL");
+    if (kind != 0 && kind != 1) return fail(B2S_ERR_INVALID_ARG, "norm: kind must be 0 (RMSNorm) or 1 (LayerNorm)");
+    if (M < 0 || K <= 0 || ldx < K || ldy < K || K > 0x7fffffff) return fail(B2S_ERR_INVALID_ARG, "norm: bad shape");
+    return launched(b2s::launch_norm(kind, false, x, ldx, g, b, eps, M, K, y, ldy, nullptr, 0, nullptr, nullptr,
+                                     static_cast<cudaStream_t>(stream)),
+                    "norm launch");
+}
+
+int b2s_norm_act_quant(const float* x, const float* g, const float* b, int64_t M, int64_t K, int64_t ldx, float eps,
+                       int kind, int8_t* q, int64_t ldq, float* s, int32_t* sums, void* stream) {
+    int rc = check_device();
+    if (rc) return rc;
+    if (!x || !q || !s) return fail(B2S_ERR_INVALID_ARG, "norm_act_quant: x, q and s must be non-NULL");
+    if (kind != 0 && kind != 1) return fail(B2S_ERR_INVALID_ARG, "norm_act_quant: kind must be 0 or 1");
+    if (M < 0 || K <= 0 || ldx < K || ldq < K || K > 0x7fffffff) return fail(B2S_ERR_INVALID_ARG, "norm_act_quant: bad shape");
+    return launched(b2s::launch_norm(kind, true, x, ldx, g, b, eps, M, K, nullptr, 0, q, ldq, s, sums,
+                                     static_cast<cudaStream_t>(stream)),
+                    "norm_act_quant launch");
+}
+
+int b2s_rope_neox(float* x, int64_t M, int n_heads, int head_dim, int64_t ld, float theta_base, int pos0,
+                  void* stream) {
+    int rc = check_device();
+    if (rc) return rc;
+    if (!x || M < 0 || n_heads <= 0 || head_dim <= 0 || (head_dim & 1) || ld < (int64_t)n_heads * head_dim)
+        return fail(B2S_ERR_INVALID_ARG, "rope_neox: bad arguments");
+    return launched(b2s::launch_rope_neox(x, M, n_heads, head_dim, ld, theta_base, pos0, static_cast<cudaStream_t>(stream)),
+                    "rope launch");
+}
+
+int b2s_attention(const float* q, int64_t ldq, const float* k, int64_t ldk, const float* v, int64_t ldv, int64_t M,
+                  int n_heads, int n_kv_heads, int head_dim, float scale, int causal, float* o, int64_t ldo,
+                  void* stream) {
+    int rc = check_device();
+    if (rc) return rc;
+    if (!q || !k || !v || !o) return fail(B2S_ERR_INVALID_ARG, "attention: NULL tensor");
+    if (M <= 0 || M > 65536 || n_heads <= 0 || n_kv_heads <= 0 || n_heads % n_kv_heads || head_dim <= 0)
+        return fail(B2S_ERR_INVALID_ARG, "attention: bad shape");
+    if (ldq < (int64_t)n_heads * head_dim || ldo < (int64_t)n_heads * head_dim || ldk < (int64_t)n_kv_heads * head_dim ||
+        ldv < (int64_t)n_kv_heads * head_dim)
+        return fail(B2S_ERR_INVALID_ARG, "attention: leading dimensions too small");
+    if (!b2s::attention_supported((int)M, head_dim, ldq, ldk, ldv, ldo, q, k, v, o))
+        return fail(B2S_ERR_UNSUPPORTED,
+                    "attention: needs head_dim %% 8 == 0 and <= 128, leading dimensions %% 4 == 0, 16-byte aligned "
+                    "tensors and (64 + roundup(M,64) + 4) x 256 + 512 x head_dim bytes of shared memory <= 227 KB");
+    return launched(b2s::launch_attention(q, ldq, k, ldk, v, ldv, 1, (int)M, n_heads, n_kv_heads, head_dim, scale,
+                                          causal != 0, o, ldo, static_cast<cudaStream_t>(stream)),
+                    "attention");
+}
+
+int b2s_patch_embed(const float* img, int C, int H, int W, int P, const float* w, const float* bias, const float* pos,
+                    int D, float* y, int64_t ldy, void* stream) {
+    int rc = check_device();
+    if (rc) return rc;
+    if (!img || !w || !y || C <= 0 || P <= 0 || H % P || W % P || D <= 0 || ldy < D)
+        return fail(B2S_ERR_INVALID_ARG, "patch_embed: bad arguments");
+    return launched(b2s::launch_patch_embed(img, 1, C, H, W, P, w, bias, pos, D, y, ldy,
+                                            static_cast<cudaStream_t>(stream)),
+                    "patch_embed");
+}
+
+int b2s_embed_tokens_hash(const int32_t* tokens, int n, int dim, uint32_t seed, float* y, int64_t ldy, void* stream) {
+    int rc = check_device();
+    if (rc) return rc;
+    if (!tokens || !y || n < 0 || dim <= 0 || ldy < dim) return fail(B2S_ERR_INVALID_ARG, "embed_tokens: bad arguments");
+    if (n == 0) return B2S_OK;
+    return launched(b2s::launch_embed_tokens(tokens, n, dim, seed, y, ldy, static_cast<cudaStream_t>(stream)),
+                    "embed_tokens launch");
 }
 
 int b2s_soft_max_ext(const float* x, const float* mask, int64_t mask_rows, int64_t M, int64_t N, float scale, float* y,

@@ -55,6 +55,35 @@ __device__ __forceinline__ float warp_sum_f(float v) {
     return v;
 }
 
+// ---------------------------------------------------------------- deterministic transcendental functions
+// exp and tanh of the library's fp32 kernels, built from IEEE operations only (fused multiply-adds,
+// products, one division) so that the CPU oracle reproduces them bit for bit: Cody and Waite's range
+// reduction x = n ln2 + r (|r| <= ln2/2, ln2 split into a 16-bit head and a tail) and the degree-7
+// Taylor polynomial of e^r in Horner form, scaled by 2^n. Relative error below 2 ulp; inputs below
+// -86 return 0 (no subnormal results), above 88 saturate at e^88.
+__device__ __forceinline__ float det_expf(float x) {
+    if (!(x >= -86.0f)) return 0.0f;  // also NaN -> 0
+    x = fminf(x, 88.0f);
+    const float n = rintf(__fmul_rn(x, 1.44269502162933349609375f));
+    float r = __fmaf_rn(-n, 0.693145751953125f, x);
+    r = __fmaf_rn(-n, 1.428606765330187045e-06f, r);
+    float p = 1.98412698412698412698e-04f;
+    p = __fmaf_rn(p, r, 1.38888888888888888889e-03f);
+    p = __fmaf_rn(p, r, 8.33333333333333333333e-03f);
+    p = __fmaf_rn(p, r, 4.16666666666666666667e-02f);
+    p = __fmaf_rn(p, r, 1.66666666666666666667e-01f);
+    p = __fmaf_rn(p, r, 0.5f);
+    p = __fmaf_rn(p, r, 1.0f);
+    p = __fmaf_rn(p, r, 1.0f);
+    return __fmul_rn(p, __int_as_float(((int)n + 127) << 23));
+}
+// tanh(u) = sign(u) (1 - 2 / (e^{2|u|} + 1)); |u| > 9 gives +-1.
+__device__ __forceinline__ float det_tanhf(float u) {
+    const float a = fabsf(u);
+    const float t = (a > 9.0f) ? 1.0f : __fsub_rn(1.0f, __fdiv_rn(2.0f, __fadd_rn(det_expf(__fmul_rn(2.0f, a)), 1.0f)));
+    return copysignf(t, u);
+}
+
 // ---------------------------------------------------------------- programmatic dependent launch
 // griddep_wait(): block until the preceding kernel in the stream (launched before this one with
 // programmatic stream serialization allowed) has completed and its memory is visible; a no-op otherwise.
@@ -222,6 +251,21 @@ __host__ __device__ constexpr uint32_t umma_idesc_i8(int M, int N) {
            | (1u << 10)                       // B: signed 8-bit
            | ((uint32_t)(N >> 3) << 17)       // N / 8
            | ((uint32_t)(M >> 4) << 24);      // M / 16
+}
+
+// Parameter generator of the random-init models: 32 hash bits of element idx of tensor `tensor`
+// (murmur3's 32-bit finalizer applied to the seed, the tensor id and the index).
+__host__ __device__ __forceinline__ uint32_t param_mix(uint32_t h) {
+    h ^= h >> 16;
+    h *= 0x85EBCA6Bu;
+    h ^= h >> 13;
+    h *= 0xC2B2AE35u;
+    h ^= h >> 16;
+    return h;
+}
+__host__ __device__ __forceinline__ uint32_t param_bits(uint32_t seed, uint32_t tensor, uint32_t idx) {
+    const uint32_t t = param_mix(seed ^ param_mix(tensor * 0x9E3779B1u + 0x7F4A7C15u));
+    return param_mix(t ^ (idx * 0x85EBCA77u + 0x165667B1u));
 }
 
 }  // namespace b2s

@@ -5,6 +5,8 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include "b2s_common.cuh"
+
 namespace b2s {
 
 // Weight operand as the kernels see it: row-padded i2_s bytes (row stride Kp/4, Kp = roundup(K,128)),
@@ -26,9 +28,32 @@ struct Q8Act {
 cudaError_t launch_act_quant(const float* x, int64_t ldx, const float* g, bool norm, float eps, int64_t M, int64_t K,
                              int8_t* q, int64_t ldq, float* s, int32_t* sums, cudaStream_t st);
 
-cudaError_t launch_gemv_i2s(const I2sWeight& w, const Q8Act& a, float* y, int64_t ldy, cudaStream_t st);
+// Optional epilogue of the plain GEMM (mode 0 of the tensor-core path and the GEMV), applied in this
+// order to v = (float)acc * (w_scale / s[m]):  v += bias[n];  v = gelu_tanh(v) if act == 1;
+// v = residual[m * ld_res + n] + v.
+// scale_rows > 0 makes the weight scale an array: output row n uses w_scale[n / scale_rows] (several
+// ternary tensors stacked row-wise into one weight, e.g. fused q/k/v, each keeping its own scale;
+// a multiple of 128 on the tensor-core path).
+struct Epilogue {
+    const float* bias;      // [N] or nullptr
+    const float* residual;  // [M x ld_res] or nullptr (may alias the output)
+    int64_t ld_res;
+    int act;                // 0 none, 1 GELU (tanh approximation)
+    int scale_rows;         // 0: one per-tensor scale
+};
 
-// Tensor-core path. mode 0: Y = W*q. mode 1 (gate/up): P = relu(Wg*q)^2 * (Wu*q).
+// GELU, tanh approximation: 0.5 x (1 + tanh(sqrt(2/pi) x (1 + 0.044715 x^2))), fp32 ops in this order,
+// tanh = det_tanhf (b2s_common.cuh).
+__device__ __forceinline__ float gelu_tanh(float x) {
+    const float inner = __fmul_rn(__fmul_rn(0.79788456080286535588f, x),
+                                  __fadd_rn(1.0f, __fmul_rn(__fmul_rn(0.044715f, x), x)));
+    return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, det_tanhf(inner)));
+}
+
+cudaError_t launch_gemv_i2s(const I2sWeight& w, const Q8Act& a, float* y, int64_t ldy, const Epilogue& epi,
+                            cudaStream_t st);
+
+// Tensor-core path. mode 0: Y = W*q (+ epilogue). mode 1 (gate/up): P = relu(Wg*q)^2 * (Wu*q).
 // tmap_* are built by the caller (host) for these exact buffers.
 struct TcGemmArgs {
     CUtensorMap tmap_w0;  // packed codes of W (or W_gate), 2D u8 [N rows][Kp/4 bytes], box 32 x 128 (64 in mode 1)
@@ -46,6 +71,7 @@ struct TcGemmArgs {
     int nsub;             // 1 or 2 sub-tiles
     int n_tiles, m_tiles, splits;  // grid; splits = K-split CTAs per cluster (1..8)
     int mode;
+    Epilogue epi;
 };
 cudaError_t launch_gemm_i2s_tc(const TcGemmArgs& args, cudaStream_t st);
 
@@ -53,6 +79,37 @@ cudaError_t launch_repack_rows(const uint8_t* src, uint8_t* dst, int64_t N, int6
 
 cudaError_t launch_softmax(const float* x, const float* mask, int64_t mask_rows, int64_t M, int64_t N, float scale,
                            float* y, cudaStream_t st);
+cudaError_t launch_softmax_rows(const float* x, const float* mask, int64_t mask_rows, int64_t M, int64_t N,
+                                float scale, int causal_rows, float* y, cudaStream_t st);
+
+// Model operators (model_ops.cu). kind 0 = RMSNorm, 1 = LayerNorm; quant writes int8 codes + s + sums.
+cudaError_t launch_norm(int kind, bool quant, const float* x, int64_t ldx, const float* g, const float* b, float eps,
+                        int64_t M, int64_t K, float* y, int64_t ldy, int8_t* q, int64_t ldq, float* s, int32_t* sums,
+                        cudaStream_t st);
+cudaError_t launch_rope_neox(float* x, int64_t M, int n_heads, int hd, int64_t ld, float base, int pos0,
+                             cudaStream_t st);
+cudaError_t launch_rope_table(float base, int hd, int n_pos, float2* tab, cudaStream_t st);
+cudaError_t launch_rope_apply(float* x, int64_t M, int n_heads, int hd, int64_t ld, const float2* tab, int period,
+                              cudaStream_t st);
+cudaError_t launch_embed_tokens(const int32_t* tokens, int n, int D, uint32_t seed, float* y, int64_t ldy,
+                                cudaStream_t st);
+cudaError_t launch_patch_embed(const float* img, int batch, int C, int H, int W, int P, const float* w,
+                               const float* bias, const float* pos, int D, float* y, int64_t ldy, cudaStream_t st);
+// Fused fp32 attention of `batch` sequences of T tokens (operation order in model_ops.cu).
+size_t attention_smem_bytes(int T, int hd);
+bool attention_supported(int T, int hd, int64_t ldq, int64_t ldk, int64_t ldv, int64_t ldo, const void* q,
+                         const void* k, const void* v, const void* o);
+cudaError_t launch_attention(const float* q, int64_t ldq, const float* k, int64_t ldk, const float* v, int64_t ldv,
+                             int batch, int T, int heads, int kv_heads, int hd, float scale, bool causal, float* o,
+                             int64_t ldo, cudaStream_t st);
+
+// The library's mul_mat dispatch (b2s status codes; failures recorded for b2s_last_error()).
+// path 0 = auto (M <= 16: GEMV, else tensor cores), 1 = GEMV, 2 = tensor cores.
+int dispatch_mul_mat_q8(const I2sWeight& w, const int8_t* q, int64_t ldq, const float* s, const int32_t* sums,
+                        int64_t M, float* y, int64_t ldy, int path, const Epilogue& epi, cudaStream_t st);
+// FFN gate/up with the squared-ReLU product: p = relu(Wg q)^2 * (Wu q) (tensor cores, mode 1).
+int dispatch_gate_up(const I2sWeight& wg, const I2sWeight& wu, const int8_t* q, int64_t ldq, const float* s,
+                     const int32_t* sums, int64_t M, float* p, int64_t ldp, cudaStream_t st);
 
 // Records `msg` as the calling thread's b2s_last_error() and returns `code`.
 int set_last_error(int code, const char* msg);

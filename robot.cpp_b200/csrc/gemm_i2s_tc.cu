@@ -130,8 +130,8 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
 gemm_i2s_tc_kernel(const __grid_constant__ CUtensorMap tmap_w0, const __grid_constant__ CUtensorMap tmap_w1,
                    const __grid_constant__ CUtensorMap tmap_q, const float* __restrict__ w0_scale,
                    const float* __restrict__ w1_scale, const float* __restrict__ s_act,
-                   const int32_t* __restrict__ sum_act, float* __restrict__ y, int64_t ldy, int M, int N, int Kp,
-                   int T, int bn_sub, int nsub, int mode) {
+                   const int32_t* __restrict__ sum_act, float* y, int64_t ldy, int M, int N, int Kp,
+                   int T, int bn_sub, int nsub, int mode, const Epilogue epi) {
     using namespace tc;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -202,7 +202,7 @@ gemm_i2s_tc_kernel(const __grid_constant__ CUtensorMap tmap_w0, const __grid_con
         const int tid = threadIdx.x - 192;
         for (int i = tid; i < nmat * T; i += 128) {
             const int j = i / T, t = i - j * T, m = m0 + t;
-            const float ws = __ldg(j == 0 ? w0_scale : w1_scale);
+            const float ws = __ldg(j == 0 ? w0_scale + (epi.scale_rows ? nb / epi.scale_rows : 0) : w1_scale);
             rfac[j * kMaxT + t] = (m < M) ? __fdiv_rn(ws, s_act[m]) : 0.0f;
         }
         for (int t = tid; t < T; t += 128) sumq[t] = (m0 + t < M) ? sum_act[m0 + t] : 0;
@@ -326,7 +326,7 @@ gemm_i2s_tc_kernel(const __grid_constant__ CUtensorMap tmap_w0, const __grid_con
     // w % 4, so each quadrant has one warp per group; the groups take alternate token chunk pairs.
     const bool split = S > 1;
     const int nchunk = T / 16;
-    const bool epi = (warp < 4) || (warp >= 6);
+    const bool is_epi = (warp < 4) || (warp >= 6);
     const int egrp = (warp < 4) ? 0 : 1;
     const int q = warp & 3;                                                  // TMEM lane quadrant
     const int row = 32 * q + lane;                                           // TMEM lane
@@ -353,7 +353,7 @@ gemm_i2s_tc_kernel(const __grid_constant__ CUtensorMap tmap_w0, const __grid_con
 
     if (split) {
         __syncthreads();  // every role has left the main loop: the rings are free; rfac/sumq are ready
-        if (epi) {
+        if (is_epi) {
             const bool good = __all_sync(0xffffffffu, *abort_flag == 0);
             for (int ch = 2 * egrp; ch < nchunk; ch += 4) {
                 int32_t ra[16], rb[16];
@@ -369,23 +369,40 @@ gemm_i2s_tc_kernel(const __grid_constant__ CUtensorMap tmap_w0, const __grid_con
             }
         }
         cluster_sync_all();
-    } else if (epi) {
+    } else if (is_epi) {
         named_bar_sync(2, 256);  // group 1's rfac/sumq are visible to group 0
     }
 
-    if (epi) {
+    if (is_epi) {
         const bool good = __all_sync(0xffffffffu, *abort_flag == 0);
         const int gu = (mode == 1) ? (lane >> 4) : 0;                     // 0 gate / 1 up lane (mode 1)
         const int n = (mode == 1) ? nb + 16 * q + (lane & 15) : nb + row;  // output column
 
-        auto finish = [&](int ch, const int32_t (&raw)[16]) {
+        // Mode 0: the bias of this thread's output column is loaded once; residual values are fetched
+        // for a whole chunk pair before the pair's accumulators are read (load_res), so their latency
+        // is paid once per pair and overlaps the TMEM loads, not once per output.
+        const float bias_n = (mode == 0 && epi.bias && n < N) ? epi.bias[n] : 0.0f;
+        auto load_res = [&](int ch, float (&r)[16]) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+                const int m = m0 + ch * 16 + j;
+                r[j] = (epi.residual && ch < nchunk && m < M && n < N) ? epi.residual[(int64_t)m * epi.ld_res + n]
+                                                                        : 0.0f;
+            }
+        };
+        auto finish = [&](int ch, const int32_t (&raw)[16], const float (&res)[16]) {
             const int t0 = ch * 16;
             if (mode == 0) {
 #pragma unroll
                 for (int j = 0; j < 16; ++j) {
                     const int t = t0 + j, m = m0 + t;
-                    const float v = __fmul_rn((float)(raw[j] - sumq[t]), rfac[t]);
-                    if (good && m < M && n < N) y[(int64_t)m * ldy + n] = v;
+                    float v = __fmul_rn((float)(raw[j] - sumq[t]), rfac[t]);
+                    if (good && m < M && n < N) {
+                        if (epi.bias) v = __fadd_rn(v, bias_n);
+                        if (epi.act == 1) v = gelu_tanh(v);
+                        if (epi.residual) v = __fadd_rn(res[j], v);
+                        y[(int64_t)m * ldy + n] = v;
+                    }
                 }
             } else {
                 float p[16];
@@ -414,6 +431,8 @@ gemm_i2s_tc_kernel(const __grid_constant__ CUtensorMap tmap_w0, const __grid_con
             for (int ch = rank; ch < nchunk; ch += S, ++i) {
                 if ((i & 1) != egrp) continue;
                 int32_t raw[16];
+                float res[16];
+                load_res(ch, res);
 #pragma unroll
                 for (int j = 0; j < 16; ++j) raw[j] = 0;
                 const uint32_t addr = smem_u32(part + (ch * 16) * 128 + row);
@@ -424,15 +443,18 @@ gemm_i2s_tc_kernel(const __grid_constant__ CUtensorMap tmap_w0, const __grid_con
 #pragma unroll
                     for (int j = 0; j < 16; ++j) raw[j] += (good ? a[j] : 0) + ((good && r + 1 < S) ? b[j] : 0);
                 }
-                finish(ch, raw);
+                finish(ch, raw, res);
             }
         } else {
             for (int ch = 2 * egrp; ch < nchunk; ch += 4) {
                 int32_t ra[16], rb[16];
+                float sa[16], sb[16];
                 const bool hb = ch + 1 < nchunk;
+                load_res(ch, sa);
+                load_res(ch + 1, sb);
                 load_pair(ch, hb, good, ra, rb);
-                finish(ch, ra);
-                if (hb) finish(ch + 1, rb);
+                finish(ch, ra, sa);
+                if (hb) finish(ch + 1, rb, sb);
             }
         }
     }
@@ -469,7 +491,7 @@ cudaError_t launch_gemm_i2s_tc(const TcGemmArgs& a, cudaStream_t st) {
     cfg.attrs = attr;
     cfg.numAttrs = 2;
     return cudaLaunchKernelEx(&cfg, gemm_i2s_tc_kernel, a.tmap_w0, a.tmap_w1, a.tmap_q, a.w0_scale, a.w1_scale, a.s,
-                              a.sums, a.y, a.ldy, a.M, a.N, a.Kp, a.T, a.bn_sub, a.nsub, a.mode);
+                              a.sums, a.y, a.ldy, a.M, a.N, a.Kp, a.T, a.bn_sub, a.nsub, a.mode, a.epi);
 }
 
 }  // namespace b2s

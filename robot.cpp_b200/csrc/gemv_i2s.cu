@@ -42,7 +42,7 @@ template <int MT>
 __global__ void __launch_bounds__(kGemvWarps * 32)
 gemv_i2s_kernel(const uint8_t* __restrict__ codes, const float* __restrict__ wscale, int N, int Kp,
                 const int8_t* __restrict__ q, int64_t ldq, int K, int mrows, const float* __restrict__ s,
-                const int32_t* __restrict__ sums, float* __restrict__ y, int64_t ldy) {
+                const int32_t* __restrict__ sums, float* y, int64_t ldy, const Epilogue epi) {
     extern __shared__ __align__(16) uint8_t q_sm[];  // MT x Kp int8, zero beyond K and beyond mrows
     __shared__ int red[kGemvWarps][kGemvRows][MT];
 
@@ -136,15 +136,19 @@ gemv_i2s_kernel(const uint8_t* __restrict__ codes, const float* __restrict__ wsc
             int tot = 0;
 #pragma unroll
             for (int w = 0; w < kGemvWarps; ++w) tot += red[w][rr][m];
-            const float rs = __fdiv_rn(__ldg(wscale), s[m]);
-            y[(int64_t)m * ldy + n] = __fmul_rn((float)(tot - sums[m]), rs);
+            const float rs = __fdiv_rn(__ldg(wscale + (epi.scale_rows ? n / epi.scale_rows : 0)), s[m]);
+            float v = __fmul_rn((float)(tot - sums[m]), rs);
+            if (epi.bias) v = __fadd_rn(v, epi.bias[n]);
+            if (epi.act == 1) v = gelu_tanh(v);
+            if (epi.residual) v = __fadd_rn(epi.residual[(int64_t)m * epi.ld_res + n], v);
+            y[(int64_t)m * ldy + n] = v;
         }
     }
 }
 
 template <int MT>
 static cudaError_t launch_mt(const I2sWeight& w, const int8_t* q, int64_t ldq, int mrows, const float* s,
-                             const int32_t* sums, float* y, int64_t ldy, cudaStream_t st) {
+                             const int32_t* sums, float* y, int64_t ldy, const Epilogue& epi, cudaStream_t st) {
     const size_t smem = (size_t)MT * (size_t)w.Kp;
     auto kfn = gemv_i2s_kernel<MT>;
     // Dynamic + static shared memory above 48 KB needs the opt-in attribute (raised once per size).
@@ -165,10 +169,11 @@ static cudaError_t launch_mt(const I2sWeight& w, const int8_t* q, int64_t ldq, i
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     return cudaLaunchKernelEx(&cfg, kfn, w.codes, w.scale, (int)w.N, (int)w.Kp, q, ldq, (int)w.K, mrows, s, sums, y,
-                              ldy);
+                              ldy, epi);
 }
 
-cudaError_t launch_gemv_i2s(const I2sWeight& w, const Q8Act& a, float* y, int64_t ldy, cudaStream_t st) {
+cudaError_t launch_gemv_i2s(const I2sWeight& w, const Q8Act& a, float* y, int64_t ldy, const Epilogue& epi,
+                            cudaStream_t st) {
     // Token groups of up to 16, each one pass over the weights; a group of m tokens runs the smallest
     // power-of-two variant >= m with the extra token rows zero.
     for (int64_t m0 = 0; m0 < a.M; m0 += 16) {
@@ -177,12 +182,14 @@ cudaError_t launch_gemv_i2s(const I2sWeight& w, const Q8Act& a, float* y, int64_
         const float* s = a.s + m0;
         const int32_t* sums = a.sums + m0;
         float* yy = y + m0 * ldy;
+        Epilogue ep = epi;  // the residual rows move with the token group
+        if (ep.residual) ep.residual += m0 * ep.ld_res;
         cudaError_t e;
-        if (mt == 1) e = launch_mt<1>(w, q, a.ldq, mt, s, sums, yy, ldy, st);
-        else if (mt == 2) e = launch_mt<2>(w, q, a.ldq, mt, s, sums, yy, ldy, st);
-        else if (mt <= 4) e = launch_mt<4>(w, q, a.ldq, mt, s, sums, yy, ldy, st);
-        else if (mt <= 8) e = launch_mt<8>(w, q, a.ldq, mt, s, sums, yy, ldy, st);
-        else e = launch_mt<16>(w, q, a.ldq, mt, s, sums, yy, ldy, st);
+        if (mt == 1) e = launch_mt<1>(w, q, a.ldq, mt, s, sums, yy, ldy, ep, st);
+        else if (mt == 2) e = launch_mt<2>(w, q, a.ldq, mt, s, sums, yy, ldy, ep, st);
+        else if (mt <= 4) e = launch_mt<4>(w, q, a.ldq, mt, s, sums, yy, ldy, ep, st);
+        else if (mt <= 8) e = launch_mt<8>(w, q, a.ldq, mt, s, sums, yy, ldy, ep, st);
+        else e = launch_mt<16>(w, q, a.ldq, mt, s, sums, yy, ldy, ep, st);
         if (e != cudaSuccess) return e;
     }
     return cudaGetLastError();

@@ -10,21 +10,25 @@ __device__ unsigned int g_device_error = 0;
 // y[m,:] = softmax(x[m,:] * scale + mask[m % mask_rows, :]), one warp per row.
 // Mirrors ggml_soft_max_ext(ctx, kq, mask, scale, 0.0f) as called at
 // src/models/smolvla/action_expert.cpp:773 and ggml_soft_max_inplace at src/models/smolvla/vision.cpp:328
-// (scale 1, no mask). Rows up to 32*kSmRegs elements stay in registers (one HBM read); longer rows
-// take a second pass that hits L1/L2. Masked -inf entries give exact zeros.
+// (scale 1, no mask). With causal_rows > 0, row r is query position r % causal_rows and the keys after
+// it are masked (the decoder's causal mask without a mask tensor). Rows up to 32*kSmRegs elements stay
+// in registers (one HBM read); longer rows take a second pass that hits L1/L2. Masked -inf entries give
+// exact zeros.
 constexpr int kSmWarps = 8;
 constexpr int kSmRegs = 16;  // elements per lane kept in registers (rows <= 512)
 
 __global__ void __launch_bounds__(kSmWarps * 32)
 softmax_kernel(const float* __restrict__ x, const float* __restrict__ mask, int64_t mask_rows, int64_t M, int N,
-               float scale, float* __restrict__ y) {
+               float scale, int causal_rows, float* __restrict__ y) {
     const int lane = threadIdx.x & 31;
     const int64_t row = (int64_t)blockIdx.x * kSmWarps + (threadIdx.x >> 5);
     if (row >= M) return;
     const float* xr = x + row * N;
     const float* mr = mask ? mask + (row % mask_rows) * N : nullptr;
+    const int qpos = causal_rows > 0 ? (int)(row % causal_rows) : N;  // keys after the query are masked
     float* yr = y + row * N;
     auto logit = [&](int i) -> float {
+        if (i > qpos) return -INFINITY;
         float v = __fmul_rn(xr[i], scale);
         if (mr) v = __fadd_rn(v, mr[i]);
         return v;
@@ -47,37 +51,43 @@ softmax_kernel(const float* __restrict__ x, const float* __restrict__ mask, int6
     if (in_regs) {
 #pragma unroll
         for (int j = 0; j < kSmRegs; ++j) {
-            const float e = (reg[j] == -INFINITY) ? 0.0f : expf(reg[j] - mx);
+            const float e = (reg[j] == -INFINITY) ? 0.0f : det_expf(__fsub_rn(reg[j], mx));
             reg[j] = e;
             sum += e;
         }
     } else {
         for (int i = lane; i < N; i += 32) {
             const float v = logit(i);
-            sum += (v == -INFINITY) ? 0.0f : expf(v - mx);
+            sum += (v == -INFINITY) ? 0.0f : det_expf(__fsub_rn(v, mx));
         }
     }
     sum = warp_sum_f(sum);
-    const float inv = (sum > 0.0f) ? 1.0f / sum : 0.0f;
+    const float inv = (sum > 0.0f) ? __fdiv_rn(1.0f, sum) : 0.0f;
     if (in_regs) {
 #pragma unroll
         for (int j = 0; j < kSmRegs; ++j) {
             const int i = lane + 32 * j;
-            if (i < N) yr[i] = reg[j] * inv;
+            if (i < N) yr[i] = __fmul_rn(reg[j], inv);
         }
     } else {
         for (int i = lane; i < N; i += 32) {
             const float v = logit(i);
-            yr[i] = ((v == -INFINITY) ? 0.0f : expf(v - mx)) * inv;
+            yr[i] = __fmul_rn((v == -INFINITY) ? 0.0f : det_expf(__fsub_rn(v, mx)), inv);
         }
     }
 }
 
+cudaError_t launch_softmax_rows(const float* x, const float* mask, int64_t mask_rows, int64_t M, int64_t N,
+                                float scale, int causal_rows, float* y, cudaStream_t st) {
+    if (M <= 0) return cudaSuccess;
+    softmax_kernel<<<(unsigned)ceil_div(M, kSmWarps), kSmWarps * 32, 0, st>>>(x, mask, mask_rows, M, (int)N, scale,
+                                                                               causal_rows, y);
+    return cudaGetLastError();
+}
+
 cudaError_t launch_softmax(const float* x, const float* mask, int64_t mask_rows, int64_t M, int64_t N, float scale,
                            float* y, cudaStream_t st) {
-    if (M <= 0) return cudaSuccess;
-    softmax_kernel<<<(unsigned)ceil_div(M, kSmWarps), kSmWarps * 32, 0, st>>>(x, mask, mask_rows, M, (int)N, scale, y);
-    return cudaGetLastError();
+    return launch_softmax_rows(x, mask, mask_rows, M, N, scale, 0, y, st);
 }
 
 // ------------------------------------------------------------------------------------------------

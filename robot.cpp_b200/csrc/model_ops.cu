@@ -1,0 +1,510 @@
+// model_ops.cu -- the non-i2_s operators of a BitVLA-shape forward around the i2_s mul_mats.
+//
+//   * norm_kernel: ggml_norm (LayerNorm) / ggml_rms_norm followed by ggml_mul(weight) and ggml_add(bias),
+//     written as fp32 (the ViT post-norm and the decoder's output norm), or as per-token int8 through the
+//     act-quant semantics (LayerNorm + act-quant feeding a ternary GEMM). ggml's CPU norms accumulate in
+//     double: mean = (float)(sum x / K); v = x - mean; var = (float)(sum v^2 / K);
+//     scale = 1/sqrtf(var + eps); y = ((v * scale) * w) + b (src/models/smolvla/vision.cpp:314 pattern).
+//   * rope kernels: ggml_rope_ext in NEOX mode (src/models/pi0/vlm.cpp:223-235): for position p and
+//     pair (i, i + d/2), theta = p * base^(-2i/d), (x0, x1) -> (x0 cos - x1 sin, x0 sin + x1 cos); the
+//     angles in double, either per element or from a per-model table.
+//   * attention: one fused fp32 kernel per (query block, head, sequence) -- scores, softmax, P V -- the
+//     ggml graph mul_mat(K, Q) -> soft_max_ext -> mul_mat(V, KQ) of
+//     src/models/smolvla/action_expert.cpp:771-774, with grouped K/V heads (GQA) as in
+//     src/models/pi0/vlm.cpp:223-235, in a fixed operation order the CPU oracle repeats bit for bit.
+//   * patch embedding (fp32 tile GEMM reading the patches straight from the image, onto bias + position
+//     embedding) and a hash-seeded token-embedding gather for random-init vocabularies (the 128256 x 2560
+//     table is never materialized).
+#include "b2s_common.cuh"
+#include "b2s_internal.h"
+
+namespace b2s {
+
+// ------------------------------------------------------------------------------------------------ norms
+constexpr int kNormThreads = 256;
+
+__device__ __forceinline__ double block_sum_dbl(double v, double* red) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    v = warp_sum_d(v);
+    __syncthreads();
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    if (warp == 0) {
+        double w = (lane < (int)(blockDim.x >> 5)) ? red[lane] : 0.0;
+        w = warp_sum_d(w);
+        if (lane == 0) red[0] = w;
+    }
+    __syncthreads();
+    return red[0];
+}
+__device__ __forceinline__ float block_max_f(float v, float* red) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    v = warp_max(v);
+    __syncthreads();
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    if (warp == 0) {
+        float w = (lane < (int)(blockDim.x >> 5)) ? red[lane] : 0.0f;
+        w = warp_max(w);
+        if (lane == 0) red[0] = w;
+    }
+    __syncthreads();
+    return red[0];
+}
+__device__ __forceinline__ int block_sum_int(int v, int* red) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    v = warp_sum_i(v);
+    __syncthreads();
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    if (warp == 0) {
+        int w = (lane < (int)(blockDim.x >> 5)) ? red[lane] : 0;
+        w = warp_sum_i(w);
+        if (lane == 0) red[0] = w;
+    }
+    __syncthreads();
+    return red[0];
+}
+
+// KIND 0: RMSNorm, 1: LayerNorm. QUANT: write int8 codes + scale + sum instead of fp32.
+template <int KIND, bool QUANT>
+__global__ void __launch_bounds__(kNormThreads)
+norm_kernel(const float* __restrict__ x, int64_t ldx, const float* __restrict__ g, const float* __restrict__ b,
+            float eps, int K, float* __restrict__ y, int64_t ldy, int8_t* __restrict__ q, int64_t ldq,
+            float* __restrict__ s_out, int32_t* __restrict__ sum_out) {
+    __shared__ double red[32];
+    const int64_t m = blockIdx.x;
+    const float* xr = x + m * ldx;
+    griddep_wait();
+    griddep_launch();
+    float mean = 0.0f;
+    if (KIND == 1) {
+        double acc = 0.0;
+        for (int i = threadIdx.x; i < K; i += blockDim.x) acc += (double)xr[i];
+        mean = (float)(block_sum_dbl(acc, red) / (double)K);
+    }
+    double acc2 = 0.0;
+    for (int i = threadIdx.x; i < K; i += blockDim.x) {
+        const float v = (KIND == 1) ? __fsub_rn(xr[i], mean) : xr[i];
+        acc2 += (double)__fmul_rn(v, v);
+    }
+    const float var = (float)(block_sum_dbl(acc2, red) / (double)K);
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
+    auto val = [&](int i) -> float {
+        float v = (KIND == 1) ? __fsub_rn(xr[i], mean) : xr[i];
+        v = __fmul_rn(v, scale);
+        if (g) v = __fmul_rn(v, g[i]);
+        if (b) v = __fadd_rn(v, b[i]);
+        return v;
+    };
+    if (!QUANT) {
+        for (int i = threadIdx.x; i < K; i += blockDim.x) y[m * ldy + i] = val(i);
+        return;
+    }
+    float amax = 0.0f;
+    for (int i = threadIdx.x; i < K; i += blockDim.x) amax = fmaxf(amax, fabsf(val(i)));
+    amax = block_max_f(amax, reinterpret_cast<float*>(red));
+    const float s = actq_scale(amax);
+    int sum = 0;
+    for (int i = threadIdx.x; i < K; i += blockDim.x) {
+        const int a = actq_round(val(i), s);
+        q[m * ldq + i] = (int8_t)a;
+        sum += a;
+    }
+    sum = block_sum_int(sum, reinterpret_cast<int*>(red));
+    if (threadIdx.x == 0) {
+        s_out[m] = s;
+        if (sum_out) sum_out[m] = sum;
+    }
+}
+
+template <typename... KArgs, typename... Args>
+static cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, cudaStream_t st, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
+cudaError_t launch_norm(int kind, bool quant, const float* x, int64_t ldx, const float* g, const float* b, float eps,
+                        int64_t M, int64_t K, float* y, int64_t ldy, int8_t* q, int64_t ldq, float* s, int32_t* sums,
+                        cudaStream_t st) {
+    if (M <= 0) return cudaSuccess;
+    const dim3 grid((unsigned)M), block(kNormThreads);
+    const int k = (int)K;
+    if (kind == 0) {
+        if (quant) return launch_pdl(norm_kernel<0, true>, grid, block, st, x, ldx, g, b, eps, k, y, ldy, q, ldq, s, sums);
+        return launch_pdl(norm_kernel<0, false>, grid, block, st, x, ldx, g, b, eps, k, y, ldy, q, ldq, s, sums);
+    }
+    if (quant) return launch_pdl(norm_kernel<1, true>, grid, block, st, x, ldx, g, b, eps, k, y, ldy, q, ldq, s, sums);
+    return launch_pdl(norm_kernel<1, false>, grid, block, st, x, ldx, g, b, eps, k, y, ldy, q, ldq, s, sums);
+}
+
+// ------------------------------------------------------------------------------------------------ RoPE
+// Angles in double, rounded once to fp32: inv_freq = base^(-2i/d), theta = p * inv_freq,
+// (cos, sin) = ((float)cos(theta), (float)sin(theta)); then x0' = x0 c - x1 s, x1' = x0 s + x1 c in fp32.
+__device__ __forceinline__ float2 rope_cs(float base, int hd, int pos, int i) {
+    const double inv = pow((double)base, -2.0 * (double)i / (double)hd);
+    const double th = (double)pos * inv;
+    return make_float2((float)cos(th), (float)sin(th));
+}
+__device__ __forceinline__ void rope_rotate(float* r, int i, int half, float2 cs) {
+    const float x0 = r[i], x1 = r[i + half];
+    r[i] = __fsub_rn(__fmul_rn(x0, cs.x), __fmul_rn(x1, cs.y));
+    r[i + half] = __fadd_rn(__fmul_rn(x0, cs.y), __fmul_rn(x1, cs.x));
+}
+
+// One thread per (token, head, pair), angles computed in place.
+__global__ void rope_neox_kernel(float* __restrict__ x, int M, int n_heads, int hd, int64_t ld, float base,
+                                 int pos0) {
+    griddep_wait();
+    griddep_launch();
+    const int half = hd / 2;
+    const int64_t total = (int64_t)M * n_heads * half;
+    for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
+        const int i = (int)(e % half);
+        const int h = (int)((e / half) % n_heads);
+        const int m = (int)(e / ((int64_t)half * n_heads));
+        rope_rotate(x + (int64_t)m * ld + (int64_t)h * hd, i, half, rope_cs(base, hd, pos0 + m, i));
+    }
+}
+
+cudaError_t launch_rope_neox(float* x, int64_t M, int n_heads, int hd, int64_t ld, float base, int pos0,
+                             cudaStream_t st) {
+    const int64_t total = M * n_heads * (hd / 2);
+    if (total <= 0) return cudaSuccess;
+    const unsigned blocks = (unsigned)((total + 255) / 256 < 148 * 8 ? (total + 255) / 256 : 148 * 8);
+    return launch_pdl(rope_neox_kernel, dim3(blocks), dim3(256), st, x, (int)M, n_heads, hd, ld, base, pos0);
+}
+
+// The (cos, sin) table [n_pos][hd/2] of the same angles, built once per model.
+__global__ void rope_table_kernel(float base, int hd, int n_pos, float2* __restrict__ tab) {
+    const int half = hd / 2;
+    for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < n_pos * half; e += gridDim.x * blockDim.x)
+        tab[e] = rope_cs(base, hd, e / half, e % half);
+}
+cudaError_t launch_rope_table(float base, int hd, int n_pos, float2* tab, cudaStream_t st) {
+    rope_table_kernel<<<(n_pos * (hd / 2) + 255) / 256, 256, 0, st>>>(base, hd, n_pos, tab);
+    return cudaGetLastError();
+}
+
+// Rotation from the table; row m is position m % period (sequences of `period` tokens stacked).
+__global__ void rope_apply_kernel(float* __restrict__ x, int M, int n_heads, int hd, int64_t ld,
+                                  const float2* __restrict__ tab, int period) {
+    griddep_wait();
+    griddep_launch();
+    const int half = hd / 2;
+    const int64_t total = (int64_t)M * n_heads * half;
+    for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
+        const int i = (int)(e % half);
+        const int h = (int)((e / half) % n_heads);
+        const int m = (int)(e / ((int64_t)half * n_heads));
+        rope_rotate(x + (int64_t)m * ld + (int64_t)h * hd, i, half, tab[(m % period) * half + i]);
+    }
+}
+cudaError_t launch_rope_apply(float* x, int64_t M, int n_heads, int hd, int64_t ld, const float2* tab, int period,
+                              cudaStream_t st) {
+    const int64_t total = M * n_heads * (hd / 2);
+    if (total <= 0) return cudaSuccess;
+    const unsigned blocks = (unsigned)((total + 255) / 256 < 148 * 8 ? (total + 255) / 256 : 148 * 8);
+    return launch_pdl(rope_apply_kernel, dim3(blocks), dim3(256), st, x, (int)M, n_heads, hd, ld, tab, period);
+}
+
+// ------------------------------------------------------------------------------------------------ embeddings
+static unsigned grid_for(int64_t total) {
+    const int64_t b = (total + 255) / 256;
+    return (unsigned)(b < 148 * 16 ? (b > 0 ? b : 1) : 148 * 16);
+}
+
+// Patch embedding of stacked CHW images ([batch][C][H][W]; patch rows of image b follow those of b - 1):
+// Y[r][d] = (bias[d] + pos[r % np][d]) + acc, acc = fma(A[r][k], W[d][k], acc) over k = 0..C*P*P-1 in
+// order from +0, with A the non-overlapping patch rows (k = c P^2 + ky P + kx) read straight from the
+// image. A 64 x 64 output tile per CTA, 4 x 4 per thread, k staged 32 at a time.
+constexpr int kPeTile = 64, kPeK = 32;
+__global__ void __launch_bounds__(256)
+patch_embed_kernel(const float* __restrict__ img, int batch, int C, int H, int W, int P, const float* __restrict__ w,
+                   const float* __restrict__ bias, const float* __restrict__ pos, int D, float* __restrict__ y,
+                   int64_t ldy) {
+    __shared__ __align__(16) float As[kPeK][kPeTile];  // [k][patch row]
+    __shared__ __align__(16) float Ws[kPeK][kPeTile];  // [k][output column]
+    const int gw = W / P, np = (H / P) * gw, kdim = C * P * P, rows = batch * np;
+    const int r0 = blockIdx.x * kPeTile, d0 = blockIdx.y * kPeTile;
+    const int t = threadIdx.x, ty = t / 16, tx = t % 16;
+    float acc[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = 0.0f;
+    for (int k0 = 0; k0 < kdim; k0 += kPeK) {
+        for (int e = t; e < kPeTile * kPeK; e += 256) {
+            const int i = e % kPeTile, kk = e / kPeTile, k = k0 + kk;
+            float a = 0.0f, b = 0.0f;
+            if (k < kdim) {
+                const int c = k / (P * P), ky = (k / P) % P, kx = k % P;
+                const int r = r0 + i;
+                if (r < rows) {
+                    const int bi = r / np, p = r % np, py = p / gw, px = p % gw;
+                    a = img[(((int64_t)bi * C + c) * H + (py * P + ky)) * W + (px * P + kx)];
+                }
+                if (d0 + i < D) b = w[(int64_t)(d0 + i) * kdim + k];
+            }
+            As[kk][i] = a;
+            Ws[kk][i] = b;
+        }
+        __syncthreads();
+#pragma unroll 8
+        for (int kk = 0; kk < kPeK; ++kk) {
+            const float4 a = *reinterpret_cast<const float4*>(&As[kk][4 * ty]);
+            const float4 b = *reinterpret_cast<const float4*>(&Ws[kk][4 * tx]);
+            const float av[4] = {a.x, a.y, a.z, a.w}, bv[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) acc[i][j] = __fmaf_rn(av[i], bv[j], acc[i][j]);
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int r = r0 + 4 * ty + i;
+        if (r >= rows) continue;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int d = d0 + 4 * tx + j;
+            if (d >= D) continue;
+            float pre = bias ? bias[d] : 0.0f;
+            if (pos) pre = __fadd_rn(pre, pos[(int64_t)(r % np) * D + d]);
+            y[(int64_t)r * ldy + d] = __fadd_rn(pre, acc[i][j]);
+        }
+    }
+}
+
+cudaError_t launch_patch_embed(const float* img, int batch, int C, int H, int W, int P, const float* w,
+                               const float* bias, const float* pos, int D, float* y, int64_t ldy, cudaStream_t st) {
+    const int rows = batch * (H / P) * (W / P);
+    const dim3 grid((unsigned)ceil_div(rows, kPeTile), (unsigned)ceil_div(D, kPeTile));
+    patch_embed_kernel<<<grid, 256, 0, st>>>(img, batch, C, H, W, P, w, bias, pos, D, y, ldy);
+    return cudaGetLastError();
+}
+
+// Random-init embedding row of token t, column c: the parameter generator of the BitVLA engine
+// (tensor 0x80000000 | t, element c) mapped to U(-0.02, 0.02) with exact fp32 steps.
+__device__ __forceinline__ float hash_embedding(uint32_t seed, uint32_t t, uint32_t c) {
+    const float u = (float)(param_bits(seed, 0x80000000u | t, c) >> 8) * (1.0f / 16777216.0f);
+    return __fadd_rn(-0.02f, __fmul_rn(0.04f, u));
+}
+__global__ void embed_tokens_kernel(const int32_t* __restrict__ tokens, int n, int D, uint32_t seed,
+                                    float* __restrict__ y, int64_t ldy) {
+    const int64_t total = (int64_t)n * D;
+    for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
+        const int i = (int)(e / D), c = (int)(e % D);
+        y[(int64_t)i * ldy + c] = hash_embedding(seed, (uint32_t)tokens[i], (uint32_t)c);
+    }
+}
+
+cudaError_t launch_embed_tokens(const int32_t* tokens, int n, int D, uint32_t seed, float* y, int64_t ldy,
+                                cudaStream_t st) {
+    embed_tokens_kernel<<<grid_for((int64_t)n * D), 256, 0, st>>>(tokens, n, D, seed, y, ldy);
+    return cudaGetLastError();
+}
+
+// ------------------------------------------------------------------------------------------------ attention
+// softmax(Q K^T * scale [+ causal mask]) V for `batch` sequences of T tokens (sequence b at rows
+// [b T, (b+1) T) of every operand), one CTA per (64-query block, head, sequence). fp32 throughout, in a
+// fixed operation order that the CPU oracle repeats exactly:
+//   S[i][j] = fp32(acc * scale), acc = fma(q[i][d], k[j][d], acc) over d = 0..hd-1 from +0;
+//   softmax of row i over its keys j < n_i (n_i = i + 1 causal, else T): m = max, e_j = det_expf(S - m),
+//   sum over lanes (lane l adds e_j, j = l mod 32, in increasing j, then an xor butterfly),
+//   p_j = e_j * (1 / sum);
+//   O[i][d] = acc, acc = fma(p_j, v[j][d], acc) over j = 0..n_i-1 from +0 (keys past n_i within the
+//   block's key range enter with p = 0, which leaves a finite sum unchanged).
+// Query head h reads K/V head h / (heads / kv_heads) (GQA). Shared memory: Q^T [hd][64], one K^T or V
+// chunk [64 keys][hd], the score block [64][Tp]; hd % 8 == 0, hd <= 128.
+constexpr int kAtQ = 64, kAtThreads = 256;
+
+__host__ __device__ inline int attention_tp(int T) { return (int)round_up(T, 64) + 4; }
+size_t attention_smem_bytes(int T, int hd) {
+    return sizeof(float) * ((size_t)hd * kAtQ * 2 + (size_t)kAtQ * attention_tp(T));
+}
+
+__global__ void __launch_bounds__(kAtThreads)
+attention_kernel(const float* __restrict__ q, int64_t ldq, const float* __restrict__ k, int64_t ldk,
+                 const float* __restrict__ v, int64_t ldv, float* __restrict__ o, int64_t ldo, int T, int heads,
+                 int kv_heads, int hd, float scale, int causal) {
+    extern __shared__ __align__(16) float at_sm[];
+    const int Tp = attention_tp(T);
+    float* Qt = at_sm;             // [hd][64]
+    float* KV = Qt + hd * kAtQ;    // K^T chunk [hd][64] or V chunk [64][hd]
+    float* S = KV + hd * kAtQ;     // [64][Tp]
+    const int h = blockIdx.y, g = h / (heads / kv_heads);
+    const int q0 = blockIdx.x * kAtQ;
+    const int64_t row0 = (int64_t)blockIdx.z * T;
+    const float* qh = q + row0 * ldq + (int64_t)h * hd;
+    const float* kh = k + row0 * ldk + (int64_t)g * hd;
+    const float* vh = v + row0 * ldv + (int64_t)g * hd;
+    const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+    const int hd4 = hd / 4;
+    griddep_wait();  // q/k/v are written by the preceding kernel
+    griddep_launch();
+
+    for (int e = t; e < kAtQ * hd4; e += kAtThreads) {
+        const int i = e % kAtQ, d4 = 4 * (e / kAtQ);
+        float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (q0 + i < T) x = *reinterpret_cast<const float4*>(qh + (int64_t)(q0 + i) * ldq + d4);
+        Qt[(d4 + 0) * kAtQ + i] = x.x;
+        Qt[(d4 + 1) * kAtQ + i] = x.y;
+        Qt[(d4 + 2) * kAtQ + i] = x.z;
+        Qt[(d4 + 3) * kAtQ + i] = x.w;
+    }
+    const int kend = causal ? min(T, q0 + kAtQ) : T;  // keys any query of this block can see
+    const int nchunks = (kend + kAtQ - 1) / kAtQ;
+
+    // ---- scores
+    const int ty = t / 16, tx = t % 16;
+    for (int c = 0; c < nchunks; ++c) {
+        const int k0 = c * kAtQ;
+        __syncthreads();  // Qt written / previous chunk consumed
+        for (int e = t; e < kAtQ * hd4; e += kAtThreads) {
+            const int j = e % kAtQ, d4 = 4 * (e / kAtQ);
+            float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (k0 + j < T) x = *reinterpret_cast<const float4*>(kh + (int64_t)(k0 + j) * ldk + d4);
+            KV[(d4 + 0) * kAtQ + j] = x.x;
+            KV[(d4 + 1) * kAtQ + j] = x.y;
+            KV[(d4 + 2) * kAtQ + j] = x.z;
+            KV[(d4 + 3) * kAtQ + j] = x.w;
+        }
+        __syncthreads();
+        float acc[4][4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) acc[i][j] = 0.0f;
+#pragma unroll 4
+        for (int d = 0; d < hd; ++d) {
+            const float4 a = *reinterpret_cast<const float4*>(&Qt[d * kAtQ + 4 * ty]);
+            const float4 b = *reinterpret_cast<const float4*>(&KV[d * kAtQ + 4 * tx]);
+            const float av[4] = {a.x, a.y, a.z, a.w}, bv[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) acc[i][j] = __fmaf_rn(av[i], bv[j], acc[i][j]);
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int row = 4 * ty + i, qi = q0 + row;
+            float4 l;
+            float* lv = reinterpret_cast<float*>(&l);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int key = k0 + 4 * tx + j;
+                lv[j] = (key >= T || (causal && key > qi)) ? -INFINITY : __fmul_rn(acc[i][j], scale);
+            }
+            *reinterpret_cast<float4*>(&S[row * Tp + k0 + 4 * tx]) = l;
+        }
+    }
+    __syncthreads();
+
+    // ---- softmax rows (one warp per row)
+    for (int row = warp; row < kAtQ; row += kAtThreads / 32) {
+        const int qi = q0 + row;
+        float* sr = S + row * Tp;
+        const int nk = (qi < T) ? (causal ? qi + 1 : T) : 0;
+        float mx = -INFINITY;
+        for (int j = lane; j < nk; j += 32) mx = fmaxf(mx, sr[j]);
+        mx = warp_max(mx);
+        float sum = 0.0f;
+        for (int j = lane; j < nk; j += 32) {
+            const float e = det_expf(__fsub_rn(sr[j], mx));
+            sr[j] = e;
+            sum = __fadd_rn(sum, e);
+        }
+        sum = warp_sum_f(sum);
+        const float inv = (sum > 0.0f) ? __fdiv_rn(1.0f, sum) : 0.0f;
+        for (int j = lane; j < kend; j += 32) sr[j] = (j < nk) ? __fmul_rn(sr[j], inv) : 0.0f;
+    }
+
+    // ---- O = P V: thread item (row group rg of 4 rows, column group cg of 8)
+    const int ncg = hd / 8;
+    const bool active = t < 16 * ncg;
+    const int rg = active ? t / ncg : 0, cg = active ? t % ncg : 0;
+    float acc[4][8];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[i][j] = 0.0f;
+    for (int c = 0; c < nchunks; ++c) {
+        const int k0 = c * kAtQ;
+        __syncthreads();  // scores finished / previous V chunk consumed
+        for (int e = t; e < kAtQ * hd4; e += kAtThreads) {
+            const int j = e / hd4, d4 = 4 * (e % hd4);
+            float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (k0 + j < T) x = *reinterpret_cast<const float4*>(vh + (int64_t)(k0 + j) * ldv + d4);
+            *reinterpret_cast<float4*>(&KV[j * hd + d4]) = x;
+        }
+        __syncthreads();
+        if (active) {
+            const int jn = min(kAtQ, kend - k0);
+            for (int jj = 0; jj < jn; ++jj) {
+                const float4 v0 = *reinterpret_cast<const float4*>(&KV[jj * hd + 8 * cg]);
+                const float4 v1 = *reinterpret_cast<const float4*>(&KV[jj * hd + 8 * cg + 4]);
+                const float vv[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const float p = S[(4 * rg + i) * Tp + k0 + jj];
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) acc[i][j] = __fmaf_rn(p, vv[j], acc[i][j]);
+                }
+            }
+        }
+    }
+    if (active) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int qi = q0 + 4 * rg + i;
+            if (qi >= T) continue;
+            float* orow = o + (row0 + qi) * ldo + (int64_t)h * hd + 8 * cg;
+            *reinterpret_cast<float4*>(orow) = make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
+            *reinterpret_cast<float4*>(orow + 4) = make_float4(acc[i][4], acc[i][5], acc[i][6], acc[i][7]);
+        }
+    }
+}
+
+bool attention_supported(int T, int hd, int64_t ldq, int64_t ldk, int64_t ldv, int64_t ldo, const void* q,
+                         const void* k, const void* v, const void* o) {
+    auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+    return T > 0 && hd > 0 && hd % 8 == 0 && hd <= 128 && ldq % 4 == 0 && ldk % 4 == 0 && ldv % 4 == 0 &&
+           ldo % 4 == 0 && a16(q) && a16(k) && a16(v) && a16(o) && attention_smem_bytes(T, hd) <= 227 * 1024;
+}
+
+cudaError_t launch_attention(const float* q, int64_t ldq, const float* k, int64_t ldk, const float* v, int64_t ldv,
+                             int batch, int T, int heads, int kv_heads, int hd, float scale, bool causal, float* o,
+                             int64_t ldo, cudaStream_t st) {
+    if (batch <= 0 || T <= 0) return cudaSuccess;
+    const size_t smem = attention_smem_bytes(T, hd);
+    static size_t opted = 0;  // largest dynamic shared memory size enabled so far (attribute is per function)
+    if (smem > 48 * 1024 && smem > opted) {
+        cudaError_t e = cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+        opted = smem;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)ceil_div(T, kAtQ), (unsigned)heads, (unsigned)batch);
+    cfg.blockDim = dim3(kAtThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, attention_kernel, q, ldq, k, ldk, v, ldv, o, ldo, T, heads, kv_heads, hd, scale,
+                              causal ? 1 : 0);
+}
+
+}  // namespace b2s

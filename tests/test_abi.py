@@ -1,5 +1,6 @@
-"""The C ABI library without a GPU: it loads, exports every symbol include/b2s.h declares, its host type
-traits agree with the oracle byte for byte, and device entry points fail cleanly (no compute calls)."""
+"""The C ABI library without a GPU: it loads, exports every symbol include/b2s.h and include/b2s_bitvla.h
+declare, its host type traits agree with the oracle byte for byte, and device entry points fail cleanly
+(no compute calls)."""
 import os
 import re
 
@@ -9,8 +10,8 @@ import pytest
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 
-def declared_symbols():
-    src = open(os.path.join(ROOT, "include", "b2s.h")).read()
+def declared_symbols(header="b2s.h"):
+    src = open(os.path.join(ROOT, "include", header)).read()
     src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
     return sorted(set(re.findall(r"\b(b2s_\w+)\s*\(", src)))
 
@@ -23,6 +24,37 @@ def test_exports_every_declared_symbol(b2s):
     missing = [s for s in decl if not hasattr(lib, s)]
     assert not missing, f"declared but not exported: {missing}"
     assert sorted(b2s.EXPORTED) == decl
+
+
+def test_exports_bitvla_symbols(b2s):
+    import ctypes
+    from b2s import bitvla
+    lib = ctypes.CDLL(b2s.LIB_PATH)
+    decl = declared_symbols("b2s_bitvla.h")
+    assert decl and not [s for s in decl if not hasattr(lib, s)]
+    assert sorted(bitvla.EXPORTED) == decl
+
+
+def test_bitvla_host_traits(b2s, orc):
+    """Host-side engine traits: the parameter generator matches the oracle's; shapes and op counts."""
+    from b2s import bitvla
+    for seed, tensor, idx in [(0, 0, 0), (7, 0x100, 12345), (0xFFFFFFFF, 0x10000 + 16 * 29 + 10, 2**31 + 5),
+                              (123, 0x80000000 | 128255, 2559)]:
+        assert bitvla.param_bits(seed, tensor, idx) == orc.bv_param_bits(seed, tensor, idx)
+    cfg = bitvla.default_config()
+    assert bitvla.seq_len(cfg) == 288 == orc.bitvla_seq_len(orc.bitvla_config())
+    ops = bitvla.ternary_ops(cfg)
+    # ViT 0.210 T + decoder 1.200 T + connector (1152x2560 and 2560x2560 over 256 tokens)
+    vit = 2 * 256 * 27 * (4 * 1152 * 1152 + 2 * 1152 * 4304)
+    dec = 2 * 288 * 30 * (2 * 2560 * 2560 + 2 * 2560 * 640 + 3 * 2560 * 6912)
+    conn = 2 * 256 * (1152 * 2560 + 2560 * 2560)
+    assert ops == vit + dec + conn
+    assert abs(vit / 1e12 - 0.210) < 0.001 and abs(dec / 1e12 - 1.200) < 0.001
+    bad = bitvla.default_config(patch=15)
+    import ctypes
+    h = ctypes.c_void_p()
+    assert bitvla._bind().b2s_bitvla_create(ctypes.byref(bad), 1, 1, ctypes.byref(h)) != 0
+    assert not h.value
 
 
 def test_nbytes(b2s, orc):

@@ -1,0 +1,125 @@
+"""The BitVLA-shape engine (C ABI include/b2s_bitvla.h) against the oracle's forward, on a B200.
+
+The engine regenerates the random-init model on the device from the seed; the oracle regenerates the
+same parameters on the host with its own copy of the generator. Every operator of the forward repeats the
+oracle's IEEE operation sequence (ternary GEMMs exact in int32, fixed-order fused multiply-adds in
+attention and patch embedding, the deterministic exp/tanh), so hidden states and actions are compared
+bit for bit, after the max-abs-rel bars (max |y - ref| / max |ref|) of 1e-5 per operator and 1e-3 end to
+end through all 30 decoder layers.
+"""
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+pytestmark = pytest.mark.gpu
+
+
+def max_abs_rel(y, ref):
+    ref = np.asarray(ref, np.float64)
+    return float(np.max(np.abs(np.asarray(y, np.float64) - ref)) / max(np.max(np.abs(ref)), 1e-30))
+
+
+def inputs(cfg, batch, seed):
+    g = np.random.Generator(np.random.PCG64(seed))
+    img = g.random((batch, 3, cfg.image_size, cfg.image_size), dtype=np.float32)
+    tok = g.integers(0, cfg.vocab, (batch, cfg.n_text)).astype(np.int32)
+    return img, tok
+
+
+def run_engine(cfg_over, seed, batch, img, tok, max_batch=None):
+    from b2s import bitvla, device_error
+    cfg = bitvla.default_config(**cfg_over)
+    m = bitvla.Model(cfg, seed, max_batch=max_batch or batch)
+    seq = m.seq_len
+    hidden = torch.full((batch * seq, cfg.dec_hidden), float("nan"), dtype=torch.float32, device="cuda")
+    actions = torch.full((batch, cfg.action_chunk * cfg.action_dim), float("nan"), dtype=torch.float32,
+                         device="cuda")
+    m.forward(torch.from_numpy(img).cuda(), torch.from_numpy(tok).cuda(), hidden, actions)
+    torch.cuda.synchronize()
+    assert device_error() == 0
+    out = hidden.cpu().numpy(), actions.cpu().numpy()
+    m.close()
+    return out
+
+
+def run_oracle(orc, cfg_over, seed, img, tok):
+    return orc.bitvla_forward(orc.bitvla_config(**cfg_over), seed, img, tok)
+
+
+@pytest.mark.parametrize("over,tol", [
+    (dict(vit_layers=0, dec_layers=0), 1e-5),             # patch embed -> post-LN -> connector -> final norm
+    (dict(vit_layers=0, dec_layers=0, n_text=0), 1e-5),   # no text tokens
+])
+def test_connector_path(b2s, orc, over, tol):
+    img, tok = inputs(orc.bitvla_config(**over), 1, 11)
+    h, a = run_engine(over, 5, 1, img, tok)
+    h_ref, a_ref = run_oracle(orc, over, 5, img, tok)
+    assert max_abs_rel(h, h_ref) <= tol and max_abs_rel(a, a_ref) <= tol
+    assert np.array_equal(h, h_ref) and np.array_equal(a, a_ref)
+
+
+@pytest.mark.parametrize("batch", [1, 3])
+def test_reduced_depth(b2s, orc, batch):
+    over = dict(vit_layers=2, dec_layers=2)
+    img, tok = inputs(orc.bitvla_config(**over), batch, 21)
+    h, a = run_engine(over, 9, batch, img, tok)
+    h_ref, a_ref = run_oracle(orc, over, 9, img, tok)
+    assert np.isfinite(h).all() and np.isfinite(a).all()
+    assert max_abs_rel(h, h_ref) <= 1e-5 and max_abs_rel(a, a_ref) <= 1e-5
+    assert np.array_equal(h, h_ref) and np.array_equal(a, a_ref)
+
+
+def test_batch_rows_independent(b2s, orc):
+    """Observation b of a batched forward equals the same observation run alone."""
+    over = dict(vit_layers=1, dec_layers=1)
+    img, tok = inputs(orc.bitvla_config(**over), 2, 31)
+    h2, a2 = run_engine(over, 3, 2, img, tok)
+    h1, a1 = run_engine(over, 3, 1, img[1:], tok[1:])
+    seq = h1.shape[0]
+    assert np.array_equal(h2[seq:], h1)
+    assert np.array_equal(a2[1:], a1)
+
+
+def test_full_depth_end_to_end(b2s, orc):
+    """The BitVLA shape (27 ViT + 30 decoder layers), one observation: 1e-3 end to end."""
+    img, tok = inputs(orc.bitvla_config(), 1, 41)
+    h, a = run_engine({}, 2024, 1, img, tok)
+    h_ref, a_ref = run_oracle(orc, {}, 2024, img, tok)
+    assert max_abs_rel(h, h_ref) <= 1e-3 and max_abs_rel(a, a_ref) <= 1e-3
+    assert np.array_equal(h, h_ref) and np.array_equal(a, a_ref)
+
+
+def test_predict_host_path(b2s):
+    """predict() (uint8 HWC host images -> host actions) equals forward() on value/255 images."""
+    from b2s import bitvla
+    over = dict(vit_layers=1, dec_layers=1)
+    cfg = bitvla.default_config(**over)
+    g = np.random.Generator(np.random.PCG64(77))
+    u8 = g.integers(0, 256, (2, cfg.image_size, cfg.image_size, 3)).astype(np.uint8)
+    tok = g.integers(0, cfg.vocab, (2, cfg.n_text)).astype(np.int32)
+    m = bitvla.Model(cfg, 17, max_batch=2)
+    act = np.zeros((2, cfg.action_chunk * cfg.action_dim), np.float32)
+    m.predict(u8, tok, act)
+    img = (u8.astype(np.float32).transpose(0, 3, 1, 2) / np.float32(255.0)).astype(np.float32)
+    a_dev = torch.zeros((2, act.shape[1]), dtype=torch.float32, device="cuda")
+    m.forward(torch.from_numpy(np.ascontiguousarray(img)).cuda(), torch.from_numpy(tok).cuda(), None, a_dev)
+    torch.cuda.synchronize()
+    assert np.array_equal(act, a_dev.cpu().numpy())
+    # replaying the captured graph gives the same answer
+    act2 = np.zeros_like(act)
+    m.predict(u8, tok, act2)
+    assert np.array_equal(act, act2)
+    m.close()
+
+
+def test_create_errors(b2s):
+    from b2s import bitvla
+    with pytest.raises(b2s.B2SError):
+        bitvla.Model(bitvla.default_config(vit_hidden=1000), 1)
+    m = bitvla.Model(bitvla.default_config(vit_layers=0, dec_layers=0), 1, max_batch=1)
+    img = torch.zeros((2, 3, 224, 224), dtype=torch.float32, device="cuda")
+    tok = torch.zeros((2, 32), dtype=torch.int32, device="cuda")
+    with pytest.raises(b2s.B2SError):
+        m.forward(img, tok)  # batch 2 > max_batch 1
+    m.close()
