@@ -21,6 +21,20 @@ threads, on the same workload.
 
 Multi-GPU: one process per GPU (torchrun); the FFN block batches are independent (data parallel, no
 collective on the data path); timing is the max over ranks; scaling "weak".
+
+--workload bitvla: the batched model-server run -- 64 independent random-init BitVLA-shape observations
+(224x224 image + 32 text tokens each; 27-layer ternary ViT, connector, 30-layer ternary decoder prefill of
+288 tokens) sharded data parallel over the ranks with no collective (strong scaling: the 64 observations
+are the whole job). Each rank runs its share as forwards of --obs-batch observations through the
+library's graph-captured engine. value = observations/s of the whole job; p50 latency = median forward
+time of one batch (every observation in it waits that long); e2e = the same through b2s_bitvla_predict
+(uint8 host images in, host actions out).
+
+--workload sweep: the i2_s GEMM roofline sweep, M in {1, 16, 256, 4096, 16384} x (K,N) in {(2560,2560),
+(2560,6912), (6912,2560), (1152,4304)} on pre-quantized int8 activations. Each point replays a CUDA graph
+of back-to-back launches over rotating weight copies (> 2x L2 of weights per pass), so weights stream
+from HBM; it reports TOP/s and algorithmic GB/s per launch against the measured peaks (HBM-bound for
+M <= 16, tensor-bound from M = 256).
 """
 from __future__ import annotations
 
@@ -49,6 +63,10 @@ def parse():
     p.add_argument("--warmup", type=int, default=20)
     p.add_argument("--impl", default="b2s", choices=["b2s", "reference"])
     p.add_argument("--cpu-seconds", type=float, default=10.0, help="bounded CPU-baseline sample length")
+    p.add_argument("--workload", default="ffn", choices=["ffn", "bitvla", "sweep"])
+    p.add_argument("--observations", type=int, default=64, help="bitvla: observations in the whole job")
+    p.add_argument("--obs-batch", type=int, default=8, help="bitvla: observations per forward")
+    p.add_argument("--sweep-m", default="", help="sweep: comma-separated M values (default: all five)")
     return p.parse_args()
 
 
@@ -377,9 +395,280 @@ def run_b2s(a, world, rank, local):
     print(json.dumps(line), flush=True)
 
 
+def run_bitvla_reference(a, world, rank):
+    """The oracle's forward (the CPU restatement of the path) on all host threads, one observation per step."""
+    if rank != 0:
+        return
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+    nthreads = cpu_threads()
+    cfg = oracle.bitvla_config()
+    imgs, toks, _ = bitvla_inputs(1, 0, cfg.image_size, cfg.n_text, cfg.vocab)
+    steps = max(1, min(a.steps, 3))
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        oracle.bitvla_forward(cfg, 1234, imgs, toks, nthreads)
+    dt = time.perf_counter() - t0
+    value = steps / dt
+    line = {"impl": "reference", "metric": METRIC, "value": round(value, 5), "unit": "obs/s", "n_gpus": world,
+            "steps": steps, "warmup": 0, "ms_per_step": round(dt / steps * 1e3, 1), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "int8xternary->int32",
+            "data": "synthetic (seeded random-init BitVLA-shape weights)",
+            "config": {"workload": "bitvla_server_64obs", "parallelism": "host threads"},
+            "cpu_baseline": {"value": round(value, 5), "unit": "obs/s", "cores": nthreads, "kind": "port",
+                             "sample": f"{steps} observation forwards, {cpu_model()}"},
+            "e2e": {"value": round(value, 5), "unit": "obs/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------------------------------- BitVLA server run
+def bitvla_inputs(n_obs: int, first: int, image_size: int, n_text: int, vocab: int):
+    """Observation i: seeded U(0,1) image (also as uint8 for the host API) and uniform token ids."""
+    import numpy as np
+    imgs = np.empty((n_obs, 3, image_size, image_size), np.float32)
+    toks = np.empty((n_obs, n_text), np.int32)
+    for j in range(n_obs):
+        g = np.random.Generator(np.random.PCG64(1000 + first + j))
+        imgs[j] = g.random((3, image_size, image_size), dtype=np.float32)
+        toks[j] = g.integers(0, vocab, n_text)
+    u8 = np.ascontiguousarray((imgs * 255.0 + 0.5).astype(np.uint8).transpose(0, 2, 3, 1))
+    return imgs, toks, u8
+
+
+def kernels_per_forward(cfg) -> int:
+    """Library kernels in one captured forward: patch embedding; 9 per ViT layer (norm+quant, qkv,
+    attention, quant, o, norm+quant, fc1, quant, fc2); connector 4; text embedding; 10 per decoder layer
+    (norm+quant, qkv, RoPE, attention, norm+quant, o, norm+quant, gate/up, norm+quant, down); final norm;
+    action head."""
+    return 1 + 9 * cfg.vit_layers + 4 + (1 if cfg.n_text > 0 else 0) + 10 * cfg.dec_layers + 2
+
+
+def run_bitvla(a, world, rank, local):
+    import numpy as np
+    import torch
+    import b2s
+    from b2s import bitvla
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    b2s.check(b2s.lib().b2s_device_check())
+    pg = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+        pg = dist
+    cfg = bitvla.default_config()
+    total = a.observations
+    lo, hi = total * rank // world, total * (rank + 1) // world
+    mine = hi - lo
+    B = max(1, min(a.obs_batch, mine))
+    batches = [(i, min(B, mine - i)) for i in range(0, mine, B)]
+    model = bitvla.Model(cfg, 1234, max_batch=B)  # same seed on every rank: replicated weights
+    imgs, toks, u8 = bitvla_inputs(mine, lo, cfg.image_size, cfg.n_text, cfg.vocab)
+    d_img = torch.from_numpy(imgs).to(dev)
+    d_tok = torch.from_numpy(toks).to(dev)
+    A = cfg.action_chunk * cfg.action_dim
+    d_act = torch.empty((mine, A), dtype=torch.float32, device=dev)
+    stream = torch.cuda.Stream(device=dev)
+
+    def step(ev=None):
+        for j, (i0, nb) in enumerate(batches):
+            if ev is not None:
+                ev[j][0].record(stream)
+            model.forward(d_img[i0:i0 + nb], d_tok[i0:i0 + nb], None, d_act[i0:i0 + nb], stream=stream)
+            if ev is not None:
+                ev[j][1].record(stream)
+
+    for _ in range(max(3, a.warmup)):
+        step()
+    stream.synchronize()
+    assert b2s.device_error() == 0
+
+    def barrier():
+        if pg is not None:
+            pg.barrier()
+
+    steps = a.steps
+    evs = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in batches]
+           for _ in range(steps)]
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        t0.record(stream)
+        for k in range(steps):
+            step(evs[k])
+        t1.record(stream)
+        torch.cuda.synchronize()
+    barrier()
+    ms = t0.elapsed_time(t1)
+    lat = sorted(e0.elapsed_time(e1) for ev in evs for e0, e1 in ev)
+    assert b2s.device_error() == 0
+
+    # e2e: host uint8 images + tokens in, host actions out, through the predict API
+    h_act = np.empty((mine, A), np.float32)
+
+    def e2e_step():
+        for i0, nb in batches:
+            model.predict(u8[i0:i0 + nb], toks[i0:i0 + nb], h_act[i0:i0 + nb], stream=stream)
+
+    e2e_step()
+    barrier()
+    torch.cuda.synchronize()
+    te = time.perf_counter()
+    for _ in range(steps):
+        e2e_step()
+    torch.cuda.synchronize()
+    e_ms = (time.perf_counter() - te) * 1e3
+    barrier()
+    if pg is not None:
+        t = torch.tensor([ms, e_ms], dtype=torch.float64, device=dev)
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        ms, e_ms = float(t[0]), float(t[1])
+        pg.destroy_process_group()
+    tern_mb = model.ternary_bytes() / 1e6
+    model.close()
+    if rank != 0:
+        return
+    ops = bitvla.ternary_ops(cfg)
+    pk, pk_kind = peaks()
+    tensor_peak_tops = 2.0 * pk.get("bf16_tflops_sustained", pk["bf16_tflops"])
+    value = steps * total / (ms * 1e-3)
+    fwd_ms = statistics.median(lat)
+    achieved = ops * B / (fwd_ms * 1e-3) / 1e12
+    line = {
+        "metric": METRIC, "value": round(value, 3), "unit": "obs/s", "n_gpus": world, "steps": steps,
+        "warmup": a.warmup, "ms_per_step": round(ms / steps, 4), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "int8xternary->int32 (fp32 attention, norms, residual)",
+        "data": "synthetic (seeded random-init BitVLA-shape weights, U(0,1) images, uniform tokens)",
+        "config": {"workload": "bitvla_server_64obs", "observations": total, "obs_per_forward": B,
+                   "image": cfg.image_size, "vit_layers": cfg.vit_layers, "decoder_layers": cfg.dec_layers,
+                   "tokens": bitvla.seq_len(cfg), "parallelism": f"dp{world} (observations sharded, no collective)",
+                   "l2": f"{tern_mb:.0f} MB of ternary weights streamed per forward (> 126 MB L2)"},
+        "latency_ms": {"p50": round(fwd_ms, 3), "p90": round(lat[int(0.9 * (len(lat) - 1))], 3),
+                       "unit": "ms per forward of obs_per_forward observations"},
+        "e2e": {"value": round(steps * total / (e_ms * 1e-3), 3), "unit": "obs/s",
+                "h2d_bytes_per_step": total * (3 * cfg.image_size ** 2 + 4 * cfg.n_text),
+                "d2h_bytes_per_step": total * A * 4, "api": "b2s_bitvla_predict (C ABI), host uint8 images"},
+        "roofline": {"kernel": "whole forward (ternary int ops / forward time)", "bound": "tensor",
+                     "achieved": round(achieved, 2), "peak": round(tensor_peak_tops, 1), "unit": "TOP/s",
+                     "frac": round(achieved / tensor_peak_tops, 4), "traffic": None,
+                     "peak_basis": f"int8 dense = 2x {pk_kind} cuBLAS bf16 sustained"},
+        "gpu_launches": steps * len(batches) * kernels_per_forward(cfg),
+        "clocks": clk.summary(),
+    }
+    if world == 1:
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import oracle  # CPU baseline leg only
+        nthreads = cpu_threads()
+        ocfg = oracle.bitvla_config()
+        t_c = time.perf_counter()
+        oracle.bitvla_forward(ocfg, 1234, imgs[:1], toks[:1], nthreads)
+        dt = time.perf_counter() - t_c
+        line["cpu_baseline"] = {"value": round(1.0 / dt, 5), "unit": "obs/s", "cores": nthreads, "kind": "port",
+                                "sample": f"1 observation (full forward) in {dt:.1f} s, {cpu_model()}"}
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------------------------------- GEMM sweep
+def run_sweep(a, world, rank, local):
+    import torch
+    import b2s
+    from b2s import workloads as wl
+
+    if rank != 0:
+        return
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    b2s.check(b2s.lib().b2s_device_check())
+    pk, pk_kind = peaks()
+    hbm = pk["hbm_gbs"]
+    tensor_peak = 2.0 * pk.get("bf16_tflops", 1590.0)  # launches timed alone: the burst figure
+    stream = torch.cuda.Stream(device=dev)
+    ms_list = [int(x) for x in a.sweep_m.split(",")] if a.sweep_m else list(wl.SWEEP_M)
+    rows = []
+    for K, N in wl.SWEEP_KN:
+        g = wl.rng(K + N)
+        w = wl.weight(g, N, K)
+        base = torch.from_numpy(w.packed).to(dev)
+        Kp = (K + 127) // 128 * 128
+        if K % 128:
+            rb = torch.empty(b2s.i2s_r_nbytes(N, K), dtype=torch.uint8, device=dev)
+            b2s.repack_rows(base, rb, N, K, stream=stream)
+            stream.synchronize()
+            base = rb
+        wbytes = N * Kp // 4
+        R = max(2, min(256, -(-(2 * 126 * 2**20 + 8 * 2**20) // wbytes)))
+        copies = []
+        for r in range(R):
+            b = base.clone()
+            if r:
+                b[:wbytes] = torch.roll(base[:wbytes], shifts=r * 4099)
+            copies.append((b, b2s.i2s_tensor(b, N, K, rowpadded=bool(K % 128))))
+        for M in ms_list:
+            ldq = (K + 15) // 16 * 16
+            q = torch.randint(-127, 128, (M, ldq), dtype=torch.int8, device=dev)[:, :K]
+            s = torch.rand(M, device=dev) + 0.5
+            u = q.to(torch.int32).sum(dim=1).to(torch.int32)
+            y = torch.empty((M, N), dtype=torch.float32, device=dev)
+            launches = R if M <= 4096 else max(2, min(R, 16))
+            def seq():
+                for r in range(launches):
+                    b2s.mul_mat_q8(copies[r % R][1], q, s, u, y, stream=stream)
+            with torch.cuda.stream(stream):
+                seq()
+            stream.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=stream):
+                seq()
+            with torch.cuda.stream(stream):
+                for _ in range(3):
+                    graph.replay()
+            stream.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            reps = 5
+            with torch.cuda.stream(stream):
+                e0.record(stream)
+                for _ in range(reps):
+                    graph.replay()
+                e1.record(stream)
+            stream.synchronize()
+            us = e0.elapsed_time(e1) * 1e3 / (reps * launches)
+            assert b2s.device_error() == 0
+            ops = 2.0 * M * N * K
+            byts = wbytes + M * K + 8 * M + 4 * M * N
+            tops, gbs = ops / us / 1e6, byts / us / 1e3
+            bound = "hbm" if M <= 16 else "tensor"
+            rows.append({"M": M, "K": K, "N": N, "path": "gemv" if M <= 16 else "tcgen05", "us": round(us, 3),
+                         "TOP/s": round(tops, 1), "GB/s": round(gbs, 1), "bound": bound,
+                         "frac": round(gbs / hbm if bound == "hbm" else tops / tensor_peak, 4)})
+            graph.reset()
+            del q, s, u, y
+        del copies
+        torch.cuda.empty_cache()
+    big = [r["TOP/s"] for r in rows if r["M"] >= 4096]
+    line = {"metric": METRIC, "value": round(sum(big) / max(1, len(big)), 1), "unit": "TOP/s (mean over M >= 4096)",
+            "n_gpus": 1, "steps": 5, "warmup": 3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "int8xternary->int32", "data": "synthetic (ternary P(0)=0.4, random int8 activations)",
+            "config": {"workload": "i2s_gemm_sweep", "l2": "rotating weight copies, > 2x L2 of weights per pass",
+                       "peaks": f"{pk_kind}: HBM {hbm} GB/s, int8 = 2x bf16 burst {tensor_peak:.0f} TOP/s"},
+            "sweep": rows}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     a = parse()
     world, rank, local = dist_env()
+    if a.workload == "sweep":
+        run_sweep(a, world, rank, local)
+        return
+    if a.workload == "bitvla":
+        if a.impl == "reference":
+            run_bitvla_reference(a, world, rank)
+        else:
+            run_bitvla(a, world, rank, local)
+        return
     if a.impl == "reference":
         run_reference(a, world, rank)
         return

@@ -123,3 +123,46 @@ class Model:
         B = images_hwc.shape[0]
         check(_bind().b2s_bitvla_predict(self._h, B, images_hwc.ctypes.data, tokens.ctypes.data,
                                          actions.ctypes.data, _stream(stream)))
+
+
+def _main(argv=None) -> None:
+    """Times forwards of the BitVLA shape on cuda:0; with --profile-range the timed forwards are bracketed
+    by cudaProfilerStart/Stop (for `ncu --profile-from-start off`).
+
+        PYTHONPATH=robot.cpp_b200 python -m b2s.bitvla --batch 8 --iters 1 --profile-range
+    """
+    import argparse
+    import torch
+
+    p = argparse.ArgumentParser(description=_main.__doc__)
+    p.add_argument("--batch", type=int, default=1)
+    p.add_argument("--iters", type=int, default=10)
+    p.add_argument("--seed", type=int, default=1234)
+    p.add_argument("--profile-range", action="store_true")
+    a = p.parse_args(argv)
+    cfg = default_config()
+    m = Model(cfg, a.seed, max_batch=a.batch)
+    img = torch.rand((a.batch, 3, cfg.image_size, cfg.image_size), device="cuda")
+    tok = torch.randint(0, cfg.vocab, (a.batch, cfg.n_text), dtype=torch.int32, device="cuda")
+    act = torch.zeros((a.batch, cfg.action_chunk * cfg.action_dim), device="cuda")
+    for _ in range(3):  # the first call captures the graph
+        m.forward(img, tok, None, act)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if a.profile_range:
+        torch.cuda.cudart().cudaProfilerStart()
+    e0.record()
+    for _ in range(a.iters):
+        m.forward(img, tok, None, act)
+    e1.record()
+    torch.cuda.synchronize()
+    if a.profile_range:
+        torch.cuda.cudart().cudaProfilerStop()
+    ms = e0.elapsed_time(e1) / a.iters
+    print(f"batch {a.batch}: {ms:.3f} ms per forward, {a.batch / ms * 1e3:.1f} obs/s, "
+          f"{ternary_ops(cfg) * a.batch / ms / 1e9:.1f} ternary TOP/s")
+    m.close()
+
+
+if __name__ == "__main__":
+    _main()

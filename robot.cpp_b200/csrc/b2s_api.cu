@@ -213,7 +213,32 @@ int run_tc(const b2s::I2sWeight& w0, const b2s::I2sWeight* w1, const int8_t* q, 
         return fail(B2S_ERR_UNSUPPORTED, "tensor-core path needs 16-byte aligned q with ldq %% 16 == 0");
     if (M > (int64_t)0x7fffffff || w0.N > (int64_t)0x7fffffff) return fail(B2S_ERR_UNSUPPORTED, "size exceeds int32");
     const int rows = (mode == 1) ? 64 : 128;
-    const TcTiling t = pick_tiling(M, w0.N, rows, w0.Kp, num_sms_current());
+    const int nsm = num_sms_current();
+    TcTiling t = pick_tiling(M, w0.N, rows, w0.Kp, nsm);
+    // Persistent kernel when the one-tile-per-CTA kernel would need more than one wave (its tiles of up to
+    // 320 tokens exceed the SM count): choose the token tile that minimises (tiles per SM) x (tile tokens +
+    // 64), the 64 standing for the per-tile fixed costs.
+    int p_grid = 0;
+    if ((int64_t)t.n_tiles * t.m_tiles > nsm) {
+        const int64_t n_tiles = b2s::ceil_div(w0.N, rows), mt0 = b2s::ceil_div(M, b2s::tcp_max_tokens());
+        int64_t best = -1;
+        for (int64_t mt = mt0; mt <= mt0 + 3; ++mt) {
+            const int64_t T = b2s::round_up(b2s::ceil_div(M, mt), 16);
+            if (T > b2s::tcp_max_tokens() || b2s::ceil_div(M, T) != mt) continue;
+            const int64_t tiles = n_tiles * mt;
+            if (tiles < nsm) continue;
+            const int64_t cost = b2s::ceil_div(tiles, nsm) * (T + 64);
+            if (best < 0 || cost < best) {
+                best = cost;
+                t.T = t.bn_sub = (int)T;
+                t.nsub = 1;
+                t.m_tiles = (int)mt;
+                t.n_tiles = (int)n_tiles;
+                t.splits = 1;
+                p_grid = (int)(tiles < nsm ? tiles : nsm);
+            }
+        }
+    }
     b2s::TcGemmArgs a;
     memset(&a, 0, sizeof(a));
     int rc;
@@ -247,6 +272,7 @@ int run_tc(const b2s::I2sWeight& w0, const b2s::I2sWeight* w1, const int8_t* q, 
     a.splits = t.splits;
     a.mode = mode;
     a.epi = epi;
+    if (p_grid > 0) return launched(b2s::launch_gemm_i2s_tcp(a, p_grid, st), "gemm_i2s_tcp launch");
     return launched(b2s::launch_gemm_i2s_tc(a, st), "gemm_i2s_tc launch");
 }
 

@@ -74,6 +74,10 @@ struct TcGemmArgs {
     Epilogue epi;
 };
 cudaError_t launch_gemm_i2s_tc(const TcGemmArgs& args, cudaStream_t st);
+// Persistent variant (gemm_i2s_tcp.cu): `grid` CTAs walk the n_tiles x m_tiles tiles of T <= 224 tokens
+// (splits must be 1; tmap_q's box is 128 x T).
+int tcp_max_tokens();
+cudaError_t launch_gemm_i2s_tcp(const TcGemmArgs& args, int grid, cudaStream_t st);
 
 cudaError_t launch_repack_rows(const uint8_t* src, uint8_t* dst, int64_t N, int64_t K, cudaStream_t st);
 

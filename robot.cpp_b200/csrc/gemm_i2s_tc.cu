@@ -126,13 +126,20 @@ __host__ __device__ constexpr uint32_t umma_idesc_u8s8(int M, int N) {
     return (2u << 4) | (0u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 
+// Epilogue variants are compile-time (EPI bits: kEpiBias, kEpiGelu, kEpiResidual): with the optional steps
+// as runtime branches inside the unrolled store loop the epilogue's code no longer fits the instruction
+// cache and the store loop runs several times slower.
+constexpr int kEpiBias = 1, kEpiGelu = 2, kEpiResidual = 4;
+
+template <int MODE, int EPI>
 __global__ void __launch_bounds__(tc::kThreads, 1)
 gemm_i2s_tc_kernel(const __grid_constant__ CUtensorMap tmap_w0, const __grid_constant__ CUtensorMap tmap_w1,
                    const __grid_constant__ CUtensorMap tmap_q, const float* __restrict__ w0_scale,
                    const float* __restrict__ w1_scale, const float* __restrict__ s_act,
                    const int32_t* __restrict__ sum_act, float* y, int64_t ldy, int M, int N, int Kp,
-                   int T, int bn_sub, int nsub, int mode, const Epilogue epi) {
+                   int T, int bn_sub, int nsub, const Epilogue epi) {
     using namespace tc;
+    constexpr int mode = MODE;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* act_sm = base;
@@ -381,13 +388,14 @@ gemm_i2s_tc_kernel(const __grid_constant__ CUtensorMap tmap_w0, const __grid_con
         // Mode 0: the bias of this thread's output column is loaded once; residual values are fetched
         // for a whole chunk pair before the pair's accumulators are read (load_res), so their latency
         // is paid once per pair and overlaps the TMEM loads, not once per output.
-        const float bias_n = (mode == 0 && epi.bias && n < N) ? epi.bias[n] : 0.0f;
+        const float bias_n = ((EPI & kEpiBias) && n < N) ? epi.bias[n] : 0.0f;
         auto load_res = [&](int ch, float (&r)[16]) {
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
                 const int m = m0 + ch * 16 + j;
-                r[j] = (epi.residual && ch < nchunk && m < M && n < N) ? epi.residual[(int64_t)m * epi.ld_res + n]
-                                                                        : 0.0f;
+                r[j] = ((EPI & kEpiResidual) && ch < nchunk && m < M && n < N)
+                           ? epi.residual[(int64_t)m * epi.ld_res + n]
+                           : 0.0f;
             }
         };
         auto finish = [&](int ch, const int32_t (&raw)[16], const float (&res)[16]) {
@@ -398,9 +406,9 @@ gemm_i2s_tc_kernel(const __grid_constant__ CUtensorMap tmap_w0, const __grid_con
                     const int t = t0 + j, m = m0 + t;
                     float v = __fmul_rn((float)(raw[j] - sumq[t]), rfac[t]);
                     if (good && m < M && n < N) {
-                        if (epi.bias) v = __fadd_rn(v, bias_n);
-                        if (epi.act == 1) v = gelu_tanh(v);
-                        if (epi.residual) v = __fadd_rn(res[j], v);
+                        if (EPI & kEpiBias) v = __fadd_rn(v, bias_n);
+                        if (EPI & kEpiGelu) v = gelu_tanh(v);
+                        if (EPI & kEpiResidual) v = __fadd_rn(res[j], v);
                         y[(int64_t)m * ldy + n] = v;
                     }
                 }
@@ -468,11 +476,12 @@ gemm_i2s_tc_kernel(const __grid_constant__ CUtensorMap tmap_w0, const __grid_con
     }
 }
 
-cudaError_t launch_gemm_i2s_tc(const TcGemmArgs& a, cudaStream_t st) {
-    static bool attr_set = false;  // per process; the attribute is per function, device-independent
+template <int MODE, int EPI>
+static cudaError_t launch_variant(const TcGemmArgs& a, cudaStream_t st) {
+    static bool attr_set = false;  // per process and variant; the attribute is per function
+    auto kfn = gemm_i2s_tc_kernel<MODE, EPI>;
     if (!attr_set) {
-        cudaError_t e = cudaFuncSetAttribute(gemm_i2s_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)tc::kSmemBytes);
+        cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tc::kSmemBytes);
         if (e != cudaSuccess) return e;
         attr_set = true;
     }
@@ -490,8 +499,24 @@ cudaError_t launch_gemm_i2s_tc(const TcGemmArgs& a, cudaStream_t st) {
     attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 2;
-    return cudaLaunchKernelEx(&cfg, gemm_i2s_tc_kernel, a.tmap_w0, a.tmap_w1, a.tmap_q, a.w0_scale, a.w1_scale, a.s,
-                              a.sums, a.y, a.ldy, a.M, a.N, a.Kp, a.T, a.bn_sub, a.nsub, a.mode, a.epi);
+    return cudaLaunchKernelEx(&cfg, kfn, a.tmap_w0, a.tmap_w1, a.tmap_q, a.w0_scale, a.w1_scale, a.s, a.sums, a.y,
+                              a.ldy, a.M, a.N, a.Kp, a.T, a.bn_sub, a.nsub, a.epi);
+}
+
+cudaError_t launch_gemm_i2s_tc(const TcGemmArgs& a, cudaStream_t st) {
+    if (a.mode == 1) return launch_variant<1, 0>(a, st);
+    const int epi = (a.epi.bias ? kEpiBias : 0) | (a.epi.act == 1 ? kEpiGelu : 0) |
+                    (a.epi.residual ? kEpiResidual : 0);
+    switch (epi) {
+        case 0: return launch_variant<0, 0>(a, st);
+        case kEpiBias: return launch_variant<0, kEpiBias>(a, st);
+        case kEpiBias | kEpiGelu: return launch_variant<0, kEpiBias | kEpiGelu>(a, st);
+        case kEpiGelu: return launch_variant<0, kEpiGelu>(a, st);
+        case kEpiResidual: return launch_variant<0, kEpiResidual>(a, st);
+        case kEpiBias | kEpiResidual: return launch_variant<0, kEpiBias | kEpiResidual>(a, st);
+        case kEpiGelu | kEpiResidual: return launch_variant<0, kEpiGelu | kEpiResidual>(a, st);
+        default: return launch_variant<0, kEpiBias | kEpiGelu | kEpiResidual>(a, st);
+    }
 }
 
 }  // namespace b2s
