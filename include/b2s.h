@@ -179,12 +179,13 @@ int b2s_rope_neox(float *x, int64_t M, int n_heads, int head_dim, int64_t ld, fl
 /* Multi-head attention softmax(Q K^T * scale [+ causal mask]) V over M tokens, fp32, with n_heads query
  * heads sharing n_kv_heads key/value heads (GQA; n_heads % n_kv_heads == 0). Q/K/V/O rows hold the heads
  * side by side (head h at columns [h*head_dim, (h+1)*head_dim)). The ggml sequence mul_mat(K, Q) ->
- * soft_max_ext -> mul_mat(V, KQ) (src/models/smolvla/action_expert.cpp:771-774) as one fused kernel with a
- * fixed fp32 operation order: scores = fma-accumulated dot products (d ascending) times scale, the
- * b2s_soft_max_ext softmax, outputs = fma-accumulated sums over keys (ascending). Needs head_dim % 8 == 0,
- * head_dim <= 128, leading dimensions % 4 == 0, 16-byte aligned tensors and
- * 4 * (128 * head_dim + 64 * (roundup(M, 64) + 4)) <= 227 KB of shared memory (M <= 576 at head_dim 128);
- * B2S_ERR_UNSUPPORTED otherwise. */
+ * soft_max_ext -> mul_mat(V, KQ) (src/models/smolvla/action_expert.cpp:771-774) as one fused kernel with
+ * an online softmax over chunks of 64 keys (the evaluation order of ggml_flash_attn_ext, used by
+ * src/models/pi0/vlm.cpp) in a fixed fp32 operation order: scores are fma-accumulated dot products
+ * (d ascending) times scale; per chunk the running max, the rescale det_exp(m - m'), the chunk's
+ * probabilities and its sum (fixed butterfly order) update l and the fma-accumulated outputs; outputs are
+ * finally multiplied by 1/l. Needs head_dim % 8 == 0, head_dim <= 128, leading dimensions % 4 == 0 and
+ * 16-byte aligned tensors (B2S_ERR_UNSUPPORTED otherwise); any M. */
 int b2s_attention(const float *q, int64_t ldq, const float *k, int64_t ldk, const float *v, int64_t ldv, int64_t M,
                   int n_heads, int n_kv_heads, int head_dim, float scale, int causal, float *o, int64_t ldo,
                   void *stream);

@@ -189,10 +189,14 @@ void orc_rope_neox(float *x, int64_t M, int n_heads, int hd, int64_t ld, const f
 }
 
 /* Attention of `batch` sequences of T tokens: head h reads q columns [h hd, (h+1) hd) at q_off, its K/V
- * head g = h / (heads / kv_heads) at k_off / v_off. The fixed fp32 evaluation of the device kernel:
- *   S[i][j] = fp32(acc * scale), acc = fmaf(q[i][d], k[j][d], acc) over d ascending from +0;
- *   row i over keys j < n_i (i + 1 if causal, else T): e_j = orc_det_expf(S - max), sum in warp order,
- *   p_j = e_j * (1/sum); O[i][d] = acc, acc = fmaf(p_j, v[j][d], acc) over j ascending from +0. */
+ * head g = h / (heads / kv_heads) at k_off / v_off. The device kernel's fixed fp32 evaluation, an online
+ * softmax over chunks of 64 keys (chunk c = keys [64c, 64c + 64)); for row i with n_i keys (i + 1 if
+ * causal, else T):
+ *   s_j = fp32(acc * scale), acc = fmaf(q[i][d], k[j][d], acc) over d ascending from +0 (-inf if j >= n_i);
+ *   per chunk: m' = max(m, max s_j), alpha = orc_det_expf(m - m'), p_j = orc_det_expf(s_j - m'),
+ *   csum = xor butterfly (8, 4, 2, 1) over partials ((p_4t + p_4t+1) + p_4t+2) + p_4t+3, t = 0..15,
+ *   l = l * alpha + csum, o[d] = o[d] * alpha then o[d] = fmaf(p_j, v[j][d], o[d]) for j ascending;
+ *   out[d] = o[d] * (1 / l). Chunks past the row's last key change nothing, so they are skipped. */
 typedef struct {
     const float *qkv; int64_t ld, q_off, k_off, v_off; int batch, heads, kv_heads, hd, T, causal;
     float scale; float *o; int64_t ldo;
@@ -200,7 +204,7 @@ typedef struct {
 
 static void attn_range(void *p, int64_t i0, int64_t i1) {
     const attn_ctx *c = (const attn_ctx *)p;
-    float *S = (float *)malloc(sizeof(float) * (size_t)c->T);
+    float *acc = (float *)malloc(sizeof(float) * (size_t)c->hd);
     const int group = c->heads / c->kv_heads;
     for (int64_t it = i0; it < i1; ++it) {
         const int b = (int)(it / c->heads), h = (int)(it % c->heads), g = h / group;
@@ -208,28 +212,48 @@ static void attn_range(void *p, int64_t i0, int64_t i1) {
         for (int i = 0; i < c->T; ++i) {
             const float *qi = rows + (int64_t)i * c->ld + c->q_off + (int64_t)h * c->hd;
             const int nk = c->causal ? i + 1 : c->T;
-            float mx = -INFINITY;
-            for (int j = 0; j < nk; ++j) {
-                const float *kj = rows + (int64_t)j * c->ld + c->k_off + (int64_t)g * c->hd;
-                float acc = 0.0f;
-                for (int d = 0; d < c->hd; ++d) acc = fmaf(qi[d], kj[d], acc);
-                S[j] = acc * c->scale;
-                if (S[j] > mx) mx = S[j];
+            float m = -INFINITY, l = 0.0f;
+            for (int d = 0; d < c->hd; ++d) acc[d] = 0.0f;
+            for (int k0 = 0; k0 < nk; k0 += 64) {
+                float sc[64], pr[64];
+                float cm = -INFINITY;
+                for (int jj = 0; jj < 64; ++jj) {
+                    const int j = k0 + jj;
+                    if (j < nk) {
+                        const float *kj = rows + (int64_t)j * c->ld + c->k_off + (int64_t)g * c->hd;
+                        float a = 0.0f;
+                        for (int d = 0; d < c->hd; ++d) a = fmaf(qi[d], kj[d], a);
+                        sc[jj] = a * c->scale;
+                    } else {
+                        sc[jj] = -INFINITY;
+                    }
+                    if (sc[jj] > cm) cm = sc[jj];
+                }
+                const float mn = (m > cm) ? m : cm;
+                const float alpha = orc_det_expf(m - mn);
+                float part[16], nxt[16];
+                for (int jj = 0; jj < 64; ++jj) pr[jj] = orc_det_expf(sc[jj] - mn);
+                for (int tq = 0; tq < 16; ++tq) part[tq] = ((pr[4 * tq] + pr[4 * tq + 1]) + pr[4 * tq + 2]) + pr[4 * tq + 3];
+                for (int off = 8; off > 0; off >>= 1) {
+                    for (int tq = 0; tq < 16; ++tq) nxt[tq] = part[tq] + part[tq ^ off];
+                    memcpy(part, nxt, sizeof part);
+                }
+                l = l * alpha + part[0];
+                m = mn;
+                const int jn = (nk - k0 < 64) ? nk - k0 : 64;
+                for (int d = 0; d < c->hd; ++d) {
+                    float a = acc[d] * alpha;
+                    for (int jj = 0; jj < jn; ++jj)
+                        a = fmaf(pr[jj], rows[(int64_t)(k0 + jj) * c->ld + c->v_off + (int64_t)g * c->hd + d], a);
+                    acc[d] = a;
+                }
             }
-            for (int j = 0; j < nk; ++j) S[j] = orc_det_expf(S[j] - mx);
-            const float sum = orc_warp_order_sum(S, nk);
-            const float inv = (sum > 0.0f) ? 1.0f / sum : 0.0f;
-            for (int j = 0; j < nk; ++j) S[j] = S[j] * inv;
+            const float inv = (l > 0.0f) ? 1.0f / l : 0.0f;
             float *oi = c->o + ((int64_t)b * c->T + i) * c->ldo + (int64_t)h * c->hd;
-            for (int d = 0; d < c->hd; ++d) {
-                float acc = 0.0f;
-                for (int j = 0; j < nk; ++j)
-                    acc = fmaf(S[j], rows[(int64_t)j * c->ld + c->v_off + (int64_t)g * c->hd + d], acc);
-                oi[d] = acc;
-            }
+            for (int d = 0; d < c->hd; ++d) oi[d] = acc[d] * inv;
         }
     }
-    free(S);
+    free(acc);
 }
 
 void orc_attention(const float *qkv, int64_t ld, int64_t q_off, int64_t k_off, int64_t v_off, int batch, int heads,

@@ -639,8 +639,8 @@ int b2s_attention(const float* q, int64_t ldq, const float* k, int64_t ldk, cons
         return fail(B2S_ERR_INVALID_ARG, "attention: leading dimensions too small");
     if (!b2s::attention_supported((int)M, head_dim, ldq, ldk, ldv, ldo, q, k, v, o))
         return fail(B2S_ERR_UNSUPPORTED,
-                    "attention: needs head_dim %% 8 == 0 and <= 128, leading dimensions %% 4 == 0, 16-byte aligned "
-                    "tensors and (64 + roundup(M,64) + 4) x 256 + 512 x head_dim bytes of shared memory <= 227 KB");
+                    "attention: needs head_dim %% 8 == 0 and <= 128, leading dimensions %% 4 == 0 and 16-byte "
+                    "aligned tensors");
     return launched(b2s::launch_attention(q, ldq, k, ldk, v, ldv, 1, (int)M, n_heads, n_kv_heads, head_dim, scale,
                                           causal != 0, o, ldo, static_cast<cudaStream_t>(stream)),
                     "attention");

@@ -8,7 +8,7 @@
 //   * rope kernels: ggml_rope_ext in NEOX mode (src/models/pi0/vlm.cpp:223-235): for position p and
 //     pair (i, i + d/2), theta = p * base^(-2i/d), (x0, x1) -> (x0 cos - x1 sin, x0 sin + x1 cos); the
 //     angles in double, either per element or from a per-model table.
-//   * attention: one fused fp32 kernel per (query block, head, sequence) -- scores, softmax, P V -- the
+//   * attention: one fused fp32 kernel per (query block, head, sequence) -- scores, online softmax, P V -- the
 //     ggml graph mul_mat(K, Q) -> soft_max_ext -> mul_mat(V, KQ) of
 //     src/models/smolvla/action_expert.cpp:771-774, with grouped K/V heads (GQA) as in
 //     src/models/pi0/vlm.cpp:223-235, in a fixed operation order the CPU oracle repeats bit for bit.
@@ -316,39 +316,43 @@ cudaError_t launch_embed_tokens(const int32_t* tokens, int n, int D, uint32_t se
 
 // ------------------------------------------------------------------------------------------------ attention
 // softmax(Q K^T * scale [+ causal mask]) V for `batch` sequences of T tokens (sequence b at rows
-// [b T, (b+1) T) of every operand), one CTA per (64-query block, head, sequence). fp32 throughout, in a
-// fixed operation order that the CPU oracle repeats exactly:
-//   S[i][j] = fp32(acc * scale), acc = fma(q[i][d], k[j][d], acc) over d = 0..hd-1 from +0;
-//   softmax of row i over its keys j < n_i (n_i = i + 1 causal, else T): m = max, e_j = det_expf(S - m),
-//   sum over lanes (lane l adds e_j, j = l mod 32, in increasing j, then an xor butterfly),
-//   p_j = e_j * (1 / sum);
-//   O[i][d] = acc, acc = fma(p_j, v[j][d], acc) over j = 0..n_i-1 from +0 (keys past n_i within the
-//   block's key range enter with p = 0, which leaves a finite sum unchanged).
+// [b T, (b+1) T) of every operand), one CTA per (64-query block, head, sequence), two CTAs per SM.
+// Keys are visited in chunks of 64 (chunk c = keys [64c, 64c + 64)) with an online softmax, in a fixed
+// fp32 operation order that the CPU oracle repeats exactly. For query row i (n_i = i + 1 keys if causal,
+// else T; keys j >= n_i count as masked):
+//   s_j  = fp32(acc * scale), acc = fma(q[i][d], k[j][d], acc) over d = 0..hd-1 from +0; masked: -inf
+//   per chunk: m' = max(m, max_j s_j);  alpha = det_expf(m - m');  p_j = det_expf(s_j - m')
+//              csum = xor-butterfly (offsets 8, 4, 2, 1) over the 16 partial sums
+//                     ((p_4t + p_4t+1) + p_4t+2) + p_4t+3, t = 0..15
+//              l = l * alpha + csum;  o[d] = o[d] * alpha, then o[d] = fma(p_j, v[j][d], o[d]) for the
+//              chunk's keys in ascending order
+//   (m starts at -inf, l and o at +0); finally out[d] = o[d] * (1 / l). A chunk where the row has no
+// key leaves l and o unchanged (alpha = 1, p = 0), so each row's result depends only on its own keys.
 // Query head h reads K/V head h / (heads / kv_heads) (GQA). Shared memory: Q^T [hd][64], one K^T or V
-// chunk [64 keys][hd], the score block [64][Tp]; hd % 8 == 0, hd <= 128.
-constexpr int kAtQ = 64, kAtThreads = 256;
+// chunk, the 64 x 64 probability tile and per-row factors; hd % 8 == 0, hd <= 128.
+constexpr int kAtQ = 64, kAtThreads = 256, kAtPP = kAtQ + 4;  // P row stride (floats)
 
-__host__ __device__ inline int attention_tp(int T) { return (int)round_up(T, 64) + 4; }
-size_t attention_smem_bytes(int T, int hd) {
-    return sizeof(float) * ((size_t)hd * kAtQ * 2 + (size_t)kAtQ * attention_tp(T));
+size_t attention_smem_bytes(int /*T*/, int hd) {
+    return sizeof(float) * ((size_t)hd * kAtQ * 2 + (size_t)kAtQ * kAtPP + 2 * kAtQ);
 }
 
-__global__ void __launch_bounds__(kAtThreads)
+__global__ void __launch_bounds__(kAtThreads, 2)
 attention_kernel(const float* __restrict__ q, int64_t ldq, const float* __restrict__ k, int64_t ldk,
                  const float* __restrict__ v, int64_t ldv, float* __restrict__ o, int64_t ldo, int T, int heads,
                  int kv_heads, int hd, float scale, int causal) {
     extern __shared__ __align__(16) float at_sm[];
-    const int Tp = attention_tp(T);
-    float* Qt = at_sm;             // [hd][64]
-    float* KV = Qt + hd * kAtQ;    // K^T chunk [hd][64] or V chunk [64][hd]
-    float* S = KV + hd * kAtQ;     // [64][Tp]
+    float* Qt = at_sm;                 // [hd][64]
+    float* KV = Qt + hd * kAtQ;        // K^T chunk [hd][64] or V chunk [64][hd]
+    float* P = KV + hd * kAtQ;         // [64][kAtPP] probabilities of the chunk
+    float* alpha_sm = P + kAtQ * kAtPP;   // [64] per-row rescale of the chunk
+    float* inv_sm = alpha_sm + kAtQ;      // [64] 1 / l at the end
     const int h = blockIdx.y, g = h / (heads / kv_heads);
     const int q0 = blockIdx.x * kAtQ;
     const int64_t row0 = (int64_t)blockIdx.z * T;
     const float* qh = q + row0 * ldq + (int64_t)h * hd;
     const float* kh = k + row0 * ldk + (int64_t)g * hd;
     const float* vh = v + row0 * ldv + (int64_t)g * hd;
-    const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+    const int t = threadIdx.x;
     const int hd4 = hd / 4;
     griddep_wait();  // q/k/v are written by the preceding kernel
     griddep_launch();
@@ -365,11 +369,28 @@ attention_kernel(const float* __restrict__ q, int64_t ldq, const float* __restri
     const int kend = causal ? min(T, q0 + kAtQ) : T;  // keys any query of this block can see
     const int nchunks = (kend + kAtQ - 1) / kAtQ;
 
-    // ---- scores
+    // score threads: rows 4 ty .. 4 ty + 3, keys 4 tx .. 4 tx + 3 of the chunk (the 16 tx of a row are
+    // 16 consecutive lanes of one warp)
     const int ty = t / 16, tx = t % 16;
+    float m_r[4], l_r[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        m_r[i] = -INFINITY;
+        l_r[i] = 0.0f;
+    }
+    // output threads: rows 4 rg .. 4 rg + 3, columns 8 cg .. 8 cg + 7
+    const int ncg = hd / 8;
+    const bool active = t < 16 * ncg;
+    const int rg = active ? t / ncg : 0, cg = active ? t % ncg : 0;
+    float acc[4][8];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[i][j] = 0.0f;
+
     for (int c = 0; c < nchunks; ++c) {
         const int k0 = c * kAtQ;
-        __syncthreads();  // Qt written / previous chunk consumed
+        __syncthreads();  // Qt written; the previous chunk's V and P reads are done
         for (int e = t; e < kAtQ * hd4; e += kAtThreads) {
             const int j = e % kAtQ, d4 = 4 * (e / kAtQ);
             float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -380,11 +401,11 @@ attention_kernel(const float* __restrict__ q, int64_t ldq, const float* __restri
             KV[(d4 + 3) * kAtQ + j] = x.w;
         }
         __syncthreads();
-        float acc[4][4];
+        float sc[4][4];
 #pragma unroll
         for (int i = 0; i < 4; ++i)
 #pragma unroll
-            for (int j = 0; j < 4; ++j) acc[i][j] = 0.0f;
+            for (int j = 0; j < 4; ++j) sc[i][j] = 0.0f;
 #pragma unroll 4
         for (int d = 0; d < hd; ++d) {
             const float4 a = *reinterpret_cast<const float4*>(&Qt[d * kAtQ + 4 * ty]);
@@ -393,54 +414,37 @@ attention_kernel(const float* __restrict__ q, int64_t ldq, const float* __restri
 #pragma unroll
             for (int i = 0; i < 4; ++i)
 #pragma unroll
-                for (int j = 0; j < 4; ++j) acc[i][j] = __fmaf_rn(av[i], bv[j], acc[i][j]);
+                for (int j = 0; j < 4; ++j) sc[i][j] = __fmaf_rn(av[i], bv[j], sc[i][j]);
         }
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
             const int row = 4 * ty + i, qi = q0 + row;
-            float4 l;
-            float* lv = reinterpret_cast<float*>(&l);
+            const int nk = (qi < T) ? (causal ? qi + 1 : T) : 0;
+            float cm = -INFINITY;
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
                 const int key = k0 + 4 * tx + j;
-                lv[j] = (key >= T || (causal && key > qi)) ? -INFINITY : __fmul_rn(acc[i][j], scale);
+                sc[i][j] = (key < nk) ? __fmul_rn(sc[i][j], scale) : -INFINITY;
+                cm = fmaxf(cm, sc[i][j]);
             }
-            *reinterpret_cast<float4*>(&S[row * Tp + k0 + 4 * tx]) = l;
-        }
-    }
-    __syncthreads();
-
-    // ---- softmax rows (one warp per row)
-    for (int row = warp; row < kAtQ; row += kAtThreads / 32) {
-        const int qi = q0 + row;
-        float* sr = S + row * Tp;
-        const int nk = (qi < T) ? (causal ? qi + 1 : T) : 0;
-        float mx = -INFINITY;
-        for (int j = lane; j < nk; j += 32) mx = fmaxf(mx, sr[j]);
-        mx = warp_max(mx);
-        float sum = 0.0f;
-        for (int j = lane; j < nk; j += 32) {
-            const float e = det_expf(__fsub_rn(sr[j], mx));
-            sr[j] = e;
-            sum = __fadd_rn(sum, e);
-        }
-        sum = warp_sum_f(sum);
-        const float inv = (sum > 0.0f) ? __fdiv_rn(1.0f, sum) : 0.0f;
-        for (int j = lane; j < kend; j += 32) sr[j] = (j < nk) ? __fmul_rn(sr[j], inv) : 0.0f;
-    }
-
-    // ---- O = P V: thread item (row group rg of 4 rows, column group cg of 8)
-    const int ncg = hd / 8;
-    const bool active = t < 16 * ncg;
-    const int rg = active ? t / ncg : 0, cg = active ? t % ncg : 0;
-    float acc[4][8];
 #pragma unroll
-    for (int i = 0; i < 4; ++i)
+            for (int off = 8; off > 0; off >>= 1) cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, off));
+            const float mn = fmaxf(m_r[i], cm);
+            const float alpha = det_expf(__fsub_rn(m_r[i], mn));
+            float4 pv;
+            pv.x = det_expf(__fsub_rn(sc[i][0], mn));
+            pv.y = det_expf(__fsub_rn(sc[i][1], mn));
+            pv.z = det_expf(__fsub_rn(sc[i][2], mn));
+            pv.w = det_expf(__fsub_rn(sc[i][3], mn));
+            float part = __fadd_rn(__fadd_rn(__fadd_rn(pv.x, pv.y), pv.z), pv.w);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) acc[i][j] = 0.0f;
-    for (int c = 0; c < nchunks; ++c) {
-        const int k0 = c * kAtQ;
-        __syncthreads();  // scores finished / previous V chunk consumed
+            for (int off = 8; off > 0; off >>= 1) part = __fadd_rn(part, __shfl_xor_sync(0xffffffffu, part, off));
+            l_r[i] = __fadd_rn(__fmul_rn(l_r[i], alpha), part);
+            m_r[i] = mn;
+            *reinterpret_cast<float4*>(&P[row * kAtPP + 4 * tx]) = pv;
+            if (tx == 0) alpha_sm[row] = alpha;
+        }
+        __syncthreads();  // P and alpha written; K^T chunk consumed
         for (int e = t; e < kAtQ * hd4; e += kAtThreads) {
             const int j = e / hd4, d4 = 4 * (e % hd4);
             float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -449,6 +453,12 @@ attention_kernel(const float* __restrict__ q, int64_t ldq, const float* __restri
         }
         __syncthreads();
         if (active) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const float al = alpha_sm[4 * rg + i];
+#pragma unroll
+                for (int j = 0; j < 8; ++j) acc[i][j] = __fmul_rn(acc[i][j], al);
+            }
             const int jn = min(kAtQ, kend - k0);
             for (int jj = 0; jj < jn; ++jj) {
                 const float4 v0 = *reinterpret_cast<const float4*>(&KV[jj * hd + 8 * cg]);
@@ -456,21 +466,29 @@ attention_kernel(const float* __restrict__ q, int64_t ldq, const float* __restri
                 const float vv[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
 #pragma unroll
                 for (int i = 0; i < 4; ++i) {
-                    const float p = S[(4 * rg + i) * Tp + k0 + jj];
+                    const float pr = P[(4 * rg + i) * kAtPP + jj];
 #pragma unroll
-                    for (int j = 0; j < 8; ++j) acc[i][j] = __fmaf_rn(p, vv[j], acc[i][j]);
+                    for (int j = 0; j < 8; ++j) acc[i][j] = __fmaf_rn(pr, vv[j], acc[i][j]);
                 }
             }
         }
     }
+    if (tx == 0) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) inv_sm[4 * ty + i] = (l_r[i] > 0.0f) ? __fdiv_rn(1.0f, l_r[i]) : 0.0f;
+    }
+    __syncthreads();
     if (active) {
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
             const int qi = q0 + 4 * rg + i;
             if (qi >= T) continue;
+            const float inv = inv_sm[4 * rg + i];
             float* orow = o + (row0 + qi) * ldo + (int64_t)h * hd + 8 * cg;
-            *reinterpret_cast<float4*>(orow) = make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
-            *reinterpret_cast<float4*>(orow + 4) = make_float4(acc[i][4], acc[i][5], acc[i][6], acc[i][7]);
+            *reinterpret_cast<float4*>(orow) = make_float4(__fmul_rn(acc[i][0], inv), __fmul_rn(acc[i][1], inv),
+                                                           __fmul_rn(acc[i][2], inv), __fmul_rn(acc[i][3], inv));
+            *reinterpret_cast<float4*>(orow + 4) = make_float4(__fmul_rn(acc[i][4], inv), __fmul_rn(acc[i][5], inv),
+                                                               __fmul_rn(acc[i][6], inv), __fmul_rn(acc[i][7], inv));
         }
     }
 }
