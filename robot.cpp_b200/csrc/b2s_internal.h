@@ -25,6 +25,13 @@ struct Q8Act {
     int64_t M, K, ldq;
 };
 
+// Register-resident norm / act-quant of rows of K <= 8192 (act_quant.cu); kind 0 RMSNorm, 1 LayerNorm,
+// 2 no norm (quant only). rowq_eligible: K % 4 == 0, 16-byte aligned rows and parameters.
+bool rowq_eligible(const float* x, int64_t ldx, const float* g, const float* b, int64_t K, const void* out,
+                   int64_t ldo, bool quant);
+cudaError_t launch_rowq(int kind, bool quant, const float* x, int64_t ldx, const float* g, const float* b, float eps,
+                        int64_t M, int64_t K, float* y, int64_t ldy, int8_t* q, int64_t ldq, float* s, int32_t* sums,
+                        cudaStream_t st);
 cudaError_t launch_act_quant(const float* x, int64_t ldx, const float* g, bool norm, float eps, int64_t M, int64_t K,
                              int8_t* q, int64_t ldq, float* s, int32_t* sums, cudaStream_t st);
 

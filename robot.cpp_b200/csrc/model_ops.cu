@@ -136,6 +136,9 @@ cudaError_t launch_norm(int kind, bool quant, const float* x, int64_t ldx, const
                         int64_t M, int64_t K, float* y, int64_t ldy, int8_t* q, int64_t ldq, float* s, int32_t* sums,
                         cudaStream_t st) {
     if (M <= 0) return cudaSuccess;
+    if (rowq_eligible(x, ldx, g, b, K, quant ? static_cast<const void*>(q) : static_cast<const void*>(y),
+                      quant ? ldq : ldy, quant))
+        return launch_rowq(kind, quant, x, ldx, g, b, eps, M, K, y, ldy, q, ldq, s, sums, st);
     const dim3 grid((unsigned)M), block(kNormThreads);
     const int k = (int)K;
     if (kind == 0) {
