@@ -577,7 +577,8 @@ def run_sweep(a, world, rank, local):
     import b2s
     from b2s import workloads as wl
 
-    if rank != 0:
+    if world > 1:
+        run_sweep_nsplit(a, world, rank, local)
         return
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
@@ -655,6 +656,82 @@ def run_sweep(a, world, rank, local):
                        "peaks": f"{pk_kind}: HBM {hbm} GB/s, int8 = 2x bf16 burst {tensor_peak:.0f} TOP/s"},
             "sweep": rows}
     print(json.dumps(line), flush=True)
+
+
+def run_sweep_nsplit(a, world, rank, local):
+    """M = 16384 N-split over the ranks: rank r owns weight rows [n0_r, n1_r) and its GEMM epilogue stores
+    its column slice straight into rank 0's output buffer over NVLink (CUDA IPC mapping, plain peer
+    stores). Timing: max over ranks of `launches` back-to-back GEMMs. Roofline of the fused GEMM+gather:
+    the slower of (ops / int8 peak) and (bytes crossing into rank 0 / measured 770 GB/s per direction)."""
+    import datetime
+    import torch
+    import torch.distributed as dist
+    import b2s
+    from b2s import workloads as wl
+    from b2s.nsplit import PeerBuffer, row_ranges, nsplit_mul_mat_q8, shard_i2s_rows
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    b2s.check(b2s.lib().b2s_device_check())
+    pk, pk_kind = peaks()
+    tensor_peak = 2.0 * pk.get("bf16_tflops", 1590.0)
+    link_gbs = 770.0
+    M = 16384
+    stream = torch.cuda.Stream(device=dev)
+    rows = []
+    for K, N in wl.SWEEP_KN:
+        g = wl.rng(K + N)
+        w = wl.weight(g, N, K)
+        n0, n1 = row_ranges(N, world)[rank]
+        shard = torch.from_numpy(shard_i2s_rows(w.packed, N, K, n0, n1)).to(dev)
+        W = b2s.i2s_tensor(shard, n1 - n0, K)
+        ldq = (K + 15) // 16 * 16
+        gq = torch.Generator(device=dev)
+        gq.manual_seed(K * 7 + N)
+        q = torch.randint(-127, 128, (M, ldq), dtype=torch.int8, device=dev, generator=gq)[:, :K]
+        sc = torch.rand(M, device=dev, generator=gq) + 0.5
+        u = q.to(torch.int32).sum(dim=1).to(torch.int32)
+        yb = PeerBuffer(M * N * 4)
+        launches = 8
+        with torch.cuda.stream(stream):
+            for _ in range(2):
+                nsplit_mul_mat_q8(b2s, W, q, sc, u, M, yb.ptr, N, n0, stream=stream)
+        stream.synchronize()
+        dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            e0.record(stream)
+            for _ in range(launches):
+                nsplit_mul_mat_q8(b2s, W, q, sc, u, M, yb.ptr, N, n0, stream=stream)
+            e1.record(stream)
+        stream.synchronize()
+        dist.barrier()
+        t = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        assert b2s.device_error() == 0
+        us = float(t[0]) * 1e3 / launches
+        ops = 2.0 * M * N * K
+        cross = 4.0 * M * (N - (row_ranges(N, world)[0][1]))  # fp32 output columns stored into rank 0 by peers
+        t_roof = max(ops / (tensor_peak * 1e12) * 1e6, cross / (link_gbs * 1e9) * 1e6)
+        rows.append({"M": M, "K": K, "N": N, "gpus": world, "us": round(us, 2), "TOP/s": round(ops / us / 1e6, 1),
+                     "nvlink_bytes_into_root": int(cross), "roofline_us": round(t_roof, 2),
+                     "frac": round(t_roof / us, 4),
+                     "bound": "nvlink" if cross / (link_gbs * 1e9) > ops / (tensor_peak * 1e12) else "tensor"})
+        dist.barrier()
+        yb.close()
+        del q, sc, u, shard
+    dist.destroy_process_group()
+    if rank == 0:
+        line = {"metric": METRIC, "value": round(sum(r["TOP/s"] for r in rows) / len(rows), 1),
+                "unit": "TOP/s (mean over shapes, whole job)", "n_gpus": world, "steps": 8, "warmup": 2,
+                "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8xternary->int32",
+                "data": "synthetic", "config": {"workload": "i2s_gemm_nsplit_m16384",
+                                                "parallelism": f"N-split over {world} GPUs, output gathered "
+                                                               "into rank 0 by epilogue peer stores"},
+                "sweep": rows}
+        print(json.dumps(line), flush=True)
 
 
 def main():
