@@ -22,7 +22,7 @@
 namespace b2s {
 
 constexpr int kGemvRows = 16;   // rows per CTA
-constexpr int kGemvWarps = 4;   // warps per CTA (split K)
+constexpr int kGemvWarps = 8;   // warps per CTA (split K)
 constexpr int kGemvUnroll = 8;  // 16-byte loads in flight per lane
 
 __device__ __forceinline__ uint4 ld_stream_v4(const void* p) {
@@ -32,6 +32,14 @@ __device__ __forceinline__ uint4 ld_stream_v4(const void* p) {
                  : "l"(p));
     return v;
 }
+// 16-byte asynchronous global -> shared copy; bytes past src_bytes (0..16) are zero-filled.
+__device__ __forceinline__ void cp_async_16(void* smem_dst, const void* src, uint32_t src_bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(smem_dst)), "l"(src),
+                 "r"(src_bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
 __device__ __forceinline__ int dp4a_us(uint32_t a, int b, int c) {
     int d;
     asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
@@ -65,24 +73,36 @@ gemv_i2s_kernel(const uint8_t* __restrict__ codes, const float* __restrict__ wsc
     griddep_launch();  // the next kernel may start streaming its own weights now
     griddep_wait();    // activations are produced by the preceding kernel
 
-    // Stage q (MT rows of K int8) into shared memory, zero-filling [K, Kp).
+    // Stage q (MT rows of K int8) into shared memory, zero-filling [K, Kp) and token rows past M. With a
+    // 16-byte aligned q and 4+ tokens every chunk is one cp.async, all in flight at once (a loop of
+    // load -> store round trips serialized 20 L2 latencies per thread at 16 tokens); otherwise plain
+    // 16-byte loads, or a byte-wise copy for unaligned q.
     const int cpr = Kp / 16;  // 16-byte chunks per token row
-    const bool q_vec = ((ldq & 15) == 0) && ((reinterpret_cast<uintptr_t>(q) & 15) == 0);
-    for (int i = threadIdx.x; i < MT * cpr; i += blockDim.x) {
-        const int m = i / cpr, c = i - m * cpr, k0 = c * 16;
-        uint4 v = make_uint4(0, 0, 0, 0);
-        const int8_t* src = q + (int64_t)m * ldq + k0;
-        if (m >= mrows) {
-            // token rows beyond M stay zero (their outputs are not stored)
-        } else if (q_vec && k0 + 16 <= K) {
-            v = *reinterpret_cast<const uint4*>(src);
-        } else {
-            uint8_t tmp[16];
-#pragma unroll
-            for (int j = 0; j < 16; ++j) tmp[j] = (k0 + j < K) ? (uint8_t)src[j] : 0;
-            v = *reinterpret_cast<uint4*>(tmp);
+    const bool q_vec = ((ldq & 15) == 0) && ((reinterpret_cast<uintptr_t>(q) & 15) == 0) && (K % 16 == 0);
+    if (q_vec && MT < 4) {  // a few chunks per thread: plain 16-byte loads
+        for (int i = threadIdx.x; i < MT * cpr; i += blockDim.x) {
+            const int m = i / cpr, k0 = (i - m * cpr) * 16;
+            uint4 v = make_uint4(0, 0, 0, 0);
+            if (m < mrows && k0 < K) v = *reinterpret_cast<const uint4*>(q + (int64_t)m * ldq + k0);
+            reinterpret_cast<uint4*>(q_sm)[i] = v;
         }
-        reinterpret_cast<uint4*>(q_sm)[i] = v;
+    } else if (q_vec) {
+        for (int i = threadIdx.x; i < MT * cpr; i += blockDim.x) {
+            const int m = i / cpr, k0 = (i - m * cpr) * 16;
+            const bool live = m < mrows && k0 < K;
+            cp_async_16(q_sm + 16 * i, live ? (const void*)(q + (int64_t)m * ldq + k0) : (const void*)q,
+                        live ? 16u : 0u);
+        }
+        cp_async_wait_all();
+    } else {
+        for (int i = threadIdx.x; i < MT * cpr; i += blockDim.x) {
+            const int m = i / cpr, k0 = (i - m * cpr) * 16;
+            uint8_t tmp[16];
+            const int8_t* src = q + (int64_t)m * ldq + k0;
+#pragma unroll
+            for (int j = 0; j < 16; ++j) tmp[j] = (m < mrows && k0 + j < K) ? (uint8_t)src[j] : 0;
+            reinterpret_cast<uint4*>(q_sm)[i] = *reinterpret_cast<uint4*>(tmp);
+        }
     }
     __syncthreads();
 
