@@ -73,6 +73,15 @@ uint32_t b2s_bitvla_param_bits(uint32_t seed, uint32_t tensor, uint32_t idx);
 int b2s_bitvla_create(const b2s_bitvla_config *cfg, uint32_t seed, int max_batch, b2s_bitvla **out);
 void b2s_bitvla_free(b2s_bitvla *m);
 
+/* Builds the model from a GGUF file (general.architecture "bitvla"; the shape from the bitvla.* keys,
+ * the text-embedding seed from bitvla.token_embd.seed; ternary weights as I2_S tensors, type 36, in the
+ * flattened i2_s layout with the fp32 scale in the 32-byte trailer; everything else F32). The tensor names
+ * and keys are the ones robot.cpp_b200/b2s/gguf.py writes. This mirrors gguf_loader::load ->
+ * parse_metadata -> bind_tensors (src/models/gguf_loader.cpp:9-162): i2_s bytes reach the device
+ * unchanged and are repacked to padded rows there. A file written from seed S loads into the same model
+ * as b2s_bitvla_create(..., S, ...). */
+int b2s_bitvla_create_from_gguf(const char *path, int max_batch, b2s_bitvla **out);
+
 /* Device bytes held by the packed ternary weights / by all weights / by activation buffers. */
 size_t b2s_bitvla_ternary_bytes(const b2s_bitvla *m);
 size_t b2s_bitvla_weight_bytes(const b2s_bitvla *m);

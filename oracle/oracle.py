@@ -294,6 +294,12 @@ def bv_ternary_rowpadded(rows: int, K: int, seed: int, tensor: int) -> np.ndarra
     return out
 
 
+def bv_uniform(n: int, seed: int, tensor: int, lo: float, hi: float) -> np.ndarray:
+    out = np.zeros(n, np.float32)
+    lib().orc_bv_gen_uniform(out, n, seed, tensor, float(lo), float(hi))
+    return out
+
+
 def bv_ternary_scale(seed: int, tensor: int, K: int) -> float:
     return float(lib().orc_bv_ternary_scale(seed, tensor, K))
 

@@ -42,6 +42,7 @@ def _bind():
         "b2s_bitvla_activation_bytes": (C.c_size_t, [vp]),
         "b2s_bitvla_forward": (C.c_int, [vp, C.c_int, vp, vp, vp, vp, vp]),
         "b2s_bitvla_predict": (C.c_int, [vp, C.c_int, vp, vp, vp, vp]),
+        "b2s_bitvla_create_from_gguf": (C.c_int, [C.c_char_p, C.c_int, C.POINTER(vp)]),
     }
     for name, (res, args) in sig.items():
         f = getattr(L, name)
@@ -53,7 +54,7 @@ def _bind():
 
 EXPORTED = ["b2s_bitvla_default_config", "b2s_bitvla_seq_len", "b2s_bitvla_ternary_ops", "b2s_bitvla_param_bits",
             "b2s_bitvla_create", "b2s_bitvla_free", "b2s_bitvla_ternary_bytes", "b2s_bitvla_weight_bytes",
-            "b2s_bitvla_activation_bytes", "b2s_bitvla_forward", "b2s_bitvla_predict"]
+            "b2s_bitvla_activation_bytes", "b2s_bitvla_forward", "b2s_bitvla_predict", "b2s_bitvla_create_from_gguf"]
 
 
 def default_config(**over) -> Config:
@@ -79,13 +80,22 @@ def param_bits(seed: int, tensor: int, idx: int) -> int:
 class Model:
     """A BitVLA-shape model on the current CUDA device."""
 
-    def __init__(self, cfg: Config, seed: int, max_batch: int = 1):
+    def __init__(self, cfg: Config, seed: int, max_batch: int = 1, gguf_path: str | None = None):
+        """Random-init model from `seed`, or (gguf_path) the model stored in a GGUF file; for a file the
+        shape comes from its metadata and `cfg`/`seed` are only recorded."""
         L = _bind()
-        self.cfg = cfg
-        self.seed = seed
         self.max_batch = max_batch
         h = C.c_void_p()
-        check(L.b2s_bitvla_create(C.byref(cfg), seed & 0xFFFFFFFF, max_batch, C.byref(h)))
+        if gguf_path is not None:
+            check(L.b2s_bitvla_create_from_gguf(gguf_path.encode(), max_batch, C.byref(h)))
+            from .gguf import GgufFile
+            kv = GgufFile(gguf_path).kv
+            cfg = default_config(vit_layers=kv["bitvla.vision.block_count"], dec_layers=kv["bitvla.block_count"])
+            seed = kv["bitvla.token_embd.seed"]
+        else:
+            check(L.b2s_bitvla_create(C.byref(cfg), seed & 0xFFFFFFFF, max_batch, C.byref(h)))
+        self.cfg = cfg
+        self.seed = seed
         self._h = h
 
     def close(self) -> None:

@@ -2,6 +2,8 @@
 #pragma once
 
 #include <cstdint>
+#include <map>
+#include <string>
 #include <cuda.h>
 #include <cuda_runtime.h>
 
@@ -121,6 +123,43 @@ int dispatch_mul_mat_q8(const I2sWeight& w, const int8_t* q, int64_t ldq, const 
 // FFN gate/up with the squared-ReLU product: p = relu(Wg q)^2 * (Wu q) (tensor cores, mode 1).
 int dispatch_gate_up(const I2sWeight& wg, const I2sWeight& wu, const int8_t* q, int64_t ldq, const float* s,
                      const int32_t* sums, int64_t M, float* p, int64_t ldp, cudaStream_t st);
+
+// Read-only GGUF container (gguf_file.cu): memory-mapped, metadata parsed, tensors indexed by name.
+struct GgufValue {
+    uint32_t type = 0;
+    uint8_t raw[8] = {};
+    std::string s;
+    uint32_t arr_type = 0;
+    uint64_t arr_n = 0;
+    const void* arr = nullptr;
+};
+struct GgufTensor {
+    int64_t ne[4] = {1, 1, 1, 1};
+    uint32_t type = 0;  // ggml type id (0 F32, 36 I2_S)
+    uint64_t offset = 0;
+    size_t nbytes = 0;
+    const uint8_t* data = nullptr;
+};
+class GgufFile {
+  public:
+    GgufFile() = default;
+    GgufFile(const GgufFile&) = delete;
+    GgufFile& operator=(const GgufFile&) = delete;
+    ~GgufFile();
+    bool open(const char* path, std::string* err);
+    void close();
+    const GgufTensor* tensor(const std::string& name) const;
+    bool u32(const std::string& key, uint32_t* out) const;
+    bool f32(const std::string& key, float* out) const;
+    bool str(const std::string& key, std::string* out) const;
+    size_t n_tensors() const { return tensors_.size(); }
+
+  private:
+    const void* map_ = nullptr;
+    size_t size_ = 0;
+    std::map<std::string, GgufValue> kv_;
+    std::map<std::string, GgufTensor> tensors_;
+};
 
 // Records `msg` as the calling thread's b2s_last_error() and returns `code`.
 int set_last_error(int code, const char* msg);

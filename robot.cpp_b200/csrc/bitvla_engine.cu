@@ -17,6 +17,7 @@
 // parameters) and one for the activation buffers of max_batch observations; a batch of B observations
 // is B stacked row blocks in every activation buffer. The forward for each batch size is captured once
 // into a CUDA graph (programmatic dependent launch edges between the library kernels) and replayed.
+#include <algorithm>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
@@ -187,6 +188,17 @@ int cuda_err(cudaError_t e, const char* what) {
     return errf(B2S_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
 }
 
+#define TRY_CUDA(expr, what)                                  \
+    do {                                                      \
+        int rc_ = cuda_err((expr), what);                     \
+        if (rc_) return rc_;                                  \
+    } while (0)
+#define TRY_B2S(expr)          \
+    do {                       \
+        int rc_ = (expr);      \
+        if (rc_) return rc_;   \
+    } while (0)
+
 }  // namespace
 
 struct b2s_bitvla {
@@ -240,97 +252,175 @@ int check_cfg(const b2s_bitvla_config& c) {
     return B2S_OK;
 }
 
-// Stacked ternary weight of `parts` tensors (rows n[i], ids id[i]) over K inputs.
-void make_tern(Arena& A, Tern& t, int64_t K, std::initializer_list<std::pair<int64_t, uint32_t>> parts, uint32_t seed,
-               std::vector<float>* host_scales, std::vector<std::pair<float*, size_t>>* scale_fills,
-               cudaStream_t st, size_t* tern_bytes) {
-    int64_t N = 0;
-    for (auto& p : parts) N += p.first;
-    t.w.N = N;
-    t.w.K = K;
-    t.w.Kp = round_up(K, (int64_t)128);
-    uint8_t* codes = static_cast<uint8_t*>(A.take((size_t)(N * t.w.Kp / 4)));
-    const int64_t tiles = ceil_div(N, (int64_t)128);
-    t.scales = A.arr<float>((size_t)tiles);
-    *tern_bytes += (size_t)(N * t.w.Kp / 4);
-    if (!A.base) return;
-    t.w.codes = codes;
-    t.w.scale = t.scales;
-    const size_t first = host_scales->size();
-    int64_t row0 = 0;
-    for (auto& p : parts) {
-        const float sc = ternary_scale(seed, p.second, K);
-        for (int64_t r = row0; r < row0 + p.first; r += 128) host_scales->push_back(sc);
-        gen_ternary_kernel<<<grid_of(p.first * t.w.Kp / 4), 256, 0, st>>>(codes + row0 * (t.w.Kp / 4), p.first, K, t.w.Kp,
-                                                                         seed, p.second);
-        row0 += p.first;
+// Where the weights come from: the seeded generator or a GGUF file. Tensor names are the ones written by
+// b2s/gguf.py (llama.cpp conventions: "v.blk.N.*" for the vision tower, "blk.N.*" for the decoder).
+struct WeightSource {
+    virtual ~WeightSource() = default;
+    // Rows [0, rows) of ternary tensor (id, name) with K inputs, as row-padded codes at dst (Kp/4 bytes
+    // per row, pad code 1); its fp32 scale in *scale.
+    virtual int ternary(uint8_t* dst, int64_t rows, int64_t K, uint32_t id, const std::string& name, float* scale,
+                        cudaStream_t st) = 0;
+    virtual int uniform(float* dst, int64_t n, uint32_t id, const std::string& name, float lo, float hi,
+                        cudaStream_t st) = 0;
+};
+
+struct GenSource : WeightSource {
+    uint32_t seed;
+    explicit GenSource(uint32_t s) : seed(s) {}
+    int ternary(uint8_t* dst, int64_t rows, int64_t K, uint32_t id, const std::string&, float* scale,
+                cudaStream_t st) override {
+        *scale = ternary_scale(seed, id, K);
+        const int64_t Kp = round_up(K, (int64_t)128);
+        gen_ternary_kernel<<<grid_of(rows * Kp / 4), 256, 0, st>>>(dst, rows, K, Kp, seed, id);
+        return cuda_err(cudaGetLastError(), "ternary generation");
     }
-    scale_fills->push_back({t.scales, first});
-}
+    int uniform(float* dst, int64_t n, uint32_t id, const std::string&, float lo, float hi, cudaStream_t st) override {
+        gen_uniform_kernel<<<grid_of(n), 256, 0, st>>>(dst, n, seed, id, lo, hi - lo);
+        return cuda_err(cudaGetLastError(), "parameter generation");
+    }
+};
 
-float* make_uniform(Arena& A, int64_t n, uint32_t seed, uint32_t id, float lo, float hi, cudaStream_t st) {
-    float* p = A.arr<float>((size_t)n);
-    if (A.base) gen_uniform_kernel<<<grid_of(n), 256, 0, st>>>(p, n, seed, id, lo, hi - lo);
-    return p;
-}
+// Tensors of a GGUF file: I2_S (flattened i2_s bytes + scale trailer, repacked to row-padded rows on
+// the device through two staging buffers) and F32.
+struct GgufSource : WeightSource {
+    const b2s::GgufFile* f = nullptr;
+    uint8_t* stage_in = nullptr;
+    uint8_t* stage_out = nullptr;
+    size_t stage_bytes = 0;
+    int ternary(uint8_t* dst, int64_t rows, int64_t K, uint32_t, const std::string& name, float* scale,
+                cudaStream_t st) override {
+        const b2s::GgufTensor* t = f->tensor(name);
+        if (!t) return errf(B2S_ERR_INVALID_ARG, "GGUF: missing tensor '%s'", name.c_str());
+        if (t->type != 36 || t->ne[0] != K || t->ne[1] != rows || t->ne[2] != 1 || t->ne[3] != 1)
+            return errf(B2S_ERR_INVALID_ARG, "GGUF: tensor '%s' must be I2_S [%lld, %lld]", name.c_str(),
+                        (long long)K, (long long)rows);
+        const int64_t Kp = round_up(K, (int64_t)128);
+        if (t->nbytes > stage_bytes || (size_t)(rows * Kp / 4 + 32) > stage_bytes)
+            return errf(B2S_ERR_INVALID_ARG, "GGUF: tensor '%s' larger than the staging buffer", name.c_str());
+        memcpy(scale, t->data + rows * K / 4, sizeof(float));
+        TRY_CUDA(cudaMemcpyAsync(stage_in, t->data, t->nbytes, cudaMemcpyHostToDevice, st), "GGUF upload");
+        TRY_CUDA(b2s::launch_repack_rows(stage_in, stage_out, rows, K, st), "GGUF row repack");
+        TRY_CUDA(cudaMemcpyAsync(dst, stage_out, (size_t)(rows * Kp / 4), cudaMemcpyDeviceToDevice, st), "GGUF copy");
+        return B2S_OK;
+    }
+    int uniform(float* dst, int64_t n, uint32_t, const std::string& name, float, float, cudaStream_t st) override {
+        const b2s::GgufTensor* t = f->tensor(name);
+        if (!t) return errf(B2S_ERR_INVALID_ARG, "GGUF: missing tensor '%s'", name.c_str());
+        if (t->type != 0 || t->ne[0] * t->ne[1] * t->ne[2] * t->ne[3] != n)
+            return errf(B2S_ERR_INVALID_ARG, "GGUF: tensor '%s' must be F32 with %lld elements", name.c_str(),
+                        (long long)n);
+        TRY_CUDA(cudaMemcpyAsync(dst, t->data, sizeof(float) * (size_t)n, cudaMemcpyHostToDevice, st), "GGUF upload");
+        return B2S_OK;
+    }
+};
 
-// Lays out (and, with A.base set, generates) every weight.
-void build_weights(b2s_bitvla* m, Arena& A, cudaStream_t st, std::vector<float>* hs,
-                   std::vector<std::pair<float*, size_t>>* fills) {
+struct Part {
+    int64_t rows;
+    uint32_t id;
+    std::string name;
+};
+
+// Lays out the weight arena; with a source (and A.base set) it also fills every tensor.
+struct Builder {
+    Arena& A;
+    WeightSource* src;
+    cudaStream_t st;
+    std::vector<float>* hs;
+    std::vector<std::pair<float*, size_t>>* fills;
+    size_t* tern_bytes;
+    int rc = B2S_OK;
+
+    // Stacked ternary weight of `parts` tensors over K inputs; one scale per 128-row tile.
+    void tern(Tern& t, int64_t K, std::initializer_list<Part> parts) {
+        int64_t N = 0;
+        for (auto& p : parts) N += p.rows;
+        t.w.N = N;
+        t.w.K = K;
+        t.w.Kp = round_up(K, (int64_t)128);
+        uint8_t* codes = static_cast<uint8_t*>(A.take((size_t)(N * t.w.Kp / 4)));
+        t.scales = A.arr<float>((size_t)ceil_div(N, (int64_t)128));
+        *tern_bytes += (size_t)(N * t.w.Kp / 4);
+        if (!A.base) return;
+        t.w.codes = codes;
+        t.w.scale = t.scales;
+        const size_t first = hs->size();
+        int64_t row0 = 0;
+        for (auto& p : parts) {
+            float sc = 0.0f;
+            if (!rc) rc = src->ternary(codes + row0 * (t.w.Kp / 4), p.rows, K, p.id, p.name, &sc, st);
+            for (int64_t r = row0; r < row0 + p.rows; r += 128) hs->push_back(sc);
+            row0 += p.rows;
+        }
+        fills->push_back({t.scales, first});
+    }
+    float* f32(int64_t n, uint32_t id, const std::string& name, float lo, float hi) {
+        float* p = A.arr<float>((size_t)n);
+        if (A.base && !rc) rc = src->uniform(p, n, id, name, lo, hi, st);
+        return p;
+    }
+};
+
+std::string vn(int l, const char* what) { return "v.blk." + std::to_string(l) + "." + what; }
+std::string dn(int l, const char* what) { return "blk." + std::to_string(l) + "." + what; }
+
+// Lays out (and, with a source, fills) every weight.
+int build_weights(b2s_bitvla* m, Arena& A, WeightSource* src, cudaStream_t st, std::vector<float>* hs,
+                  std::vector<std::pair<float*, size_t>>* fills) {
     const b2s_bitvla_config& c = m->cfg;
-    const uint32_t sd = m->seed;
     const int D = c.vit_hidden, P = c.patch, kdim = 3 * P * P;
     const float pa = 1.0f / sqrtf((float)kdim);
     m->ternary_bytes = 0;
-    size_t* tb = &m->ternary_bytes;
-    m->patch_w = make_uniform(A, (int64_t)D * kdim, sd, kIdPatchW, -pa, pa, st);
-    m->patch_b = make_uniform(A, D, sd, kIdPatchB, -0.02f, 0.02f, st);
-    m->pos = make_uniform(A, (int64_t)m->np * D, sd, kIdPos, -0.02f, 0.02f, st);
+    Builder B{A, src, st, hs, fills, &m->ternary_bytes};
+    m->patch_w = B.f32((int64_t)D * kdim, kIdPatchW, "v.patch_embd.weight", -pa, pa);
+    m->patch_b = B.f32(D, kIdPatchB, "v.patch_embd.bias", -0.02f, 0.02f);
+    m->pos = B.f32((int64_t)m->np * D, kIdPos, "v.position_embd.weight", -0.02f, 0.02f);
     m->vit.resize((size_t)c.vit_layers);
     for (int l = 0; l < c.vit_layers; ++l) {
         VitLayer& L = m->vit[(size_t)l];
-        L.ln1_w = make_uniform(A, D, sd, vit_id(l, kVLn1W), 0.9f, 1.1f, st);
-        L.ln1_b = make_uniform(A, D, sd, vit_id(l, kVLn1B), -0.02f, 0.02f, st);
-        make_tern(A, L.qkv, D, {{D, vit_id(l, kVQ)}, {D, vit_id(l, kVK)}, {D, vit_id(l, kVV)}}, sd, hs, fills, st, tb);
-        L.qkv_b = A.arr<float>((size_t)3 * D);
-        if (A.base)
-            for (int j = 0; j < 3; ++j)
-                gen_uniform_kernel<<<grid_of(D), 256, 0, st>>>(L.qkv_b + j * D, D, sd, vit_id(l, kVQB + j), -0.02f, 0.04f);
-        make_tern(A, L.o, D, {{D, vit_id(l, kVO)}}, sd, hs, fills, st, tb);
-        L.o_b = make_uniform(A, D, sd, vit_id(l, kVOB), -0.02f, 0.02f, st);
-        L.ln2_w = make_uniform(A, D, sd, vit_id(l, kVLn2W), 0.9f, 1.1f, st);
-        L.ln2_b = make_uniform(A, D, sd, vit_id(l, kVLn2B), -0.02f, 0.02f, st);
-        make_tern(A, L.fc1, D, {{c.vit_ffn, vit_id(l, kVFc1)}}, sd, hs, fills, st, tb);
-        L.fc1_b = make_uniform(A, c.vit_ffn, sd, vit_id(l, kVFc1B), -0.02f, 0.02f, st);
-        make_tern(A, L.fc2, c.vit_ffn, {{D, vit_id(l, kVFc2)}}, sd, hs, fills, st, tb);
-        L.fc2_b = make_uniform(A, D, sd, vit_id(l, kVFc2B), -0.02f, 0.02f, st);
+        L.ln1_w = B.f32(D, vit_id(l, kVLn1W), vn(l, "ln1.weight"), 0.9f, 1.1f);
+        L.ln1_b = B.f32(D, vit_id(l, kVLn1B), vn(l, "ln1.bias"), -0.02f, 0.02f);
+        B.tern(L.qkv, D, {{D, vit_id(l, kVQ), vn(l, "attn_q.weight")}, {D, vit_id(l, kVK), vn(l, "attn_k.weight")},
+                          {D, vit_id(l, kVV), vn(l, "attn_v.weight")}});
+        L.qkv_b = B.f32(D, vit_id(l, kVQB), vn(l, "attn_q.bias"), -0.02f, 0.02f);
+        B.f32(D, vit_id(l, kVKB), vn(l, "attn_k.bias"), -0.02f, 0.02f);  // contiguous after the q bias
+        B.f32(D, vit_id(l, kVVB), vn(l, "attn_v.bias"), -0.02f, 0.02f);
+        B.tern(L.o, D, {{D, vit_id(l, kVO), vn(l, "attn_out.weight")}});
+        L.o_b = B.f32(D, vit_id(l, kVOB), vn(l, "attn_out.bias"), -0.02f, 0.02f);
+        L.ln2_w = B.f32(D, vit_id(l, kVLn2W), vn(l, "ln2.weight"), 0.9f, 1.1f);
+        L.ln2_b = B.f32(D, vit_id(l, kVLn2B), vn(l, "ln2.bias"), -0.02f, 0.02f);
+        B.tern(L.fc1, D, {{c.vit_ffn, vit_id(l, kVFc1), vn(l, "ffn_up.weight")}});
+        L.fc1_b = B.f32(c.vit_ffn, vit_id(l, kVFc1B), vn(l, "ffn_up.bias"), -0.02f, 0.02f);
+        B.tern(L.fc2, c.vit_ffn, {{D, vit_id(l, kVFc2), vn(l, "ffn_down.weight")}});
+        L.fc2_b = B.f32(D, vit_id(l, kVFc2B), vn(l, "ffn_down.bias"), -0.02f, 0.02f);
     }
-    m->post_w = make_uniform(A, D, sd, kIdPostW, 0.9f, 1.1f, st);
-    m->post_b = make_uniform(A, D, sd, kIdPostB, -0.02f, 0.02f, st);
-    make_tern(A, m->conn1, D, {{c.conn_hidden, kIdConn1}}, sd, hs, fills, st, tb);
-    m->conn1_b = make_uniform(A, c.conn_hidden, sd, kIdConn1B, -0.02f, 0.02f, st);
-    make_tern(A, m->conn2, c.conn_hidden, {{c.dec_hidden, kIdConn2}}, sd, hs, fills, st, tb);
-    m->conn2_b = make_uniform(A, c.dec_hidden, sd, kIdConn2B, -0.02f, 0.02f, st);
+    m->post_w = B.f32(D, kIdPostW, "v.post_ln.weight", 0.9f, 1.1f);
+    m->post_b = B.f32(D, kIdPostB, "v.post_ln.bias", -0.02f, 0.02f);
+    B.tern(m->conn1, D, {{c.conn_hidden, kIdConn1, "mm.0.weight"}});
+    m->conn1_b = B.f32(c.conn_hidden, kIdConn1B, "mm.0.bias", -0.02f, 0.02f);
+    B.tern(m->conn2, c.conn_hidden, {{c.dec_hidden, kIdConn2, "mm.2.weight"}});
+    m->conn2_b = B.f32(c.dec_hidden, kIdConn2B, "mm.2.bias", -0.02f, 0.02f);
     const int H = c.dec_hidden, KV = c.dec_kv_heads * c.head_dim;
     m->dec.resize((size_t)c.dec_layers);
     for (int l = 0; l < c.dec_layers; ++l) {
         DecLayer& L = m->dec[(size_t)l];
-        L.attn_norm = make_uniform(A, H, sd, dec_id(l, kDAttnNorm), 0.9f, 1.1f, st);
-        make_tern(A, L.qkv, H, {{H, dec_id(l, kDQ)}, {KV, dec_id(l, kDK)}, {KV, dec_id(l, kDV)}}, sd, hs, fills, st, tb);
-        L.attn_sub = make_uniform(A, H, sd, dec_id(l, kDAttnSub), 0.9f, 1.1f, st);
-        make_tern(A, L.o, H, {{H, dec_id(l, kDO)}}, sd, hs, fills, st, tb);
-        L.ffn_norm = make_uniform(A, H, sd, dec_id(l, kDFfnNorm), 0.9f, 1.1f, st);
-        make_tern(A, L.gate, H, {{c.dec_ffn, dec_id(l, kDGate)}}, sd, hs, fills, st, tb);
-        make_tern(A, L.up, H, {{c.dec_ffn, dec_id(l, kDUp)}}, sd, hs, fills, st, tb);
-        L.ffn_sub = make_uniform(A, c.dec_ffn, sd, dec_id(l, kDFfnSub), 0.9f, 1.1f, st);
-        make_tern(A, L.down, c.dec_ffn, {{H, dec_id(l, kDDown)}}, sd, hs, fills, st, tb);
+        L.attn_norm = B.f32(H, dec_id(l, kDAttnNorm), dn(l, "attn_norm.weight"), 0.9f, 1.1f);
+        B.tern(L.qkv, H, {{H, dec_id(l, kDQ), dn(l, "attn_q.weight")}, {KV, dec_id(l, kDK), dn(l, "attn_k.weight")},
+                          {KV, dec_id(l, kDV), dn(l, "attn_v.weight")}});
+        L.attn_sub = B.f32(H, dec_id(l, kDAttnSub), dn(l, "attn_sub_norm.weight"), 0.9f, 1.1f);
+        B.tern(L.o, H, {{H, dec_id(l, kDO), dn(l, "attn_output.weight")}});
+        L.ffn_norm = B.f32(H, dec_id(l, kDFfnNorm), dn(l, "ffn_norm.weight"), 0.9f, 1.1f);
+        B.tern(L.gate, H, {{c.dec_ffn, dec_id(l, kDGate), dn(l, "ffn_gate.weight")}});
+        B.tern(L.up, H, {{c.dec_ffn, dec_id(l, kDUp), dn(l, "ffn_up.weight")}});
+        L.ffn_sub = B.f32(c.dec_ffn, dec_id(l, kDFfnSub), dn(l, "ffn_sub_norm.weight"), 0.9f, 1.1f);
+        B.tern(L.down, c.dec_ffn, {{H, dec_id(l, kDDown), dn(l, "ffn_down.weight")}});
     }
-    m->final_norm = make_uniform(A, H, sd, kIdFinalNorm, 0.9f, 1.1f, st);
+    m->final_norm = B.f32(H, kIdFinalNorm, "output_norm.weight", 0.9f, 1.1f);
     const int NA = c.action_chunk * c.action_dim;
     const float aa = 1.0f / sqrtf((float)H);
-    m->act_w = make_uniform(A, (int64_t)NA * H, sd, kIdActW, -aa, aa, st);
-    m->act_b = make_uniform(A, NA, sd, kIdActB, -0.02f, 0.02f, st);
+    m->act_w = B.f32((int64_t)NA * H, kIdActW, "action_head.weight", -aa, aa);
+    m->act_b = B.f32(NA, kIdActB, "action_head.bias", -0.02f, 0.02f);
     m->rope = A.arr<float2>((size_t)m->seq * (size_t)(c.head_dim / 2));
+    return B.rc;
 }
 
 void build_acts(b2s_bitvla* m, Arena& A) {
@@ -360,16 +450,6 @@ void build_acts(b2s_bitvla* m, Arena& A) {
     m->qsum = A.arr<int32_t>((size_t)Mmax);
 }
 
-#define TRY_CUDA(expr, what)                                  \
-    do {                                                      \
-        int rc_ = cuda_err((expr), what);                     \
-        if (rc_) return rc_;                                  \
-    } while (0)
-#define TRY_B2S(expr)          \
-    do {                       \
-        int rc_ = (expr);      \
-        if (rc_) return rc_;   \
-    } while (0)
 
 // Enqueues the forward of `B` observations already in m->img / m->tok (results in m->hidden, m->actions).
 int enqueue_forward(b2s_bitvla* m, int B, cudaStream_t st) {
@@ -542,8 +622,13 @@ double b2s_bitvla_ternary_ops(const b2s_bitvla_config* c) {
 
 uint32_t b2s_bitvla_param_bits(uint32_t seed, uint32_t tensor, uint32_t idx) { return param_bits(seed, tensor, idx); }
 
-int b2s_bitvla_create(const b2s_bitvla_config* cfg, uint32_t seed, int max_batch, b2s_bitvla** out) {
-    if (!cfg || !out || max_batch <= 0) return errf(B2S_ERR_INVALID_ARG, "bitvla_create: bad arguments");
+}  // extern "C"
+
+namespace {
+
+// Shared by both constructors: lays out and allocates the arenas, fills the weights from `src`, zeroes
+// the activations and builds the RoPE table.
+int create_model(const b2s_bitvla_config* cfg, uint32_t seed, int max_batch, WeightSource* src, b2s_bitvla** out) {
     *out = nullptr;
     int rc = b2s_device_check();
     if (rc) return rc;
@@ -559,7 +644,7 @@ int b2s_bitvla_create(const b2s_bitvla_config* cfg, uint32_t seed, int max_batch
     std::vector<float> hs;
     std::vector<std::pair<float*, size_t>> fills;
     Arena wa;
-    build_weights(m, wa, nullptr, &hs, &fills);
+    build_weights(m, wa, nullptr, nullptr, &hs, &fills);
     Arena aa;
     build_acts(m, aa);
     m->wbytes = wa.off;
@@ -579,11 +664,11 @@ int b2s_bitvla_create(const b2s_bitvla_config* cfg, uint32_t seed, int max_batch
         return cuda_err(e, "bitvla_create allocation");
     }
     wa = Arena{static_cast<uint8_t*>(m->wmem), 0};
-    build_weights(m, wa, st, &hs, &fills);
+    rc = build_weights(m, wa, src, st, &hs, &fills);
     aa = Arena{static_cast<uint8_t*>(m->amem), 0};
     build_acts(m, aa);
-    // Upload the per-tile scales (each make_tern appended ceil(N/128) entries starting at f.second).
-    for (size_t i = 0; i < fills.size(); ++i) {
+    // Upload the per-tile scales (each stacked weight appended ceil(N/128) entries starting at f.second).
+    for (size_t i = 0; i < fills.size() && !rc; ++i) {
         const size_t first = fills[i].second;
         const size_t last = (i + 1 < fills.size()) ? fills[i + 1].second : hs.size();
         if (e == cudaSuccess)
@@ -592,15 +677,82 @@ int b2s_bitvla_create(const b2s_bitvla_config* cfg, uint32_t seed, int max_batch
     }
     if (e == cudaSuccess) e = cudaMemsetAsync(m->amem, 0, m->abytes, st);
     if (e == cudaSuccess) e = b2s::launch_rope_table(cfg->rope_theta, cfg->head_dim, m->seq, m->rope, st);
-    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    cudaError_t es = cudaStreamSynchronize(st);  // also before any error return: staged copies must finish
+    if (e == cudaSuccess) e = es;
     if (e == cudaSuccess) e = cudaGetLastError();
     cudaStreamDestroy(st);
-    if (e != cudaSuccess) {
+    if (rc || e != cudaSuccess) {
         b2s_bitvla_free(m);
-        return cuda_err(e, "bitvla_create weight generation");
+        return rc ? rc : cuda_err(e, "bitvla_create weight upload");
     }
     *out = m;
     return B2S_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int b2s_bitvla_create(const b2s_bitvla_config* cfg, uint32_t seed, int max_batch, b2s_bitvla** out) {
+    if (!cfg || !out || max_batch <= 0) return errf(B2S_ERR_INVALID_ARG, "bitvla_create: bad arguments");
+    GenSource gen(seed);
+    return create_model(cfg, seed, max_batch, &gen, out);
+}
+
+int b2s_bitvla_create_from_gguf(const char* path, int max_batch, b2s_bitvla** out) {
+    if (!path || !out || max_batch <= 0) return errf(B2S_ERR_INVALID_ARG, "bitvla_create_from_gguf: bad arguments");
+    *out = nullptr;
+    b2s::GgufFile f;
+    std::string err;
+    if (!f.open(path, &err)) return errf(B2S_ERR_INVALID_ARG, "%s", err.c_str());
+    std::string arch;
+    if (!f.str("general.architecture", &arch) || arch != "bitvla")
+        return errf(B2S_ERR_INVALID_ARG, "GGUF: general.architecture is '%s', expected 'bitvla'", arch.c_str());
+    b2s_bitvla_config c;
+    b2s_bitvla_default_config(&c);
+    struct U { const char* key; int* dst; } us[] = {
+        {"bitvla.image_size", &c.image_size}, {"bitvla.patch_size", &c.patch},
+        {"bitvla.vision.block_count", &c.vit_layers}, {"bitvla.vision.embedding_length", &c.vit_hidden},
+        {"bitvla.vision.feed_forward_length", &c.vit_ffn}, {"bitvla.vision.attention.head_count", &c.vit_heads},
+        {"bitvla.connector.embedding_length", &c.conn_hidden}, {"bitvla.block_count", &c.dec_layers},
+        {"bitvla.embedding_length", &c.dec_hidden}, {"bitvla.feed_forward_length", &c.dec_ffn},
+        {"bitvla.attention.head_count", &c.dec_heads}, {"bitvla.attention.head_count_kv", &c.dec_kv_heads},
+        {"bitvla.attention.key_length", &c.head_dim}, {"bitvla.vocab_size", &c.vocab},
+        {"bitvla.text_tokens", &c.n_text}, {"bitvla.action.chunk_size", &c.action_chunk},
+        {"bitvla.action.dim", &c.action_dim}};
+    for (auto& u : us) {
+        uint32_t v;
+        if (!f.u32(u.key, &v)) return errf(B2S_ERR_INVALID_ARG, "GGUF: missing u32 key '%s'", u.key);
+        *u.dst = (int)v;
+    }
+    struct F { const char* key; float* dst; } fs[] = {
+        {"bitvla.vision.attention.layer_norm_epsilon", &c.vit_eps},
+        {"bitvla.attention.layer_norm_rms_epsilon", &c.dec_eps}, {"bitvla.rope.freq_base", &c.rope_theta}};
+    for (auto& x : fs)
+        if (!f.f32(x.key, x.dst)) return errf(B2S_ERR_INVALID_ARG, "GGUF: missing f32 key '%s'", x.key);
+    uint32_t seed = 0;
+    if (!f.u32("bitvla.token_embd.seed", &seed)) return errf(B2S_ERR_INVALID_ARG, "GGUF: missing bitvla.token_embd.seed");
+    int rc = b2s_device_check();
+    if (rc) return rc;
+    if ((rc = check_cfg(c))) return rc;
+    // staging for the largest ternary tensor (flattened bytes in, row-padded bytes out)
+    const int64_t Kmax = std::max({(int64_t)c.vit_hidden, (int64_t)c.vit_ffn, (int64_t)c.conn_hidden,
+                                   (int64_t)c.dec_hidden, (int64_t)c.dec_ffn});
+    const int64_t Nmax = std::max({(int64_t)c.vit_ffn, (int64_t)c.conn_hidden, (int64_t)c.dec_hidden,
+                                   (int64_t)c.dec_ffn, (int64_t)c.vit_hidden});
+    GgufSource src;
+    src.f = &f;
+    src.stage_bytes = (size_t)(Nmax * round_up(Kmax, (int64_t)128) / 4 + 64);
+    cudaError_t e = cudaMalloc(reinterpret_cast<void**>(&src.stage_in), src.stage_bytes);
+    if (e == cudaSuccess) e = cudaMalloc(reinterpret_cast<void**>(&src.stage_out), src.stage_bytes);
+    if (e != cudaSuccess) {
+        cudaFree(src.stage_in);
+        return cuda_err(e, "GGUF staging buffers");
+    }
+    rc = create_model(&c, seed, max_batch, &src, out);
+    cudaFree(src.stage_in);
+    cudaFree(src.stage_out);
+    return rc;
 }
 
 void b2s_bitvla_free(b2s_bitvla* m) {
