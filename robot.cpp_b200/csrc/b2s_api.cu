@@ -190,6 +190,12 @@ TcTiling pick_tiling(int64_t M, int64_t n_out, int rows_per_cta, int64_t Kp, int
     if (s > nkt / 2) s = (int)(nkt / 2);
     if (s > 8) s = 8;
     if (s < 1) s = 1;
+    // A cluster must fit inside one GPC: take the largest split whose clusters all fit at once (one wave).
+    while (s > 1) {
+        const int act = b2s::tc_max_active_clusters(s);
+        if (act <= 0 || tiles <= act) break;
+        --s;
+    }
     t.splits = s;
     return t;
 }

@@ -83,6 +83,8 @@ struct TcGemmArgs {
     Epilogue epi;
 };
 cudaError_t launch_gemm_i2s_tc(const TcGemmArgs& args, cudaStream_t st);
+// Clusters of `size` (1..8) CTAs of the split-K kernel that fit on the device at once; <= 0 if unknown.
+int tc_max_active_clusters(int size);
 // Persistent variant (gemm_i2s_tcp.cu): `grid` CTAs walk the n_tiles x m_tiles tiles of T <= 224 tokens
 // (splits must be 1; tmap_q's box is 128 x T).
 int tcp_max_tokens();

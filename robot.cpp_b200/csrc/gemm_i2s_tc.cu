@@ -503,6 +503,36 @@ static cudaError_t launch_variant(const TcGemmArgs& a, cudaStream_t st) {
                               a.ldy, a.M, a.N, a.Kp, a.T, a.bn_sub, a.nsub, a.epi);
 }
 
+// Clusters of `size` CTAs of this kernel that can be resident at once on the current device (a cluster
+// must fit inside one GPC, so e.g. 7-CTA clusters leave SMs of every GPC idle). Cached per device/size.
+int tc_max_active_clusters(int size) {
+    static int cache[64][9];
+    int dev = 0;
+    if (size < 1 || size > 8 || cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
+    if (cache[dev][size]) return cache[dev][size];
+    auto kfn = gemm_i2s_tc_kernel<0, 0>;
+    if (cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tc::kSmemBytes) != cudaSuccess)
+        return 0;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(1, 1, (unsigned)size);
+    cfg.blockDim = dim3(tc::kThreads);
+    cfg.dynamicSmemBytes = tc::kSmemBytes;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = (unsigned)size;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, kfn, &cfg) != cudaSuccess) {
+        (void)cudaGetLastError();
+        return 0;
+    }
+    cache[dev][size] = n > 0 ? n : -1;
+    return cache[dev][size];
+}
+
 cudaError_t launch_gemm_i2s_tc(const TcGemmArgs& a, cudaStream_t st) {
     if (a.mode == 1) return launch_variant<1, 0>(a, st);
     const int epi = (a.epi.bias ? kEpiBias : 0) | (a.epi.act == 1 ? kEpiGelu : 0) |
