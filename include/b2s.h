@@ -109,7 +109,9 @@ int b2s_act_quant(const float *x, int64_t M, int64_t K, int64_t ldx, int8_t *q, 
 int b2s_rms_norm_act_quant(const float *x, const float *g, int64_t M, int64_t K, int64_t ldx, float eps,
                            int8_t *q, int64_t ldq, float *s, int32_t *sums, void *stream);
 
-/* Workspace bytes b2s_mul_mat needs for these operands (int8 activations, scales, sums). */
+/* Workspace bytes b2s_mul_mat needs for these operands: int8 activations, scales and sums, then room for
+ * the split-K partials of small-M launches (those reduce through L2 when the room is there, through
+ * distributed shared memory otherwise). Any size >= the activation part is accepted. */
 size_t b2s_mul_mat_workspace_size(const b2s_tensor *W, const b2s_tensor *X);
 
 /* The MUL_MAT node: Y = mul_mat(W, X). W: I2_S (ne0 % 128 == 0) or I2_S_R, ne=[K,N], contiguous;

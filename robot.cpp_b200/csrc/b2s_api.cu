@@ -214,7 +214,7 @@ int num_sms_current() {
 
 int run_tc(const b2s::I2sWeight& w0, const b2s::I2sWeight* w1, const int8_t* q, int64_t ldq, const float* s,
            const int32_t* sums, int64_t M, float* Y, int64_t ldy, int mode, cudaStream_t st,
-           const b2s::Epilogue& epi = b2s::Epilogue{}) {
+           const b2s::Epilogue& epi = b2s::Epilogue{}, void* splitk_ws = nullptr, size_t splitk_bytes = 0) {
     if ((reinterpret_cast<uintptr_t>(q) & 15) != 0 || ldq % 16 != 0)
         return fail(B2S_ERR_UNSUPPORTED, "tensor-core path needs 16-byte aligned q with ldq %% 16 == 0");
     if (M > (int64_t)0x7fffffff || w0.N > (int64_t)0x7fffffff) return fail(B2S_ERR_UNSUPPORTED, "size exceeds int32");
@@ -278,6 +278,10 @@ int run_tc(const b2s::I2sWeight& w0, const b2s::I2sWeight* w1, const int8_t* q, 
     a.splits = t.splits;
     a.mode = mode;
     a.epi = epi;
+    a.part = nullptr;
+    if (t.splits > 1 && splitk_ws && ((reinterpret_cast<uintptr_t>(splitk_ws) & 255) == 0) &&
+        splitk_bytes >= (size_t)t.n_tiles * t.m_tiles * t.splits * t.T * 128 * sizeof(int32_t))
+        a.part = static_cast<int32_t*>(splitk_ws);
     if (p_grid > 0) return launched(b2s::launch_gemm_i2s_tcp(a, p_grid, st), "gemm_i2s_tcp launch");
     return launched(b2s::launch_gemm_i2s_tc(a, st), "gemm_i2s_tc launch");
 }
@@ -285,14 +289,15 @@ int run_tc(const b2s::I2sWeight& w0, const b2s::I2sWeight* w1, const int8_t* q, 
 // path: 0 auto, 1 GEMV, 2 tensor cores
 int mul_mat_q8_impl(const b2s::I2sWeight& w, const int8_t* q, int64_t ldq, const float* s, const int32_t* sums,
                     int64_t M, float* Y, int64_t ldy, int path, cudaStream_t st,
-                    const b2s::Epilogue& epi = b2s::Epilogue{}) {
+                    const b2s::Epilogue& epi = b2s::Epilogue{}, void* splitk_ws = nullptr,
+                    size_t splitk_bytes = 0) {
     if (M <= 0) return B2S_OK;
     if (path == 0) path = (M <= 16) ? 1 : 2;
     if (path == 1) {
         b2s::Q8Act a{q, s, sums, M, w.K, ldq};
         return launched(b2s::launch_gemv_i2s(w, a, Y, ldy, epi, st), "gemv_i2s launch");
     }
-    return run_tc(w, nullptr, q, ldq, s, sums, M, Y, ldy, 0, st, epi);
+    return run_tc(w, nullptr, q, ldq, s, sums, M, Y, ldy, 0, st, epi, splitk_ws, splitk_bytes);
 }
 
 }  // namespace
@@ -300,16 +305,27 @@ int mul_mat_q8_impl(const b2s::I2sWeight& w, const int8_t* q, int64_t ldq, const
 namespace b2s {
 
 int dispatch_mul_mat_q8(const I2sWeight& w, const int8_t* q, int64_t ldq, const float* s, const int32_t* sums,
-                        int64_t M, float* y, int64_t ldy, int path, const Epilogue& epi, cudaStream_t st) {
+                        int64_t M, float* y, int64_t ldy, int path, const Epilogue& epi, cudaStream_t st,
+                        void* splitk_ws, size_t splitk_bytes) {
     if (epi.scale_rows < 0 || (epi.scale_rows % 128 != 0 && path != 1))
         return fail(B2S_ERR_UNSUPPORTED, "stacked weight scales need scale_rows %% 128 == 0");
-    return mul_mat_q8_impl(w, q, ldq, s, sums, M, y, ldy, path, st, epi);
+    return mul_mat_q8_impl(w, q, ldq, s, sums, M, y, ldy, path, st, epi, splitk_ws, splitk_bytes);
 }
 
 int dispatch_gate_up(const I2sWeight& wg, const I2sWeight& wu, const int8_t* q, int64_t ldq, const float* s,
-                     const int32_t* sums, int64_t M, float* p, int64_t ldp, cudaStream_t st) {
+                     const int32_t* sums, int64_t M, float* p, int64_t ldp, cudaStream_t st, void* splitk_ws,
+                     size_t splitk_bytes) {
     if (M <= 0) return B2S_OK;
-    return run_tc(wg, &wu, q, ldq, s, sums, M, p, ldp, 1, st);
+    return run_tc(wg, &wu, q, ldq, s, sums, M, p, ldp, 1, st, Epilogue{}, splitk_ws, splitk_bytes);
+}
+
+size_t splitk_ws_bytes(int64_t M, int64_t n_out, int rows_per_cta) {
+    // A K split is chosen only while tiles x splits <= the SM count; tiles hold at most 320 tokens.
+    const int64_t nsm = num_sms_current();
+    const int64_t m_tiles = ceil_div(M, 320), n_tiles = ceil_div(n_out, rows_per_cta);
+    if (M <= 0 || n_tiles * m_tiles >= nsm) return 0;
+    const int64_t T = round_up(ceil_div(M, m_tiles), 32);
+    return (size_t)(nsm * (T < 320 ? T : 320) * 128) * sizeof(int32_t);
 }
 
 int set_last_error(int code, const char* msg) { return fail(code, "%s", msg); }
@@ -469,7 +485,7 @@ int b2s_rms_norm_act_quant(const float* x, const float* g, int64_t M, int64_t K,
 size_t b2s_mul_mat_workspace_size(const b2s_tensor* W, const b2s_tensor* X) {
     if (!W || !X) return 0;
     const int64_t M = X->ne[1] * (X->ne[2] > 0 ? X->ne[2] : 1) * (X->ne[3] > 0 ? X->ne[3] : 1);
-    return act_ws(M, W->ne[0]).total;
+    return a256(act_ws(M, W->ne[0]).total) + b2s::splitk_ws_bytes(M, W->ne[1], 128);
 }
 
 int b2s_mul_mat_q8_ex(const b2s_tensor* W, const int8_t* q, int64_t ldq, const float* s, const int32_t* sums,
@@ -530,7 +546,11 @@ int b2s_mul_mat(const b2s_tensor* W, const b2s_tensor* X, b2s_tensor* Y, void* w
                                              l.ldq, s, sums, st),
                        "act_quant launch")))
         return rc;
-    return mul_mat_q8_impl(w, q, l.ldq, s, sums, M, static_cast<float*>(Y->data), ldy, 0, st);
+    // workspace beyond the activation layout (b2s_mul_mat_workspace_size includes it) holds split-K partials
+    const size_t sk_off = a256(l.total);
+    void* sk = workspace_bytes > sk_off ? ws + sk_off : nullptr;
+    return mul_mat_q8_impl(w, q, l.ldq, s, sums, M, static_cast<float*>(Y->data), ldy, 0, st, b2s::Epilogue{}, sk,
+                           sk ? workspace_bytes - sk_off : 0);
 }
 
 int b2s_ffn_gate_up_sqrelu_q8(const b2s_tensor* W_gate, const b2s_tensor* W_up, const int8_t* q, int64_t ldq,
@@ -547,18 +567,21 @@ int b2s_ffn_gate_up_sqrelu_q8(const b2s_tensor* W_gate, const b2s_tensor* W_up, 
     return run_tc(wg, &wu, q, ldq, s, sums, M, P, ldp, 1, static_cast<cudaStream_t>(stream));
 }
 
-static void ffn_layout(int64_t M, int64_t H, int64_t F, WsLayout* l1, size_t* p_off, WsLayout* l2) {
+static void ffn_layout(int64_t M, int64_t H, int64_t F, WsLayout* l1, size_t* p_off, WsLayout* l2,
+                       size_t* sk_off, size_t* sk_bytes) {
     *l1 = act_ws(M, H);
     *p_off = a256(l1->total);
     *l2 = act_ws(M, F, *p_off + sizeof(float) * (size_t)(M * F));
+    *sk_off = a256(l2->total);
+    *sk_bytes = std::max(b2s::splitk_ws_bytes(M, F, 64), b2s::splitk_ws_bytes(M, H, 128));
 }
 
 size_t b2s_ffn_block_workspace_size(int64_t M, int64_t H, int64_t F) {
     if (M <= 0 || H <= 0 || F <= 0) return 0;
     WsLayout l1, l2;
-    size_t p_off;
-    ffn_layout(M, H, F, &l1, &p_off, &l2);
-    return l2.total;
+    size_t p_off, sk_off, sk_bytes;
+    ffn_layout(M, H, F, &l1, &p_off, &l2, &sk_off, &sk_bytes);
+    return sk_off + sk_bytes;
 }
 
 int b2s_ffn_block(const float* X, int64_t M, const float* g1, const float* g2, float eps, const b2s_tensor* W_gate,
@@ -576,10 +599,11 @@ int b2s_ffn_block(const float* X, int64_t M, const float* g1, const float* g2, f
     if (!X || !Y) return fail(B2S_ERR_INVALID_ARG, "ffn_block: X and Y must be non-NULL");
     if (M <= 0) return M == 0 ? B2S_OK : fail(B2S_ERR_INVALID_ARG, "ffn_block: M < 0");
     WsLayout l1, l2;
-    size_t p_off;
-    ffn_layout(M, H, F, &l1, &p_off, &l2);
-    if (!workspace || workspace_bytes < l2.total)
-        return fail(B2S_ERR_WORKSPACE, "ffn_block needs %zu workspace bytes, got %zu", l2.total, workspace_bytes);
+    size_t p_off, sk_off, sk_bytes;
+    ffn_layout(M, H, F, &l1, &p_off, &l2, &sk_off, &sk_bytes);
+    if (!workspace || workspace_bytes < sk_off + sk_bytes)
+        return fail(B2S_ERR_WORKSPACE, "ffn_block needs %zu workspace bytes, got %zu", sk_off + sk_bytes,
+                    workspace_bytes);
     if ((reinterpret_cast<uintptr_t>(workspace) & 255) != 0) return fail(B2S_ERR_WORKSPACE, "workspace must be 256-byte aligned");
     uint8_t* ws = static_cast<uint8_t*>(workspace);
     cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -592,10 +616,11 @@ int b2s_ffn_block(const float* X, int64_t M, const float* g1, const float* g2, f
     int32_t* u2 = reinterpret_cast<int32_t*>(ws + l2.sum_off);
     if ((rc = launched(b2s::launch_act_quant(X, H, g1, true, eps, M, H, q1, l1.ldq, s1, u1, st), "rms_norm_act_quant 1")))
         return rc;
-    if ((rc = run_tc(wg, &wu, q1, l1.ldq, s1, u1, M, P, F, 1, st))) return rc;
+    void* sk = ws + sk_off;
+    if ((rc = run_tc(wg, &wu, q1, l1.ldq, s1, u1, M, P, F, 1, st, b2s::Epilogue{}, sk, sk_bytes))) return rc;
     if ((rc = launched(b2s::launch_act_quant(P, F, g2, true, eps, M, F, q2, l2.ldq, s2, u2, st), "rms_norm_act_quant 2")))
         return rc;
-    return mul_mat_q8_impl(wd, q2, l2.ldq, s2, u2, M, Y, H, 0, st);
+    return mul_mat_q8_impl(wd, q2, l2.ldq, s2, u2, M, Y, H, 0, st, b2s::Epilogue{}, sk, sk_bytes);
 }
 
 int b2s_norm(const float* x, const float* g, const float* b, int64_t M, int64_t K, int64_t ldx, float eps, int kind,

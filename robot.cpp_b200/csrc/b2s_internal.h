@@ -81,7 +81,11 @@ struct TcGemmArgs {
     int n_tiles, m_tiles, splits;  // grid; splits = K-split CTAs per cluster (1..8)
     int mode;
     Epilogue epi;
+    int32_t* part;        // split-K partials in global memory (n_tiles * m_tiles * splits * T * 128 int32), or
+                          // nullptr for the distributed-shared-memory reduction
 };
+// Global split-K workspace that covers any tiling of an M-token GEMM with n_out outputs per matrix.
+size_t splitk_ws_bytes(int64_t M, int64_t n_out, int rows_per_cta);
 cudaError_t launch_gemm_i2s_tc(const TcGemmArgs& args, cudaStream_t st);
 // Clusters of `size` (1..8) CTAs of the split-K kernel that fit on the device at once; <= 0 if unknown.
 int tc_max_active_clusters(int size);
@@ -121,10 +125,12 @@ cudaError_t launch_attention(const float* q, int64_t ldq, const float* k, int64_
 // The library's mul_mat dispatch (b2s status codes; failures recorded for b2s_last_error()).
 // path 0 = auto (M <= 16: GEMV, else tensor cores), 1 = GEMV, 2 = tensor cores.
 int dispatch_mul_mat_q8(const I2sWeight& w, const int8_t* q, int64_t ldq, const float* s, const int32_t* sums,
-                        int64_t M, float* y, int64_t ldy, int path, const Epilogue& epi, cudaStream_t st);
+                        int64_t M, float* y, int64_t ldy, int path, const Epilogue& epi, cudaStream_t st,
+                        void* splitk_ws = nullptr, size_t splitk_bytes = 0);
 // FFN gate/up with the squared-ReLU product: p = relu(Wg q)^2 * (Wu q) (tensor cores, mode 1).
 int dispatch_gate_up(const I2sWeight& wg, const I2sWeight& wu, const int8_t* q, int64_t ldq, const float* s,
-                     const int32_t* sums, int64_t M, float* p, int64_t ldp, cudaStream_t st);
+                     const int32_t* sums, int64_t M, float* p, int64_t ldp, cudaStream_t st,
+                     void* splitk_ws = nullptr, size_t splitk_bytes = 0);
 
 // Read-only GGUF container (gguf_file.cu): memory-mapped, metadata parsed, tensors indexed by name.
 struct GgufValue {

@@ -211,6 +211,8 @@ struct b2s_bitvla {
     size_t wbytes = 0;
     void* amem = nullptr;
     size_t abytes = 0;
+    void* splitk_ws = nullptr;  // split-K partials of the GEMMs (global memory, reused by every launch)
+    size_t splitk_bytes = 0;
     // weights
     float *patch_w = nullptr, *patch_b = nullptr, *pos = nullptr, *post_w = nullptr, *post_b = nullptr;
     float *conn1_b = nullptr, *conn2_b = nullptr, *final_norm = nullptr, *act_w = nullptr, *act_b = nullptr;
@@ -445,6 +447,16 @@ void build_acts(b2s_bitvla* m, Arena& A) {
     for (int k : {c.vit_ffn, c.conn_hidden, H, c.dec_ffn}) kmax = k > kmax ? k : kmax;
     m->ldq = (int)round_up((int64_t)kmax, (int64_t)16);
     const int64_t Mmax = Md > Mv ? Md : Mv;
+    {
+        size_t sk = 0;
+        const int64_t Ms[2] = {Mv, Md};
+        const int64_t outs[6] = {3 * (int64_t)D, D, c.vit_ffn, c.conn_hidden, H + 2 * (int64_t)KV, H};
+        for (int64_t mm : Ms)
+            for (int64_t n : outs) sk = std::max(sk, b2s::splitk_ws_bytes(mm, n, 128));
+        sk = std::max(sk, b2s::splitk_ws_bytes(Md, c.dec_ffn, 64));
+        m->splitk_bytes = sk;
+        m->splitk_ws = A.take(sk);
+    }
     m->q8 = A.arr<int8_t>((size_t)(Mmax * m->ldq));
     m->qs = A.arr<float>((size_t)Mmax);
     m->qsum = A.arr<int32_t>((size_t)Mmax);
@@ -459,7 +471,8 @@ int enqueue_forward(b2s_bitvla* m, int B, cudaStream_t st) {
     const int ldq = m->ldq;
     auto gemm = [&](const Tern& t, int64_t M, float* y, int64_t ldy, const float* bias, const float* res, int act) {
         b2s::Epilogue e{bias, res, res ? ldy : 0, act, 128};
-        return b2s::dispatch_mul_mat_q8(t.w, m->q8, ldq, m->qs, m->qsum, M, y, ldy, 2, e, st);
+        return b2s::dispatch_mul_mat_q8(t.w, m->q8, ldq, m->qs, m->qsum, M, y, ldy, 2, e, st, m->splitk_ws,
+                                        m->splitk_bytes);
     };
     // ---------------------------------------------------------------- vision tower
     TRY_CUDA(b2s::launch_patch_embed(m->img, B, 3, c.image_size, c.image_size, c.patch, m->patch_w, m->patch_b, m->pos,
@@ -527,7 +540,8 @@ int enqueue_forward(b2s_bitvla* m, int B, cudaStream_t st) {
         TRY_B2S(gemm(L.o, Md, m->dx, H, nullptr, m->dx, 0));
         TRY_CUDA(b2s::launch_act_quant(m->dx, H, L.ffn_norm, true, c.dec_eps, Md, H, m->q8, ldq, m->qs, m->qsum, st),
                  "ffn_norm");
-        TRY_B2S(b2s::dispatch_gate_up(L.gate.w, L.up.w, m->q8, ldq, m->qs, m->qsum, Md, m->dp, c.dec_ffn, st));
+        TRY_B2S(b2s::dispatch_gate_up(L.gate.w, L.up.w, m->q8, ldq, m->qs, m->qsum, Md, m->dp, c.dec_ffn, st,
+                                      m->splitk_ws, m->splitk_bytes));
         TRY_CUDA(b2s::launch_act_quant(m->dp, c.dec_ffn, L.ffn_sub, true, c.dec_eps, Md, c.dec_ffn, m->q8, ldq, m->qs,
                                        m->qsum, st),
                  "ffn_sub_norm");
