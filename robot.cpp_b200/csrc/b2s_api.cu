@@ -93,6 +93,21 @@ int make_tmap_u8(CUtensorMap* m, const void* ptr, uint64_t cols, uint64_t rows, 
     return B2S_OK;
 }
 
+// 2D fp32 tensor map without swizzle: `cols` floats per row, `rows` rows of stride `ld` floats, box
+// box_c x box_r. Returns false (no error recorded) when the base or stride is not TMA-compatible.
+bool make_tmap_f32(CUtensorMap* m, const void* ptr, uint64_t cols, uint64_t rows, uint64_t ld, uint32_t box_c,
+                   uint32_t box_r) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn || (reinterpret_cast<uintptr_t>(ptr) & 15) != 0 || (ld * 4) % 16 != 0) return false;
+    cuuint64_t dims[2] = {cols, rows};
+    cuuint64_t strides[1] = {ld * 4};
+    cuuint32_t box[2] = {box_c, box_r};
+    cuuint32_t estr[2] = {1, 1};
+    return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 // ---------------------------------------------------------------- descriptor validation
 int weight_view(const b2s_tensor* W, b2s::I2sWeight* out, const char* name) {
     if (!W) return fail(B2S_ERR_INVALID_ARG, "%s is NULL", name);
@@ -257,9 +272,11 @@ int run_tc(const b2s::I2sWeight& w0, const b2s::I2sWeight* w1, const int8_t* q, 
         if ((rc = make_tmap_u8(&a.tmap_w1, w1->codes, (uint64_t)(w1->Kp / 4), (uint64_t)w1->N, (uint64_t)(w1->Kp / 4),
                                32, (uint32_t)rows, false)))
             return rc;
+        a.y_tma = make_tmap_f32(&a.tmap_y, Y, (uint64_t)w0.N, (uint64_t)M, (uint64_t)ldy, 64, 16) ? 1 : 0;
     } else {
         a.tmap_w1 = a.tmap_w0;
     }
+    if (!a.y_tma) a.tmap_y = a.tmap_w0;  // unused placeholder
     a.w0_scale = w0.scale;
     a.w1_scale = (mode == 1) ? w1->scale : w0.scale;
     a.s = s;

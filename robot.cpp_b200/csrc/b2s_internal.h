@@ -68,6 +68,8 @@ struct TcGemmArgs {
     CUtensorMap tmap_w0;  // packed codes of W (or W_gate), 2D u8 [N rows][Kp/4 bytes], box 32 x 128 (64 in mode 1)
     CUtensorMap tmap_w1;  // packed codes of W_up (mode 1), box 32 x 64
     CUtensorMap tmap_q;   // int8 activations 2D [M rows][K], box 128 x bn_sub, 128B swizzle
+    CUtensorMap tmap_y;   // mode 1: fp32 output 2D [M rows][N] (row stride ldy), box 64 x 16, for TMA stores
+    int y_tma;            // tmap_y is valid (y 16-byte aligned, ldy a multiple of 4)
     const float* w0_scale;
     const float* w1_scale;
     const float* s;       // act scales [M]

@@ -19,8 +19,11 @@
 //   * warps 0-3 read the accumulators back (tcgen05.ld, two 16-token chunks per wait) and write fp32
 //     y = (float)(acc - sum_q[m]) * (w_scale / s[m]) with coalesced stores.
 // Mode 1 (FFN gate/up): in every converter warp, lanes 0-15 hold 16 gate rows and lanes 16-31 the 16 up
-// rows of the same output columns, so one accumulator set holds both and the epilogue pairs them with
-// one warp shuffle, writing p = relu(g)^2 * u (the squared-ReLU gate product fused into the GEMM).
+// rows of the same output columns, so one accumulator set holds both, and the epilogue writes
+// p = relu(g)^2 * u (the squared-ReLU gate product fused into the GEMM). Without split-K it reads gate and
+// up of the same output into one thread with 16x64b TMEM loads, stages the fp32 tile in the drained
+// shared-memory ring and writes it with TMA tile stores; with split-K (or an output TMA cannot address)
+// it pairs the 32x32b-loaded rows with one warp shuffle and stores directly.
 //
 // Split-K across a thread-block cluster: when the output tiles alone cannot fill the GPU, the grid's
 // z dimension splits the K loop over the S CTAs of a cluster (1 x 1 x S). Each CTA stores its int32
@@ -136,10 +139,11 @@ constexpr int kEpiBias = 1, kEpiGelu = 2, kEpiResidual = 4;
 template <int MODE, int EPI>
 __global__ void __launch_bounds__(tc::kThreads, 1)
 gemm_i2s_tc_kernel(const __grid_constant__ CUtensorMap tmap_w0, const __grid_constant__ CUtensorMap tmap_w1,
-                   const __grid_constant__ CUtensorMap tmap_q, const float* __restrict__ w0_scale,
-                   const float* __restrict__ w1_scale, const float* __restrict__ s_act,
-                   const int32_t* __restrict__ sum_act, float* y, int64_t ldy, int M, int N, int Kp,
-                   int T, int bn_sub, int nsub, const Epilogue epi, int32_t* __restrict__ part_g) {
+                   const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_y,
+                   const float* __restrict__ w0_scale, const float* __restrict__ w1_scale,
+                   const float* __restrict__ s_act, const int32_t* __restrict__ sum_act, float* y, int64_t ldy,
+                   int M, int N, int Kp, int T, int bn_sub, int nsub, const Epilogue epi,
+                   int32_t* __restrict__ part_g, int y_tma) {
     using namespace tc;
     constexpr int mode = MODE;
     extern __shared__ uint8_t smem_raw[];
@@ -209,12 +213,16 @@ gemm_i2s_tc_kernel(const __grid_constant__ CUtensorMap tmap_w0, const __grid_con
         griddep_wait();  // scales and sums come from the preceding kernel
         const int nmat = (mode == 1) ? 2 : 1;
         const int tid = threadIdx.x - 192;
+        // The staged mode-1 epilogue reads the factors of the even tokens of a 16-token chunk, then the odd
+        // ones (the column order of a 16x64b TMEM load), so they are stored in that order.
+        const bool perm = (mode == 1) && S == 1 && y_tma;
+        auto pos = [&](int t) { return perm ? (t & ~15) + ((t & 1) << 3) + ((t & 15) >> 1) : t; };
         for (int i = tid; i < nmat * T; i += 128) {
             const int j = i / T, t = i - j * T, m = m0 + t;
             const float ws = __ldg(j == 0 ? w0_scale + (epi.scale_rows ? nb / epi.scale_rows : 0) : w1_scale);
-            rfac[j * kMaxT + t] = (m < M) ? __fdiv_rn(ws, s_act[m]) : 0.0f;
+            rfac[j * kMaxT + pos(t)] = (m < M) ? __fdiv_rn(ws, s_act[m]) : 0.0f;
         }
-        for (int t = tid; t < T; t += 128) sumq[t] = (m0 + t < M) ? sum_act[m0 + t] : 0;
+        for (int t = tid; t < T; t += 128) sumq[pos(t)] = (m0 + t < M) ? sum_act[m0 + t] : 0;
         int good = 1;
         if (lane == 0) good = mbar_wait(&bars->accfull, 0);
         if (!__shfl_sync(0xffffffffu, good, 0) && lane == 0) *abort_flag = 1;
@@ -387,7 +395,67 @@ gemm_i2s_tc_kernel(const __grid_constant__ CUtensorMap tmap_w0, const __grid_con
         named_bar_sync(2, 256);  // group 1's rfac/sumq are visible to group 0
     }
 
-    if (is_epi) {
+    if constexpr (MODE == 1) {
+        if (!split && y_tma && is_epi) {
+            // Staged FFN epilogue. Per 16-token chunk, each warp loads its quadrant's 16 gate lanes and the
+            // 16 up lanes of the same output columns with two 16x64b loads, so thread i holds gate and up of
+            // output column 16q + (i >> 2) + 8 (i & 1) for the tokens (i >> 1) & 1 + 2j, j = 0..7: the
+            // product needs no shuffle. Results go to shared memory as a [T][64] fp32 tile (the drained
+            // stage ring); once the group's four warps have written a chunk pair, one thread stores it with
+            // TMA (box 64 x 16), which also drops the rows past M.
+            const bool good = __all_sync(0xffffffffu, *abort_flag == 0);
+            const int col = 16 * q + (lane >> 2) + 8 * (lane & 1);  // output column within the CTA's 64
+            const int par = (lane >> 1) & 1;                           // token parity within the chunk
+            float* stage = reinterpret_cast<float*>(act_sm);           // [T][64] fp32
+            const uint32_t lane_g = tmem_base + ((uint32_t)(q * 32) << 16);
+            const uint32_t lane_u = tmem_base + ((uint32_t)(q * 32 + 16) << 16);
+            const bool issuer = (q == 0) && lane == 0;
+            auto finish16 = [&](int ch, const uint32_t (&g)[8], const uint32_t (&u)[8]) {
+                const int t0 = ch * 16, f = t0 + 8 * par;
+                const int4 sq0 = *reinterpret_cast<const int4*>(sumq + f);
+                const int4 sq1 = *reinterpret_cast<const int4*>(sumq + f + 4);
+                const float4 rg0 = *reinterpret_cast<const float4*>(rfac + f);
+                const float4 rg1 = *reinterpret_cast<const float4*>(rfac + f + 4);
+                const float4 ru0 = *reinterpret_cast<const float4*>(rfac + kMaxT + f);
+                const float4 ru1 = *reinterpret_cast<const float4*>(rfac + kMaxT + f + 4);
+                const int sq[8] = {sq0.x, sq0.y, sq0.z, sq0.w, sq1.x, sq1.y, sq1.z, sq1.w};
+                const float rg[8] = {rg0.x, rg0.y, rg0.z, rg0.w, rg1.x, rg1.y, rg1.z, rg1.w};
+                const float ru[8] = {ru0.x, ru0.y, ru0.z, ru0.w, ru1.x, ru1.y, ru1.z, ru1.w};
+                float* dst = stage + (t0 + par) * 64 + col;
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    const float gv = __fmul_rn((float)((int32_t)g[j] - sq[j]), rg[j]);
+                    const float uv = __fmul_rn((float)((int32_t)u[j] - sq[j]), ru[j]);
+                    const float rgv = gv > 0.0f ? gv : 0.0f;
+                    dst[j * 128] = __fmul_rn(__fmul_rn(rgv, rgv), uv);
+                }
+            };
+            for (int ch = 2 * egrp; ch < nchunk; ch += 4) {
+                const bool hb = ch + 1 < nchunk;
+                uint32_t g0[8], u0[8], g1[8], u1[8];
+                if (good) {
+                    tmem_ld_16x64b_x8(lane_g + chunk_col(ch), g0);
+                    tmem_ld_16x64b_x8(lane_u + chunk_col(ch), u0);
+                    if (hb) {
+                        tmem_ld_16x64b_x8(lane_g + chunk_col(ch + 1), g1);
+                        tmem_ld_16x64b_x8(lane_u + chunk_col(ch + 1), u1);
+                    }
+                    tc_wait_ld();
+                    finish16(ch, g0, u0);
+                    if (hb) finish16(ch + 1, g1, u1);
+                }
+                fence_proxy_async_smem();
+                named_bar_sync(3 + egrp, 128);  // the group's four quadrants of the chunk pair are staged
+                if (issuer && good) {
+                    tma_store_2d(&tmap_y, stage + ch * 16 * 64, nb, m0 + ch * 16);
+                    if (hb) tma_store_2d(&tmap_y, stage + (ch + 1) * 16 * 64, nb, m0 + ch * 16 + 16);
+                    bulk_commit();
+                }
+            }
+            if (issuer) bulk_wait_all();  // the staged tile is read and written before the CTA exits
+        }
+    }
+    if (is_epi && !(MODE == 1 && !split && y_tma)) {
         const bool good = __all_sync(0xffffffffu, *abort_flag == 0);
         const int gu = (mode == 1) ? (lane >> 4) : 0;                     // 0 gate / 1 up lane (mode 1)
         const int n = (mode == 1) ? nb + 16 * q + (lane & 15) : nb + row;  // output column
@@ -525,8 +593,9 @@ static cudaError_t launch_variant(const TcGemmArgs& a, cudaStream_t st) {
     attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 2;
-    return cudaLaunchKernelEx(&cfg, kfn, a.tmap_w0, a.tmap_w1, a.tmap_q, a.w0_scale, a.w1_scale, a.s, a.sums, a.y,
-                              a.ldy, a.M, a.N, a.Kp, a.T, a.bn_sub, a.nsub, a.epi, a.part);
+    return cudaLaunchKernelEx(&cfg, kfn, a.tmap_w0, a.tmap_w1, a.tmap_q, a.tmap_y, a.w0_scale, a.w1_scale, a.s,
+                              a.sums, a.y, a.ldy, a.M, a.N, a.Kp, a.T, a.bn_sub, a.nsub, a.epi, a.part,
+                              (MODE == 1 && a.y_tma) ? 1 : 0);
 }
 
 // Clusters of `size` CTAs of this kernel that can be resident at once on the current device (a cluster

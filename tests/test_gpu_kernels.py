@@ -190,6 +190,28 @@ def test_gate_up_sqrelu(b2s, orc):
     assert np.array_equal(p.cpu().numpy(), p_ref)
 
 
+@pytest.mark.parametrize("M,F,pad", [(300, 6912, 0), (203, 6880, 0), (300, 6912, 3), (17, 6912, 0)])
+def test_gate_up_sqrelu_tiles(b2s, orc, M, F, pad):
+    """Gate/up at tile counts that fill the GPU without split-K: the staged epilogue (shared-memory tile,
+    TMA stores that drop rows past M and columns past F), and with a row stride that is not a multiple of
+    16 bytes (pad=3) the direct-store epilogue."""
+    H = 2560
+    g = wl.rng(510 + M + pad)
+    wg, wu = wl.weight(g, F, H), wl.weight(g, F, H)
+    x = wl.activations(g, M, H)
+    bg, Wg = weight_dev(b2s, wg)
+    bu, Wu = weight_dev(b2s, wu)
+    q, s, u = q8_buffers(M, H)
+    b2s.act_quant(dev(x), q, s, u)
+    full = torch.full((M, F + pad), 7.0, dtype=torch.float32, device="cuda")
+    p = full[:, :F]
+    b2s.ffn_gate_up_sqrelu_q8(Wg, Wu, q, s, u, p)
+    sync_ok(b2s)
+    p_ref = orc.sqrelu_mul(orc.fast_mul_mat_i2s(wg.packed, x, F, 8), orc.fast_mul_mat_i2s(wu.packed, x, F, 8))
+    assert np.array_equal(p.cpu().numpy(), p_ref)
+    assert bool(full[:, F:].eq(7.0).all())  # nothing written past the F columns of a row
+
+
 @pytest.mark.parametrize("M", [300, 7])
 def test_ffn_block_config1(b2s, orc, M):
     """BitNet-b1.58-2B FFN block (H=2560, F=6912), prefill M=300 and a decode-size M."""
