@@ -149,44 +149,55 @@ act_quant_kernel(const float* __restrict__ x, int64_t ldx, const float* __restri
 }
 
 // ------------------------------------------------------------------------------------------------
-// Register-resident variant for rows of K <= 128 * 4 * VPT floats (16-byte aligned, K % 4 == 0): one
-// 128-thread CTA per row reads the row from HBM once into registers (VPT float4 per thread) and runs the
-// norm's sums, the absmax and the code sum as in-register partials combined by warp shuffles and one
-// 4-entry shared-memory step. KIND: 0 RMSNorm, 1 LayerNorm, 2 no norm. The fp32 operation sequence per
-// element is the one of act_quant_kernel / norm_kernel; only the (double) summation order differs.
-constexpr int kRowThreads = 128;
-
+// Register-resident variant for rows of K <= 8192 floats (16-byte aligned, K % 4 == 0): one CTA of TPR
+// threads per row (128 or 256, VPT = 4 or 8 float4 per thread) reads the row from memory once into
+// registers and runs the norm's sums, the absmax and the code sum as in-register partials combined by
+// warp shuffles and one TPR/32-entry shared-memory step. The kernel is latency-bound (a row of P is in
+// L2 when it runs): wide CTAs keep the per-thread dependency chains short, and the configuration keeps
+// every row of a prefill batch (a few hundred rows) resident in one wave (4 CTAs of 256 threads per SM).
+// KIND: 0 RMSNorm, 1 LayerNorm, 2 no norm. The fp32 operation sequence per element is the one of
+// act_quant_kernel / norm_kernel; only the (double) summation order differs.
+template <int NW>
 __device__ __forceinline__ double row_sum_d(double v, double* red) {
     v = warp_sum_d(v);
     if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
     __syncthreads();
-    const double t = ((red[0] + red[1]) + red[2]) + red[3];
+    double t = red[0];
+#pragma unroll
+    for (int w = 1; w < NW; ++w) t += red[w];
     __syncthreads();
     return t;
 }
+template <int NW>
 __device__ __forceinline__ float row_max_f(float v, float* red) {
     v = warp_max(v);
     if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
     __syncthreads();
-    const float t = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+    float t = red[0];
+#pragma unroll
+    for (int w = 1; w < NW; ++w) t = fmaxf(t, red[w]);
     __syncthreads();
     return t;
 }
+template <int NW>
 __device__ __forceinline__ int row_sum_i(int v, int* red) {
     v = warp_sum_i(v);
     if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
     __syncthreads();
-    const int t = red[0] + red[1] + red[2] + red[3];
+    int t = red[0];
+#pragma unroll
+    for (int w = 1; w < NW; ++w) t += red[w];
     __syncthreads();
     return t;
 }
 
-template <int KIND, bool QUANT, int VPT>
-__global__ void __launch_bounds__(kRowThreads)
+template <int KIND, bool QUANT, int TPR, int VPT>
+__global__ void __launch_bounds__(TPR)
 rowq_kernel(const float* __restrict__ x, int64_t ldx, const float* __restrict__ g, const float* __restrict__ b,
             float eps, int K, float* __restrict__ y, int64_t ldy, int8_t* __restrict__ q, int64_t ldq,
             float* __restrict__ s_out, int32_t* __restrict__ sum_out) {
-    __shared__ double red_d[4];
+    constexpr int NW = TPR / 32;
+    __shared__ double red_d[NW];
     float* red_f = reinterpret_cast<float*>(red_d);
     int* red_i = reinterpret_cast<int*>(red_d);
     const int64_t m = blockIdx.x;
@@ -197,7 +208,7 @@ rowq_kernel(const float* __restrict__ x, int64_t ldx, const float* __restrict__ 
     float4 r[VPT];
 #pragma unroll
     for (int i = 0; i < VPT; ++i) {
-        const int c = threadIdx.x + kRowThreads * i;
+        const int c = threadIdx.x + TPR * i;
         r[i] = (c < K4) ? x4[c] : make_float4(0.f, 0.f, 0.f, 0.f);
     }
     float mean = 0.0f, nscale = 1.0f;
@@ -210,13 +221,13 @@ rowq_kernel(const float* __restrict__ x, int64_t ldx, const float* __restrict__ 
             acc += (double)r[i].z;
             acc += (double)r[i].w;
         }
-        mean = (float)(row_sum_d(acc, red_d) / (double)K);
+        mean = (float)(row_sum_d<NW>(acc, red_d) / (double)K);
     }
     if (KIND != 2) {
         double acc2 = 0.0;
 #pragma unroll
         for (int i = 0; i < VPT; ++i) {
-            if (threadIdx.x + kRowThreads * i >= K4) continue;
+            if (threadIdx.x + TPR * i >= K4) continue;
             const float vx = (KIND == 1) ? __fsub_rn(r[i].x, mean) : r[i].x;
             const float vy = (KIND == 1) ? __fsub_rn(r[i].y, mean) : r[i].y;
             const float vz = (KIND == 1) ? __fsub_rn(r[i].z, mean) : r[i].z;
@@ -226,7 +237,7 @@ rowq_kernel(const float* __restrict__ x, int64_t ldx, const float* __restrict__ 
             acc2 += (double)__fmul_rn(vz, vz);
             acc2 += (double)__fmul_rn(vw, vw);
         }
-        const float var = (float)(row_sum_d(acc2, red_d) / (double)K);
+        const float var = (float)(row_sum_d<NW>(acc2, red_d) / (double)K);
         nscale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
     }
     const float4* g4 = reinterpret_cast<const float4*>(g);
@@ -241,7 +252,7 @@ rowq_kernel(const float* __restrict__ x, int64_t ldx, const float* __restrict__ 
     };
 #pragma unroll
     for (int i = 0; i < VPT; ++i) {
-        const int c = threadIdx.x + kRowThreads * i;
+        const int c = threadIdx.x + TPR * i;
         if (c >= K4) continue;
         const float4 gv = (KIND != 2 && g) ? g4[c] : make_float4(0.f, 0.f, 0.f, 0.f);
         const float4 bv = (KIND != 2 && b) ? b4[c] : make_float4(0.f, 0.f, 0.f, 0.f);
@@ -254,7 +265,7 @@ rowq_kernel(const float* __restrict__ x, int64_t ldx, const float* __restrict__ 
         float4* y4 = reinterpret_cast<float4*>(y + m * ldy);
 #pragma unroll
         for (int i = 0; i < VPT; ++i) {
-            const int c = threadIdx.x + kRowThreads * i;
+            const int c = threadIdx.x + TPR * i;
             if (c < K4) y4[c] = r[i];
         }
         return;
@@ -262,53 +273,56 @@ rowq_kernel(const float* __restrict__ x, int64_t ldx, const float* __restrict__ 
     float amax = 0.0f;
 #pragma unroll
     for (int i = 0; i < VPT; ++i) {
-        if (threadIdx.x + kRowThreads * i >= K4) continue;
+        if (threadIdx.x + TPR * i >= K4) continue;
         amax = fmaxf(amax, fmaxf(fmaxf(fabsf(r[i].x), fabsf(r[i].y)), fmaxf(fabsf(r[i].z), fabsf(r[i].w))));
     }
-    amax = row_max_f(amax, red_f);
+    amax = row_max_f<NW>(amax, red_f);
     const float s = actq_scale(amax);
     char4* q4 = reinterpret_cast<char4*>(q + m * ldq);
     int sum = 0;
 #pragma unroll
     for (int i = 0; i < VPT; ++i) {
-        const int c = threadIdx.x + kRowThreads * i;
+        const int c = threadIdx.x + TPR * i;
         if (c >= K4) continue;
         const int a0 = actq_round(r[i].x, s), a1 = actq_round(r[i].y, s);
         const int a2 = actq_round(r[i].z, s), a3 = actq_round(r[i].w, s);
         q4[c] = make_char4((signed char)a0, (signed char)a1, (signed char)a2, (signed char)a3);
         sum += a0 + a1 + a2 + a3;
     }
-    sum = row_sum_i(sum, red_i);
+    sum = row_sum_i<NW>(sum, red_i);
     if (threadIdx.x == 0) {
         s_out[m] = s;
         if (sum_out) sum_out[m] = sum;
     }
 }
 
-template <int KIND, bool QUANT, int VPT>
-static cudaError_t launch_rowq_vpt(const float* x, int64_t ldx, const float* g, const float* b, float eps,
+template <int KIND, bool QUANT, int TPR, int VPT>
+static cudaError_t launch_rowq_tpr(const float* x, int64_t ldx, const float* g, const float* b, float eps,
                                    int64_t M, int K, float* y, int64_t ldy, int8_t* q, int64_t ldq, float* s,
                                    int32_t* sums, cudaStream_t st) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)M);
-    cfg.blockDim = dim3(kRowThreads);
+    cfg.blockDim = dim3(TPR);
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, rowq_kernel<KIND, QUANT, VPT>, x, ldx, g, b, eps, K, y, ldy, q, ldq, s, sums);
+    return cudaLaunchKernelEx(&cfg, rowq_kernel<KIND, QUANT, TPR, VPT>, x, ldx, g, b, eps, K, y, ldy, q, ldq, s,
+                              sums);
 }
 
 template <int KIND, bool QUANT>
 static cudaError_t launch_rowq_k(const float* x, int64_t ldx, const float* g, const float* b, float eps, int64_t M,
                                  int K, float* y, int64_t ldy, int8_t* q, int64_t ldq, float* s, int32_t* sums,
                                  cudaStream_t st) {
-    const int per = (K / 4 + kRowThreads - 1) / kRowThreads;
-    if (per <= 4) return launch_rowq_vpt<KIND, QUANT, 4>(x, ldx, g, b, eps, M, K, y, ldy, q, ldq, s, sums, st);
-    if (per <= 8) return launch_rowq_vpt<KIND, QUANT, 8>(x, ldx, g, b, eps, M, K, y, ldy, q, ldq, s, sums, st);
-    return launch_rowq_vpt<KIND, QUANT, 16>(x, ldx, g, b, eps, M, K, y, ldy, q, ldq, s, sums, st);
+    const int K4 = K / 4;
+    if (K4 <= 128 * 4)
+        return launch_rowq_tpr<KIND, QUANT, 128, 4>(x, ldx, g, b, eps, M, K, y, ldy, q, ldq, s, sums, st);
+    if (K4 <= 256 * 4)
+        return launch_rowq_tpr<KIND, QUANT, 256, 4>(x, ldx, g, b, eps, M, K, y, ldy, q, ldq, s, sums, st);
+    return launch_rowq_tpr<KIND, QUANT, 256, 8>(x, ldx, g, b, eps, M, K, y, ldy, q, ldq, s, sums, st);
 }
 
 bool rowq_eligible(const float* x, int64_t ldx, const float* g, const float* b, int64_t K, const void* out,
@@ -316,7 +330,7 @@ bool rowq_eligible(const float* x, int64_t ldx, const float* g, const float* b, 
     auto a16 = [](const void* p) { return p == nullptr || (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
     const bool out_ok = quant ? ((reinterpret_cast<uintptr_t>(out) & 3) == 0 && ldo % 4 == 0)
                               : (a16(out) && ldo % 4 == 0);
-    return K > 0 && K % 4 == 0 && K <= 4 * kRowThreads * 16 && ldx % 4 == 0 && a16(x) && a16(g) && a16(b) && out_ok;
+    return K > 0 && K % 4 == 0 && K <= 4 * 256 * 8 && ldx % 4 == 0 && a16(x) && a16(g) && a16(b) && out_ok;
 }
 
 cudaError_t launch_rowq(int kind, bool quant, const float* x, int64_t ldx, const float* g, const float* b, float eps,
