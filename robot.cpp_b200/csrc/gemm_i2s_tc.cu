@@ -5,9 +5,10 @@
 // shared memory:
 //   * warp 4 (producer) TMA-loads, per 128-wide K step, the packed weight tile (128 rows x 32 bytes from
 //     local HBM, no multicast) and the int8 activation tile(s) (bn_sub rows x 128 bytes, 128B swizzle)
-//     into a 4-stage shared-memory ring. The weight tiles of the first ring round are requested before
-//     the kernel waits for its producer kernel (programmatic dependent launch), so their HBM latency
-//     overlaps the end of the preceding kernel;
+//     into a 4-stage shared-memory ring, weights and activations on separate barriers. The weight tiles
+//     of the first ring round are requested before the kernel waits for its producer kernel
+//     (programmatic dependent launch), so their HBM latency and their unpacking overlap the end of the
+//     preceding kernel;
 //   * warps 0-3 (converters) each own 32 TMEM lanes. A thread reads one weight row's 32 packed bytes and
 //     extracts the unsigned 2-bit codes {0,1,2} of each bit-plane with one shift and one mask per 4
 //     weights, then stores the 128 codes with one tcgen05.st.32x32b.x32 into the TMEM A stage that
@@ -52,13 +53,17 @@ constexpr int kThreads = 320;  // warps 0-3 converters+epilogue, 4 TMA, 5 MMA, 6
 constexpr uint32_t kTmemCols = 512;
 
 // One ring index s serves the shared-memory stage and the TMEM A stage of the same K step:
-//   full[s]     TMA bytes of stage s landed (expect_tx; producer arrives once)
+//   wfull[s]    the packed weight tile of stage s landed (expect_tx; producer arrives once). The weights
+//               have their own barrier so that the converters can unpack them before the (larger,
+//               later-requested) activation tile of the stage lands;
+//   full[s]     the activation tile(s) of stage s landed (expect_tx; producer arrives once)
 //   afull[s]    the converters wrote TMEM A stage s (one arrival per converter warp)
 //   consumed[s] the MMAs of stage s completed (one tcgen05.commit): frees both the shared-memory
 //               stage (producer may refill it) and the TMEM A stage (converters may overwrite it); the
 //               converters read stage s's packed weights before arriving on afull[s], i.e. before
 //               those MMAs were issued.
 struct alignas(8) Bars {
+    uint64_t wfull[kStages];
     uint64_t full[kStages];
     uint64_t afull[kStages];
     uint64_t consumed[kStages];
@@ -166,20 +171,22 @@ gemm_i2s_tc_kernel(const __grid_constant__ CUtensorMap tmap_w0, const __grid_con
     const int npre = nk < kStages ? nk : kStages;
     const uint32_t acc_stride = (uint32_t)((bn_sub + 31) / 32 * 32);
     const uint32_t a_col0 = acc_stride * (uint32_t)nsub;    // TMEM A ring after the accumulators (<= 320)
-    const uint32_t tx = (uint32_t)T * 128u + (uint32_t)kWStageBytes;
+    const uint32_t tx = (uint32_t)T * 128u;
 
     auto load_w = [&](int s, int kt) {
         uint8_t* wst = w_sm + (size_t)s * kWStageBytes;
+        mbar_arrive_expect_tx(&bars->wfull[s], (uint32_t)kWStageBytes);
         if (mode == 1) {
-            tma_load_2d(wst, &tmap_w0, &bars->full[s], kt * 32, nb);
-            tma_load_2d(wst + 64 * 32, &tmap_w1, &bars->full[s], kt * 32, nb);
+            tma_load_2d(wst, &tmap_w0, &bars->wfull[s], kt * 32, nb);
+            tma_load_2d(wst + 64 * 32, &tmap_w1, &bars->wfull[s], kt * 32, nb);
         } else {
-            tma_load_2d(wst, &tmap_w0, &bars->full[s], kt * 32, nb);
+            tma_load_2d(wst, &tmap_w0, &bars->wfull[s], kt * 32, nb);
         }
     };
 
     if (threadIdx.x == 128) {  // producer thread: barriers, descriptors, weights of the first ring round
         for (int i = 0; i < kStages; ++i) {
+            mbar_init(&bars->wfull[i], 1);
             mbar_init(&bars->full[i], 1);
             mbar_init(&bars->afull[i], 4);  // one arrival per converter warp
             mbar_init(&bars->consumed[i], 1);
@@ -191,10 +198,7 @@ gemm_i2s_tc_kernel(const __grid_constant__ CUtensorMap tmap_w0, const __grid_con
         tma_prefetch_desc(&tmap_q);
         tma_prefetch_desc(&tmap_w0);
         if (mode == 1) tma_prefetch_desc(&tmap_w1);
-        for (int i = 0; i < npre; ++i) {  // weights do not depend on the preceding kernel
-            mbar_arrive_expect_tx(&bars->full[i], tx);
-            load_w(i, kt0 + i);
-        }
+        for (int i = 0; i < npre; ++i) load_w(i, kt0 + i);  // weights do not depend on the preceding kernel
     }
     if (warp == 0) {
         tmem_alloc(&bars->tmem_slot, kTmemCols);
@@ -237,11 +241,11 @@ gemm_i2s_tc_kernel(const __grid_constant__ CUtensorMap tmap_w0, const __grid_con
             uint32_t ph = 0;
             for (int it = 0; it < nk; ++it) {
                 const int kt = kt0 + it;
-                if (it >= kStages) {  // first-round stages were armed before the setup barrier
+                if (it >= kStages) {  // first-round weights were requested before the setup barrier
                     if (!mbar_wait(&bars->consumed[s], ph ^ 1u) || *abort_flag) { *abort_flag = 1; break; }
-                    mbar_arrive_expect_tx(&bars->full[s], tx);
                     load_w(s, kt);
                 }
+                mbar_arrive_expect_tx(&bars->full[s], tx);
                 uint8_t* act = act_sm + (size_t)s * kActStageBytes;
                 for (int u = 0; u < nsub; ++u)
                     tma_load_2d(act + (size_t)u * bn_sub * 128, &tmap_q, &bars->full[s], kt * kBK, m0 + u * bn_sub);
@@ -251,6 +255,9 @@ gemm_i2s_tc_kernel(const __grid_constant__ CUtensorMap tmap_w0, const __grid_con
             if (*abort_flag) {  // drain copies still in flight before the CTA's shared memory goes away
                 for (int it = (issued > kStages ? issued - kStages : 0); it < issued; ++it)
                     mbar_wait(&bars->full[it % kStages], (uint32_t)(it / kStages) & 1u, 2u);
+                const int wissued = issued > npre ? issued : npre;  // first-round weights went out at start
+                for (int it = (wissued > kStages ? wissued - kStages : 0); it < wissued; ++it)
+                    mbar_wait(&bars->wfull[it % kStages], (uint32_t)(it / kStages) & 1u, 2u);
             }
         }
     } else if (warp == 5) {
@@ -264,8 +271,8 @@ gemm_i2s_tc_kernel(const __grid_constant__ CUtensorMap tmap_w0, const __grid_con
             int s = 0;
             uint32_t ph = 0;
             for (int it = 0; it < nk; ++it) {
-                // afull[s] is arrived only after the converters observed full[s]; waiting on full[s] as
-                // well makes the TMA bytes of the activation tile visible to this thread's MMAs.
+                // afull[s]: the unpacked weights of the stage are in TMEM; full[s]: its activation tile
+                // landed (the wait also makes those TMA-written bytes visible to this thread's MMAs).
                 if (!mbar_wait(&bars->afull[s], ph) || !mbar_wait(&bars->full[s], ph)) { *abort_flag = 1; break; }
                 tc_fence_after();
                 const uint32_t b_base = act_base + (uint32_t)s * kActStageBytes;
@@ -304,11 +311,11 @@ gemm_i2s_tc_kernel(const __grid_constant__ CUtensorMap tmap_w0, const __grid_con
         uint32_t ph = 0;
         for (int it = 0; it < nk; ++it) {
             int good = 1;
-            if (lane == 0) good = (*abort_flag == 0) && mbar_wait(&bars->full[s], ph);
+            if (lane == 0) good = (*abort_flag == 0) && mbar_wait(&bars->wfull[s], ph);
             if (!__shfl_sync(0xffffffffu, good, 0)) { ok = false; break; }
             // Every lane acquires the completed phase itself before reading the TMA-written bytes (the
             // phase cannot advance: stage s is refilled only after this warp arrives on afull[s]).
-            (void)mbar_try_wait(&bars->full[s], ph);
+            (void)mbar_try_wait(&bars->wfull[s], ph);
             const uint4* src = reinterpret_cast<const uint4*>(w_sm + (size_t)s * kWStageBytes + r_sm * 32);
             const uint4 p0 = src[0], p1 = src[1];
             if (lane == 0) good = mbar_wait(&bars->consumed[s], ph ^ 1u);  // TMEM A stage s is free
