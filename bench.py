@@ -62,15 +62,21 @@ N_SETS = 16
 def parse():
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=2000)
-    p.add_argument("--warmup", type=int, default=20)
+    p.add_argument("--steps", type=int, default=None,
+                   help="timed steps (default: 2000 FFN blocks; 10 BitVLA jobs of --observations each)")
+    p.add_argument("--warmup", type=int, default=None, help="untimed warm-up steps (default: 20 FFN, 3 BitVLA)")
     p.add_argument("--impl", default="b2s", choices=["b2s", "reference"])
     p.add_argument("--cpu-seconds", type=float, default=10.0, help="bounded CPU-baseline sample length")
     p.add_argument("--workload", default="ffn", choices=["ffn", "bitvla", "sweep"])
     p.add_argument("--observations", type=int, default=64, help="bitvla: observations in the whole job")
     p.add_argument("--obs-batch", type=int, default=8, help="bitvla: observations per forward")
     p.add_argument("--sweep-m", default="", help="sweep: comma-separated M values (default: all five)")
-    return p.parse_args()
+    a = p.parse_args()
+    if a.steps is None:
+        a.steps = 10 if a.workload == "bitvla" else 2000
+    if a.warmup is None:
+        a.warmup = 3 if a.workload == "bitvla" else 20
+    return a
 
 
 def dist_env():

@@ -152,6 +152,26 @@ def test_mul_mat_op_config0(b2s, orc, M):
     assert np.array_equal(y.cpu().numpy(), y_ref)
 
 
+@pytest.mark.parametrize("M,K,N", [(300, 6912, 2560), (37, 2560, 2560), (129, 1152, 4304), (20, 2560, 640),
+                                   (300, 2560, 1280), (250, 6912, 128)])
+def test_mul_mat_splitk_workspace(b2s, orc, M, K, N):
+    """MUL_MAT with a workspace at tile counts below the SM count: split-K over a cluster with the int32
+    partial tiles exchanged through the workspace in L2 (a workspace holding stale bytes must not matter)."""
+    g = wl.rng(700 + M + K + N)
+    w = wl.weight(g, N, K)
+    x = wl.activations(g, M, K)
+    buf, W = weight_dev(b2s, w)
+    xd = dev(x)
+    X = b2s.f32_tensor(xd)
+    ws = torch.full((b2s.mul_mat_workspace_size(W, X),), 0x5A, dtype=torch.uint8, device="cuda")  # not zero
+    y_ref = orc.fast_mul_mat_i2s(w.packed, x, N, 8)
+    for _ in range(2):  # the second call finds the first call's partials in the workspace
+        y = torch.full((M, N), float("nan"), dtype=torch.float32, device="cuda")
+        b2s.mul_mat(W, xd, y, ws)
+        sync_ok(b2s)
+        assert np.array_equal(y.cpu().numpy(), y_ref)
+
+
 def test_repack_rows_and_mul_mat(b2s, orc):
     """K % 128 != 0 (ViT FFN down 4304 -> 1152 shape, fewer rows): flattened i2_s -> row-padded."""
     K, N, M = 4304, 64, 20
