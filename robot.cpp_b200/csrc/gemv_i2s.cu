@@ -1,4 +1,4 @@
-// gemv_i2s.cu -- decode-size (M <= 16) i2_s x int8 GEMV with dp4a.
+// gemv_i2s.cu -- decode-size (M <= 16) i2_s x int8 GEMV: dp4a for one token, warp int8 MMAs for 2..16.
 //
 // Streams the packed 2-bit weights once from HBM with 128-bit loads and decodes them in registers:
 // a 16-byte half of a 32-byte i2_s block holds, for each of its 4 bit-planes g, 16 consecutive
@@ -166,6 +166,211 @@ gemv_i2s_kernel(const uint8_t* __restrict__ codes, const float* __restrict__ wsc
     }
 }
 
+// ------------------------------------------------------------------------------------------------
+// 2..16 tokens: warp-level int8 MMAs (mma.sync m16n8k32, A = unsigned codes, B = int8 activations).
+// At these token counts the dp4a loop above is bound by its instruction rate (each weight code is
+// multiplied M times); the MMA does 16 rows x 8 tokens x 32 k per instruction at 2048 MAC/cycle/SM, so
+// the kernel is bound by the weight stream instead. (tcgen05 is no help here: one tcgen05.mma costs
+// about 200 cycles per 32-wide K slice whatever N is, so 16 tokens would use 6% of it.)
+//
+// A warp owns 16 weight rows (one MMA row tile); thread (g = lane / 4, t = lane % 4) loads 8 bytes
+// (words 2t, 2t+1) of each 32-byte i2_s block of rows g and g + 8, so a warp load instruction reads 8 full
+// 32-byte sectors. For bit-plane p of the block, word 2t gives the codes of k = 32p + 8t + [0,4) and word
+// 2t+1 those of k = 32p + 8t + [4,8); they are the A fragment's k = 4t + [0,4) and 16 + 4t + [0,4), and
+// the B fragment reads the activations of exactly those k (one 8-byte shared-memory load per token):
+// the MMA's k order is a permutation of the true order, which an exact int32 sum does not see.
+// A CTA holds ROWT row tiles (16 ROWT rows); the 8 / ROWT warps of a row tile split its blocks and
+// reduce through shared memory. Every CTA stages all M x K activations, so more rows per CTA means
+// less of that (L2-resident, but read by every CTA at once) traffic per weight byte. The epilogue is
+// the dp4a kernel's.
+constexpr int kMmaQPad = 32;  // bytes added to each token row in shared memory (conflict-free 8-byte loads)
+
+__device__ __forceinline__ void mma_u8s8_16832(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                               uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint2 ld_stream_v2(const void* p) {
+    uint2 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p));
+    return v;
+}
+
+template <int NT, int ROWT>  // NT n-tiles of 8 tokens; ROWT row tiles of 16 rows per CTA
+__global__ void __launch_bounds__(kGemvWarps * 32)
+gemv_i2s_mma_kernel(const uint8_t* __restrict__ codes, const float* __restrict__ wscale, int N, int Kp,
+                    const int8_t* __restrict__ q, int64_t ldq, int K, int mrows, const float* __restrict__ s,
+                    const int32_t* __restrict__ sums, float* y, int64_t ldy, const Epilogue epi) {
+    constexpr int MT = 8 * NT, WPT = kGemvWarps / ROWT;  // warps per row tile
+    extern __shared__ __align__(16) uint8_t q_sm[];  // MT rows of (Kp + kMmaQPad) int8, zero past K / mrows
+    __shared__ int red[kGemvWarps][kGemvRows][MT];
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int rt = warp / WPT, ws = warp - rt * WPT;  // row tile, K share within it
+    const int g = lane >> 2, t = lane & 3;
+    const int row_a = (blockIdx.x * ROWT + rt) * kGemvRows + g, row_b = row_a + 8;
+    const bool ok_a = row_a < N, ok_b = row_b < N;
+    const int nblk = Kp / kQK;
+    const int per = (nblk + WPT - 1) / WPT;
+    const int b0 = min(nblk, ws * per), b1 = min(nblk, b0 + per);
+    const int64_t rbytes = Kp / 4;
+    const uint8_t* wa = codes + (int64_t)(ok_a ? row_a : 0) * rbytes + 8 * t;
+    const uint8_t* wb = codes + (int64_t)(ok_b ? row_b : 0) * rbytes + 8 * t;
+
+    uint2 va[kGemvUnroll], vb[kGemvUnroll];
+    int b = b0;
+    int cnt = min(kGemvUnroll, b1 - b);
+#pragma unroll
+    for (int u = 0; u < kGemvUnroll; ++u) {
+        if (u < cnt) {
+            va[u] = ok_a ? ld_stream_v2(wa + 32 * (b + u)) : make_uint2(0x55555555u, 0x55555555u);
+            vb[u] = ok_b ? ld_stream_v2(wb + 32 * (b + u)) : make_uint2(0x55555555u, 0x55555555u);
+        }
+    }
+
+    griddep_launch();  // the next kernel may start streaming its own weights now
+    griddep_wait();    // activations are produced by the preceding kernel
+
+    // Stage the activations of this warp's K share only: the mrows token rows x [128 b0, 128 b1) bytes at a
+    // row stride of Kp + kMmaQPad, zero past K (token rows past mrows are not staged: their B fragments are
+    // zero). The ROWT warps that share the K range split the copy and meet at a named barrier; no
+    // CTA-wide barrier stands between a warp and its MMAs.
+    const int qstride = Kp + kMmaQPad;  // bytes
+    const int c0 = 8 * b0, nck = 8 * (b1 - b0);  // 16-byte chunks of the share (8 per block)
+    const bool q_vec = ((ldq & 15) == 0) && ((reinterpret_cast<uintptr_t>(q) & 15) == 0) && (K % 16 == 0);
+    if (q_vec) {
+        for (int i = lane + 32 * rt; i < mrows * nck; i += 32 * ROWT) {
+            const int m = i / nck, k0 = 16 * (c0 + i - m * nck);
+            const bool live = k0 < K;
+            cp_async_16(q_sm + (size_t)m * qstride + k0, live ? (const void*)(q + (int64_t)m * ldq + k0) : (const void*)q,
+                        live ? 16u : 0u);
+        }
+        cp_async_wait_all();
+    } else {
+        for (int i = lane + 32 * rt; i < mrows * nck; i += 32 * ROWT) {
+            const int m = i / nck, k0 = 16 * (c0 + i - m * nck);
+            uint8_t tmp[16];
+            const int8_t* src = q + (int64_t)m * ldq + k0;
+#pragma unroll
+            for (int j = 0; j < 16; ++j) tmp[j] = (k0 + j < K) ? (uint8_t)src[j] : 0;
+            *reinterpret_cast<uint4*>(q_sm + (size_t)m * qstride + k0) = *reinterpret_cast<uint4*>(tmp);
+        }
+    }
+    if (ROWT == 1) __syncwarp();
+    else asm volatile("bar.sync %0, %1;" ::"r"(1 + ws), "r"(32 * ROWT) : "memory");
+
+    int acc[NT][4];
+#pragma unroll
+    for (int n = 0; n < NT; ++n)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) acc[n][i] = 0;
+    // token g of n-tile n reads its activations at q_sm + (8n + g) * qstride + 128 bb + 32 p + 8 t
+    const uint8_t* qg = q_sm + (size_t)g * qstride + 8 * t;
+
+    while (cnt > 0) {
+#pragma unroll
+        for (int u = 0; u < kGemvUnroll; ++u) {
+            if (u < cnt) {
+                const int bb = b + u;
+#pragma unroll
+                for (int p = 0; p < 4; ++p) {
+                    const int sh = 6 - 2 * p;
+                    const uint32_t a0 = (va[u].x >> sh) & 0x03030303u, a2 = (va[u].y >> sh) & 0x03030303u;
+                    const uint32_t a1 = (vb[u].x >> sh) & 0x03030303u, a3 = (vb[u].y >> sh) & 0x03030303u;
+#pragma unroll
+                    for (int n = 0; n < NT; ++n) {
+                        const uint2 bv = (8 * n + g < mrows)
+                            ? *reinterpret_cast<const uint2*>(qg + (size_t)(8 * n) * qstride + 128 * bb + 32 * p)
+                            : make_uint2(0u, 0u);
+                        mma_u8s8_16832(acc[n], a0, a1, a2, a3, bv.x, bv.y);
+                    }
+                }
+            }
+        }
+        b += cnt;
+        cnt = min(kGemvUnroll, b1 - b);
+#pragma unroll
+        for (int u = 0; u < kGemvUnroll; ++u) {
+            if (u < cnt) {
+                va[u] = ok_a ? ld_stream_v2(wa + 32 * (b + u)) : make_uint2(0x55555555u, 0x55555555u);
+                vb[u] = ok_b ? ld_stream_v2(wb + 32 * (b + u)) : make_uint2(0x55555555u, 0x55555555u);
+            }
+        }
+    }
+
+    // D fragment: acc[n][0..1] = row g, tokens 8n + 2t + {0,1}; acc[n][2..3] = row g + 8, same tokens.
+#pragma unroll
+    for (int n = 0; n < NT; ++n) {
+        red[warp][g][8 * n + 2 * t] = acc[n][0];
+        red[warp][g][8 * n + 2 * t + 1] = acc[n][1];
+        red[warp][g + 8][8 * n + 2 * t] = acc[n][2];
+        red[warp][g + 8][8 * n + 2 * t + 1] = acc[n][3];
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < ROWT * kGemvRows * MT; i += blockDim.x) {
+        const int rr = i / MT, m = i - rr * MT;             // rr: row within the CTA
+        const int rti = rr / kGemvRows, r16 = rr - rti * kGemvRows;
+        const int n = blockIdx.x * ROWT * kGemvRows + rr;
+        if (n < N && m < mrows) {
+            int tot = 0;
+#pragma unroll
+            for (int w = 0; w < WPT; ++w) tot += red[rti * WPT + w][r16][m];
+            const float rs = __fdiv_rn(__ldg(wscale + (epi.scale_rows ? n / epi.scale_rows : 0)), s[m]);
+            float v = __fmul_rn((float)(tot - sums[m]), rs);
+            if (epi.bias) v = __fadd_rn(v, epi.bias[n]);
+            if (epi.act == 1) v = gelu_tanh(v);
+            if (epi.residual) v = __fadd_rn(epi.residual[(int64_t)m * epi.ld_res + n], v);
+            y[(int64_t)m * ldy + n] = v;
+        }
+    }
+}
+
+template <int NT, int ROWT>
+static cudaError_t launch_mma_nt(const I2sWeight& w, const int8_t* q, int64_t ldq, int mrows, const float* s,
+                                 const int32_t* sums, float* y, int64_t ldy, const Epilogue& epi, cudaStream_t st) {
+    const size_t smem = (size_t)(8 * NT) * (size_t)(w.Kp + kMmaQPad);
+    auto kfn = gemv_i2s_mma_kernel<NT, ROWT>;
+    static int opted_in = 0;
+    if (smem + sizeof(int) * kGemvWarps * kGemvRows * 8 * NT > 48 * 1024 && (int)smem > opted_in) {
+        cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+        opted_in = (int)smem;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)ceil_div(w.N, ROWT * kGemvRows));
+    cfg.blockDim = dim3(kGemvWarps * 32);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kfn, w.codes, w.scale, (int)w.N, (int)w.Kp, q, ldq, (int)w.K, mrows, s, sums, y,
+                              ldy, epi);
+}
+
+// Row tiles per CTA for the MMA GEMV: enough CTAs to keep about one per SM streaming weights, and as few
+// as that allows, so the activations (staged by every CTA) are re-read as little as possible.
+static int mma_row_tiles(int64_t N) {
+    const int64_t tiles = ceil_div(N, kGemvRows);
+    if (tiles >= 4 * 148) return 4;
+    if (tiles >= 2 * 148) return 2;
+    return 1;
+}
+
+template <int NT>
+static cudaError_t launch_mma(const I2sWeight& w, const int8_t* q, int64_t ldq, int mrows, const float* s,
+                              const int32_t* sums, float* y, int64_t ldy, const Epilogue& epi, cudaStream_t st) {
+    switch (mma_row_tiles(w.N)) {
+        case 4: return launch_mma_nt<NT, 4>(w, q, ldq, mrows, s, sums, y, ldy, epi, st);
+        case 2: return launch_mma_nt<NT, 2>(w, q, ldq, mrows, s, sums, y, ldy, epi, st);
+        default: return launch_mma_nt<NT, 1>(w, q, ldq, mrows, s, sums, y, ldy, epi, st);
+    }
+}
+
 template <int MT>
 static cudaError_t launch_mt(const I2sWeight& w, const int8_t* q, int64_t ldq, int mrows, const float* s,
                              const int32_t* sums, float* y, int64_t ldy, const Epilogue& epi, cudaStream_t st) {
@@ -206,10 +411,8 @@ cudaError_t launch_gemv_i2s(const I2sWeight& w, const Q8Act& a, float* y, int64_
         if (ep.residual) ep.residual += m0 * ep.ld_res;
         cudaError_t e;
         if (mt == 1) e = launch_mt<1>(w, q, a.ldq, mt, s, sums, yy, ldy, ep, st);
-        else if (mt == 2) e = launch_mt<2>(w, q, a.ldq, mt, s, sums, yy, ldy, ep, st);
-        else if (mt <= 4) e = launch_mt<4>(w, q, a.ldq, mt, s, sums, yy, ldy, ep, st);
-        else if (mt <= 8) e = launch_mt<8>(w, q, a.ldq, mt, s, sums, yy, ldy, ep, st);
-        else e = launch_mt<16>(w, q, a.ldq, mt, s, sums, yy, ldy, ep, st);
+        else if (mt <= 8) e = launch_mma<1>(w, q, a.ldq, mt, s, sums, yy, ldy, ep, st);
+        else e = launch_mma<2>(w, q, a.ldq, mt, s, sums, yy, ldy, ep, st);
         if (e != cudaSuccess) return e;
     }
     return cudaGetLastError();
