@@ -172,6 +172,28 @@ def test_mul_mat_splitk_workspace(b2s, orc, M, K, N):
         assert np.array_equal(y.cpu().numpy(), y_ref)
 
 
+@pytest.mark.parametrize("M", [2, 11, 16])
+def test_gemv_mma_ragged_k(b2s, orc, M):
+    """The 2..16-token GEMV with K = 208 (row-padded to 256) and an activation row stride of 212 bytes (not a
+    multiple of 16: byte-wise staging), at token counts that leave part of the last 8-token MMA tile empty."""
+    K, N = 208, 64
+    g = wl.rng(450 + M)
+    w = wl.weight(g, N, K)
+    src = dev(w.packed)
+    dst = torch.zeros(b2s.i2s_r_nbytes(N, K), dtype=torch.uint8, device="cuda")
+    b2s.repack_rows(src, dst, N, K)
+    W = b2s.i2s_tensor(dst, N, K, rowpadded=True)
+    x = wl.activations(g, M, K)
+    q = torch.zeros((M, K + 4), dtype=torch.int8, device="cuda")[:, :K]
+    s = torch.zeros(M, dtype=torch.float32, device="cuda")
+    u = torch.zeros(M, dtype=torch.int32, device="cuda")
+    b2s.act_quant(dev(x), q, s, u)
+    y = torch.full((M, N), float("nan"), dtype=torch.float32, device="cuda")
+    b2s.mul_mat_q8(W, q, s, u, y, path=1)
+    sync_ok(b2s)
+    assert np.array_equal(y.cpu().numpy(), orc.mul_mat_i2s(w.packed, x, N))
+
+
 def test_repack_rows_and_mul_mat(b2s, orc):
     """K % 128 != 0 (ViT FFN down 4304 -> 1152 shape, fewer rows): flattened i2_s -> row-padded."""
     K, N, M = 4304, 64, 20
