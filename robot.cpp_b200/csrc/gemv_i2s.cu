@@ -170,8 +170,8 @@ gemv_i2s_kernel(const uint8_t* __restrict__ codes, const float* __restrict__ wsc
 // 2..16 tokens: warp-level int8 MMAs (mma.sync m16n8k32, A = unsigned codes, B = int8 activations).
 // At these token counts the dp4a loop above is bound by its instruction rate (each weight code is
 // multiplied M times); the MMA does 16 rows x 8 tokens x 32 k per instruction at 2048 MAC/cycle/SM, so
-// the kernel is bound by the weight stream instead. (tcgen05 is no help here: one tcgen05.mma costs
-// about 200 cycles per 32-wide K slice whatever N is, so 16 tokens would use 6% of it.)
+// the kernel is bound by the weight stream instead. The codes go from the loaded registers straight into
+// the MMA; the tcgen05 path would stage 128-row weight tiles through tensor memory for 16 tokens.
 //
 // A warp owns 16 weight rows (one MMA row tile); thread (g = lane / 4, t = lane % 4) loads 8 bytes
 // (words 2t, 2t+1) of each 32-byte i2_s block of rows g and g + 8, so a warp load instruction reads 8 full
