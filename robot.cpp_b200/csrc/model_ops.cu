@@ -349,9 +349,11 @@ attention_kernel(const float* __restrict__ q, int64_t ldq, const float* __restri
     float* P = KV + hd * kAtQ;         // [64][kAtPP] probabilities of the chunk
     float* alpha_sm = P + kAtQ * kAtPP;   // [64] per-row rescale of the chunk
     float* inv_sm = alpha_sm + kAtQ;      // [64] 1 / l at the end
-    const int h = blockIdx.y, g = h / (heads / kv_heads);
-    const int q0 = blockIdx.x * kAtQ;
-    const int64_t row0 = (int64_t)blockIdx.z * T;
+    // Grid (heads, batch, query blocks) with the last query block first: under a causal mask block b
+    // visits b + 1 key chunks, so launching the heaviest blocks first shortens the grid's tail.
+    const int h = blockIdx.x, g = h / (heads / kv_heads);
+    const int q0 = (int)(gridDim.z - 1u - blockIdx.z) * kAtQ;
+    const int64_t row0 = (int64_t)blockIdx.y * T;
     const float* qh = q + row0 * ldq + (int64_t)h * hd;
     const float* kh = k + row0 * ldk + (int64_t)g * hd;
     const float* vh = v + row0 * ldv + (int64_t)g * hd;
@@ -515,7 +517,7 @@ cudaError_t launch_attention(const float* q, int64_t ldq, const float* k, int64_
         opted = smem;
     }
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)ceil_div(T, kAtQ), (unsigned)heads, (unsigned)batch);
+    cfg.gridDim = dim3((unsigned)heads, (unsigned)batch, (unsigned)ceil_div(T, kAtQ));
     cfg.blockDim = dim3(kAtThreads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
