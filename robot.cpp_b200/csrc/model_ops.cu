@@ -197,26 +197,32 @@ cudaError_t launch_rope_table(float base, int hd, int n_pos, float2* tab, cudaSt
     return cudaGetLastError();
 }
 
-// Rotation from the table; row m is position m % period (sequences of `period` tokens stacked).
+// Rotation from the table; row m is position m % period (sequences of `period` tokens stacked). Grid
+// (pair blocks of a row, rows): each thread rotates one (head, i) pair of row blockIdx.y, with 32-bit index
+// arithmetic (a grid-stride loop that split a 64-bit element index with three divisions per element was
+// bound by those divisions).
 __global__ void rope_apply_kernel(float* __restrict__ x, int M, int n_heads, int hd, int64_t ld,
-                                  const float2* __restrict__ tab, int period) {
+                                  const float2* __restrict__ tab, int period, int m0) {
     griddep_wait();
     griddep_launch();
     const int half = hd / 2;
-    const int64_t total = (int64_t)M * n_heads * half;
-    for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
-        const int i = (int)(e % half);
-        const int h = (int)((e / half) % n_heads);
-        const int m = (int)(e / ((int64_t)half * n_heads));
-        rope_rotate(x + (int64_t)m * ld + (int64_t)h * hd, i, half, tab[(m % period) * half + i]);
-    }
+    const int j = blockIdx.x * blockDim.x + threadIdx.x;  // pair index within the row
+    const int m = m0 + (int)blockIdx.y;
+    if (j >= n_heads * half || m >= M) return;
+    const int h = j / half, i = j - h * half;
+    rope_rotate(x + (int64_t)m * ld + (int64_t)h * hd, i, half, tab[(m % period) * half + i]);
 }
 cudaError_t launch_rope_apply(float* x, int64_t M, int n_heads, int hd, int64_t ld, const float2* tab, int period,
                               cudaStream_t st) {
-    const int64_t total = M * n_heads * (hd / 2);
-    if (total <= 0) return cudaSuccess;
-    const unsigned blocks = (unsigned)((total + 255) / 256 < 148 * 8 ? (total + 255) / 256 : 148 * 8);
-    return launch_pdl(rope_apply_kernel, dim3(blocks), dim3(256), st, x, (int)M, n_heads, hd, ld, tab, period);
+    const int64_t pairs = (int64_t)n_heads * (hd / 2);
+    if (M <= 0 || pairs <= 0) return cudaSuccess;
+    for (int64_t m0 = 0; m0 < M; m0 += 65535) {  // grid y is at most 65535 rows per launch
+        const int64_t rows = (M - m0) < 65535 ? (M - m0) : 65535;
+        cudaError_t e = launch_pdl(rope_apply_kernel, dim3((unsigned)ceil_div(pairs, 256), (unsigned)rows), dim3(256),
+                                   st, x, (int)M, n_heads, hd, ld, tab, period, (int)m0);
+        if (e != cudaSuccess) return e;
+    }
+    return cudaSuccess;
 }
 
 // ------------------------------------------------------------------------------------------------ embeddings
