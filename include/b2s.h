@@ -80,6 +80,15 @@ int b2s_device_check(void);
  * wait timed out, bit 1 = a drain wait at kernel exit timed out. Synchronous. */
 int b2s_device_error(uint32_t *out_bits, int clear);
 
+/* Test hook for the failure path of the kernels' bounded waits (no counterpart in the reference; failure
+ * detection in the style of its bool/status-plus-message checks). Launches one CTA on `stream` that holds
+ * what a GEMM CTA holds -- 32 tensor-memory columns and one bulk copy of `bytes` bytes of src (device memory,
+ * 16-byte aligned, 16..4096 bytes, a multiple of 16) in flight -- then waits on an mbarrier that nothing
+ * arrives at, bounded by wait_limit_ns (at most one second). When the wait runs out the kernel sets bit 0
+ * of the device error word, waits (bounded) for its copy to land, frees its tensor memory and returns: the
+ * sequence every pipelined kernel follows on a timeout. Read the result with b2s_device_error. */
+int b2s_debug_wait_timeout(const void *src, size_t bytes, uint64_t wait_limit_ns, void *stream);
+
 /* ---------------------------------------------------------------- i2_s type traits (host) */
 /* Bytes of an i2_s tensor of nrow rows x n_per_row weights (ggml_nbytes for GGML_TYPE_I2_S). */
 size_t b2s_i2s_nbytes(int64_t nrow, int64_t n_per_row);
@@ -116,8 +125,8 @@ size_t b2s_mul_mat_workspace_size(const b2s_tensor *W, const b2s_tensor *X);
 
 /* The MUL_MAT node: Y = mul_mat(W, X). W: I2_S (ne0 % 128 == 0) or I2_S_R, ne=[K,N], contiguous;
  * X: F32 ne=[K,M], rows contiguous (nb[0] = 4); Y: F32 ne=[N,M], rows contiguous. Uses the caller's
- * workspace for the quantized activations; allocates nothing. Decode sizes (M <= 16) run the dp4a GEMV,
- * larger M the tcgen05 tensor-core GEMM. */
+ * workspace for the quantized activations; allocates nothing. Decode sizes run a GEMV (M = 1: dp4a on
+ * CUDA cores; M = 2..16: warp-level int8 MMAs), larger M the tcgen05 tensor-core GEMM. */
 int b2s_mul_mat(const b2s_tensor *W, const b2s_tensor *X, b2s_tensor *Y, void *workspace, size_t workspace_bytes,
                 void *stream);
 
@@ -127,18 +136,22 @@ int b2s_mul_mat(const b2s_tensor *W, const b2s_tensor *X, b2s_tensor *Y, void *w
  * (the scheduler has already allocated every buffer and hands the op no allocator), or a robot control
  * loop past start-up (cudaMalloc can synchronize the device and adds latency jitter). The quantized
  * activations go to a library-owned 4 MiB static device array instead (held by every GPU that loads the
- * library until the process exits). Limit: the call's scratch need, b2s_mul_mat_workspace_size(W, X)
- * (about M*roundup(K,16) + 8*M bytes), must be at most 4 MiB, else B2S_ERR_WORKSPACE and nothing is
- * launched. The first call on a device looks up the array's address; make it before any stream capture.
- * All calls on a device share the array: calls that overlap on the GPU race, so serialize them. */
+ * library until the process exits). Limit: the call's activation scratch, a256(M*roundup(K,16)) +
+ * a256(4*M) + a256(4*M) bytes (a256 = rounded up to a multiple of 256), must be at most 4 MiB, else
+ * B2S_ERR_WORKSPACE and nothing is launched; the rest of the array holds split-K partials, so the kernels
+ * are the ones b2s_mul_mat picks with a full workspace. Malformed W/X/Y get the status b2s_mul_mat gives.
+ * The first call on a device looks up the array's address and caches it for the process; make it before
+ * any stream capture, and do not reset the device afterwards. All calls on a device share the array:
+ * calls that overlap on the GPU race, so serialize them. */
 int b2s_mul_mat_static(const b2s_tensor *W, const b2s_tensor *X, b2s_tensor *Y, void *stream);
 
 /* MUL_MAT on already-quantized activations (producer-fused path): q [M x ldq] int8 (ldq % 16 == 0,
  * 16-byte aligned), s [M], sums [M] from b2s_act_quant / b2s_rms_norm_act_quant. Y [M x ldy] f32. */
 int b2s_mul_mat_q8(const b2s_tensor *W, const int8_t *q, int64_t ldq, const float *s, const int32_t *sums,
                    int64_t M, float *Y, int64_t ldy, void *stream);
-/* Same with the kernel chosen explicitly: path 0 = automatic, 1 = dp4a GEMV (any M, run in token groups
- * of 8), 2 = tcgen05 tensor-core GEMM (any M). For tests and tuning; results are identical. */
+/* Same with the kernel chosen explicitly: path 0 = automatic, 1 = GEMV (any M, run in token groups of up to
+ * 16: one token on dp4a, 2..16 on warp int8 MMAs), 2 = tcgen05 tensor-core GEMM (any M). For tests and
+ * tuning; results are identical. */
 int b2s_mul_mat_q8_ex(const b2s_tensor *W, const int8_t *q, int64_t ldq, const float *s, const int32_t *sums,
                       int64_t M, float *Y, int64_t ldy, int path, void *stream);
 
@@ -206,6 +219,29 @@ int b2s_embed_tokens_hash(const int32_t *tokens, int n, int dim, uint32_t seed, 
  * mask may be NULL. Rows contiguous, N columns (src/models/smolvla/action_expert.cpp:773). */
 int b2s_soft_max_ext(const float *x, const float *mask, int64_t mask_rows, int64_t M, int64_t N, float scale,
                      float *y, void *stream);
+
+/* ---------------------------------------------------------------- N-split over several GPUs (host side)
+ * A MUL_MAT of very many tokens split over the output rows of W across g GPUs (one process per GPU): rank r
+ * computes Y[:, n0_r:n1_r) and its GEMM epilogue stores the slice straight into the root GPU's output over
+ * NVLink (plain peer stores; no gather kernel, no collective). The root exports its output buffer with
+ * b2s_peer_export, the handle's 64 bytes reach the other ranks by any transport, each opens it with
+ * b2s_peer_open and passes (peer_ptr + n0_r floats, ldy = N) as the Y of b2s_mul_mat_q8. The reference
+ * has no multi-GPU path (one ggml CUDA backend on device 0, src/models/ggml_backend.cpp:62-202); these
+ * calls are the plumbing that replaces a ggml tensor split plus gather for this op. */
+#define B2S_PEER_HANDLE_BYTES 64
+/* Balanced contiguous split of n_rows over `world` ranks: rank gets [*n0, *n1) (sizes differ by <= 1). */
+int b2s_nsplit_range(int64_t n_rows, int world, int rank, int64_t *n0, int64_t *n1);
+/* Host: rows [r0, r1) of an I2_S (n_per_row % 128 == 0) or I2_S_R tensor as a standalone tensor of the same
+ * type (code bytes, then the 32-byte trailer with the fp32 scale) at dst. Returns the bytes written, 0 on
+ * error. */
+size_t b2s_i2s_shard_rows(const void *src, int32_t type, int64_t nrow, int64_t n_per_row, int64_t r0, int64_t r1,
+                          void *dst);
+/* CUDA IPC export of a device allocation of the current device into B2S_PEER_HANDLE_BYTES bytes. */
+int b2s_peer_export(const void *dev_ptr, void *handle, size_t handle_bytes);
+/* Maps a peer's exported allocation into the current device's address space (peer access enabled). */
+int b2s_peer_open(const void *handle, size_t handle_bytes, void **dev_ptr);
+/* Unmaps a pointer returned by b2s_peer_open. */
+int b2s_peer_close(void *dev_ptr);
 
 #ifdef __cplusplus
 }

@@ -270,61 +270,180 @@ static void quant(const float *x, int64_t M, int64_t K, q8buf *qb, int nth) {
     orc_fast_act_quant_padded(x, M, K, qb->q, qb->s, qb->sums, nth);
 }
 
-/* y = W q (+ bias) (GELU if act) (+ residual, res may alias y): the device epilogue order. */
-static void linear(const tern_w *w, const q8buf *qb, int64_t M, float *y, int64_t ldy, const float *bias, int act,
-                   const float *res, int nth) {
-    float *tmp = (float *)malloc(sizeof(float) * (size_t)(M * w->N));
-    orc_fast_gemm_q8_rp(w->codes, w->tiles, w->N, w->K, qb->q, qb->s, qb->sums, M, tmp, w->N, nth);
-    for (int64_t m = 0; m < M; ++m)
-        for (int64_t n = 0; n < w->N; ++n) {
-            float v = tmp[m * w->N + n];
-            if (bias) v = v + bias[n];
-            if (act == 1) v = orc_gelu_tanh(v);
-            if (res) v = res[m * ldy + n] + v;
-            y[m * ldy + n] = v;
+typedef struct { const float *tmp; int64_t N, ldy; float *y; const float *bias, *res; int act; } epi_ctx;
+
+static void epi_range(void *p, int64_t m0, int64_t m1) {
+    const epi_ctx *c = (const epi_ctx *)p;
+    for (int64_t m = m0; m < m1; ++m)
+        for (int64_t n = 0; n < c->N; ++n) {
+            float v = c->tmp[m * c->N + n];
+            if (c->bias) v = v + c->bias[n];
+            if (c->act == 1) v = orc_gelu_tanh(v);
+            if (c->res) v = c->res[m * c->ldy + n] + v;
+            c->y[m * c->ldy + n] = v;
         }
-    free(tmp);
 }
 
-/* ---------------------------------------------------------------- forward */
-int orc_bitvla_forward(const b2s_bitvla_config *cfg, uint32_t seed, int batch, const float *images,
-                       const int32_t *tokens, float *hidden, float *actions, int nth) {
+/* y = W q (+ bias) (GELU if act) (+ residual, res may alias y): the device epilogue order. `tmp` holds
+ * M x N floats. */
+static void linear(const tern_w *w, const q8buf *qb, int64_t M, float *y, int64_t ldy, const float *bias, int act,
+                   const float *res, float *tmp, int nth) {
+    orc_fast_gemm_q8_rp(w->codes, w->tiles, w->N, w->K, qb->q, qb->s, qb->sums, M, tmp, w->N, nth);
+    epi_ctx c = {tmp, w->N, ldy, y, bias, res, act};
+    orc_parallel_for(M, nth, epi_range, &c);
+}
+
+/* ---------------------------------------------------------------- the model (weights generated once) */
+typedef struct {
+    float *ln1_w, *ln1_b, *qkv_b, *o_b, *ln2_w, *ln2_b, *fc1_b, *fc2_b;
+    tern_w qkv, wo, fc1, fc2;
+} vit_layer;
+typedef struct {
+    float *attn_norm, *attn_sub, *ffn_norm, *ffn_sub;
+    tern_w qkv, wo, gate, up, down;
+} dec_layer;
+typedef struct orc_bitvla_model orc_bitvla_model;
+struct orc_bitvla_model {
+    b2s_bitvla_config c;
+    uint32_t seed;
+    float *patch_w, *patch_b, *pos, *post_w, *post_b, *c1_b, *c2_b, *final_norm, *act_w, *act_b;
+    tern_w c1, c2;
+    vit_layer *vit;
+    dec_layer *dec;
+};
+
+orc_bitvla_model *orc_bitvla_create(const b2s_bitvla_config *cfg, uint32_t seed, int nth) {
+    orc_bitvla_model *m = (orc_bitvla_model *)calloc(1, sizeof(orc_bitvla_model));
     const b2s_bitvla_config c = *cfg;
+    m->c = c;
+    m->seed = seed;
+    const int P = c.patch, G = c.image_size / P, np = G * G, kdim = 3 * P * P;
+    const int D = c.vit_hidden, F = c.vit_ffn, H = c.dec_hidden, KV = c.dec_kv_heads * c.head_dim;
+    const float pa = 1.0f / sqrtf((float)kdim);
+    m->patch_w = uniform_new((int64_t)D * kdim, seed, 1, -pa, pa);
+    m->patch_b = uniform_new(D, seed, 2, -0.02f, 0.02f);
+    m->pos = uniform_new((int64_t)np * D, seed, 3, -0.02f, 0.02f);
+    m->vit = (vit_layer *)calloc((size_t)(c.vit_layers > 0 ? c.vit_layers : 1), sizeof(vit_layer));
+    for (int l = 0; l < c.vit_layers; ++l) {
+        vit_layer *L = &m->vit[l];
+        const uint32_t base = 0x100u + 16u * (uint32_t)l;
+        L->ln1_w = uniform_new(D, seed, base + 0, 0.9f, 1.1f);
+        L->ln1_b = uniform_new(D, seed, base + 1, -0.02f, 0.02f);
+        const int64_t rows3[3] = {D, D, D};
+        const uint32_t ids3[3] = {base + 2, base + 3, base + 4};
+        L->qkv = make_tern(3, rows3, ids3, D, seed, nth);
+        L->qkv_b = (float *)malloc(sizeof(float) * 3 * (size_t)D);
+        for (int j = 0; j < 3; ++j) orc_bv_gen_uniform(L->qkv_b + j * D, D, seed, base + 5 + j, -0.02f, 0.02f);
+        L->wo = make_tern1(D, base + 8, D, seed, nth);
+        L->o_b = uniform_new(D, seed, base + 9, -0.02f, 0.02f);
+        L->ln2_w = uniform_new(D, seed, base + 10, 0.9f, 1.1f);
+        L->ln2_b = uniform_new(D, seed, base + 11, -0.02f, 0.02f);
+        L->fc1 = make_tern1(F, base + 12, D, seed, nth);
+        L->fc1_b = uniform_new(F, seed, base + 13, -0.02f, 0.02f);
+        L->fc2 = make_tern1(D, base + 14, F, seed, nth);
+        L->fc2_b = uniform_new(D, seed, base + 15, -0.02f, 0.02f);
+    }
+    m->post_w = uniform_new(D, seed, 4, 0.9f, 1.1f);
+    m->post_b = uniform_new(D, seed, 5, -0.02f, 0.02f);
+    m->c1 = make_tern1(c.conn_hidden, 6, D, seed, nth);
+    m->c1_b = uniform_new(c.conn_hidden, seed, 7, -0.02f, 0.02f);
+    m->c2 = make_tern1(H, 8, c.conn_hidden, seed, nth);
+    m->c2_b = uniform_new(H, seed, 9, -0.02f, 0.02f);
+    m->dec = (dec_layer *)calloc((size_t)(c.dec_layers > 0 ? c.dec_layers : 1), sizeof(dec_layer));
+    for (int l = 0; l < c.dec_layers; ++l) {
+        dec_layer *L = &m->dec[l];
+        const uint32_t base = 0x10000u + 16u * (uint32_t)l;
+        L->attn_norm = uniform_new(H, seed, base + 0, 0.9f, 1.1f);
+        const int64_t rows3[3] = {H, KV, KV};
+        const uint32_t ids3[3] = {base + 1, base + 2, base + 3};
+        L->qkv = make_tern(3, rows3, ids3, H, seed, nth);
+        L->attn_sub = uniform_new(H, seed, base + 4, 0.9f, 1.1f);
+        L->wo = make_tern1(H, base + 5, H, seed, nth);
+        L->ffn_norm = uniform_new(H, seed, base + 6, 0.9f, 1.1f);
+        L->gate = make_tern1(c.dec_ffn, base + 7, H, seed, nth);
+        L->up = make_tern1(c.dec_ffn, base + 8, H, seed, nth);
+        L->ffn_sub = uniform_new(c.dec_ffn, seed, base + 9, 0.9f, 1.1f);
+        L->down = make_tern1(H, base + 10, c.dec_ffn, seed, nth);
+    }
+    m->final_norm = uniform_new(H, seed, 10, 0.9f, 1.1f);
+    const int NA = c.action_chunk * c.action_dim;
+    const float aa = 1.0f / sqrtf((float)H);
+    m->act_w = uniform_new((int64_t)NA * H, seed, 11, -aa, aa);
+    m->act_b = uniform_new(NA, seed, 12, -0.02f, 0.02f);
+    return m;
+}
+
+void orc_bitvla_free(orc_bitvla_model *m) {
+    if (!m) return;
+    for (int l = 0; l < m->c.vit_layers; ++l) {
+        vit_layer *L = &m->vit[l];
+        free(L->ln1_w); free(L->ln1_b); free(L->qkv_b); free(L->o_b); free(L->ln2_w); free(L->ln2_b);
+        free(L->fc1_b); free(L->fc2_b);
+        free_tern(&L->qkv); free_tern(&L->wo); free_tern(&L->fc1); free_tern(&L->fc2);
+    }
+    for (int l = 0; l < m->c.dec_layers; ++l) {
+        dec_layer *L = &m->dec[l];
+        free(L->attn_norm); free(L->attn_sub); free(L->ffn_norm); free(L->ffn_sub);
+        free_tern(&L->qkv); free_tern(&L->wo); free_tern(&L->gate); free_tern(&L->up); free_tern(&L->down);
+    }
+    free(m->vit); free(m->dec);
+    free(m->patch_w); free(m->patch_b); free(m->pos); free(m->post_w); free(m->post_b); free(m->c1_b);
+    free(m->c2_b); free(m->final_norm); free(m->act_w); free(m->act_b);
+    free_tern(&m->c1); free_tern(&m->c2);
+    free(m);
+}
+
+/* Patch embedding rows: y = (bias + pos) + acc, acc = fmaf(col[k], w[d][k], acc), k ascending. */
+typedef struct { const orc_bitvla_model *m; const float *images; float *vx; } patch_ctx;
+
+static void patch_range(void *p, int64_t r0, int64_t r1) {
+    const patch_ctx *pc = (const patch_ctx *)p;
+    const b2s_bitvla_config *c = &pc->m->c;
+    const int P = c->patch, G = c->image_size / P, np = G * G, kdim = 3 * P * P, D = c->vit_hidden;
+    float *col = (float *)malloc(sizeof(float) * (size_t)kdim);
+    for (int64_t r = r0; r < r1; ++r) {
+        const int64_t b = r / np;
+        const int p_ = (int)(r % np), py = p_ / G, px = p_ % G;
+        for (int k = 0; k < kdim; ++k) {
+            const int ch = k / (P * P), ky = (k / P) % P, kx = k % P;
+            col[k] = pc->images[((b * 3 + ch) * c->image_size + (py * P + ky)) * c->image_size + (px * P + kx)];
+        }
+        for (int d = 0; d < D; ++d) {
+            float acc = 0.0f;
+            for (int k = 0; k < kdim; ++k) acc = fmaf(col[k], pc->m->patch_w[(int64_t)d * kdim + k], acc);
+            const float pre = pc->m->patch_b[d] + pc->m->pos[(int64_t)p_ * D + d];
+            pc->vx[r * D + d] = pre + acc;
+        }
+    }
+    free(col);
+}
+
+int orc_bitvla_run(const orc_bitvla_model *m, int batch, const float *images, const int32_t *tokens, float *hidden,
+                   float *actions, int nth) {
+    const b2s_bitvla_config c = m->c;
+    const uint32_t seed = m->seed;
     const int P = c.patch, G = c.image_size / P, np = G * G, seq = np + c.n_text;
     const int D = c.vit_hidden, F = c.vit_ffn, H = c.dec_hidden, KV = c.dec_kv_heads * c.head_dim;
     const int64_t Mv = (int64_t)batch * np, Md = (int64_t)batch * seq;
     int kmax = D;
     const int ks[4] = {F, c.conn_hidden, H, c.dec_ffn};
     for (int i = 0; i < 4; ++i) kmax = ks[i] > kmax ? ks[i] : kmax;
+    int nmax = 3 * D;
+    const int ns[5] = {F, c.conn_hidden, H + 2 * KV, c.dec_ffn, H};
+    for (int i = 0; i < 5; ++i) nmax = ns[i] > nmax ? ns[i] : nmax;
     const int64_t Mmax = Md > Mv ? Md : Mv;
     q8buf qb;
     qb.q = (int8_t *)malloc((size_t)(Mmax * rup(kmax, QK)));
     qb.s = (float *)malloc(sizeof(float) * (size_t)Mmax);
     qb.sums = (int32_t *)malloc(sizeof(int32_t) * (size_t)Mmax);
+    float *tmp_lin = (float *)malloc(sizeof(float) * (size_t)(Mmax * nmax));
 
-    /* ---- patch embedding: y = (bias + pos) + acc, acc = fmaf(col[k], w[d][k], acc), k ascending ---- */
-    const int kdim = 3 * P * P;
-    const float pa = 1.0f / sqrtf((float)kdim);
-    float *patch_w = uniform_new((int64_t)D * kdim, seed, 1, -pa, pa);
-    float *patch_b = uniform_new(D, seed, 2, -0.02f, 0.02f);
-    float *pos = uniform_new((int64_t)np * D, seed, 3, -0.02f, 0.02f);
+    /* ---- patch embedding ---- */
     float *vx = (float *)malloc(sizeof(float) * (size_t)(Mv * D));
-    float *col = (float *)malloc(sizeof(float) * (size_t)kdim);
-    for (int b = 0; b < batch; ++b)
-        for (int p = 0; p < np; ++p) {
-            const int py = p / G, px = p % G;
-            for (int k = 0; k < kdim; ++k) {
-                const int ch = k / (P * P), ky = (k / P) % P, kx = k % P;
-                col[k] = images[(((int64_t)b * 3 + ch) * c.image_size + (py * P + ky)) * c.image_size + (px * P + kx)];
-            }
-            for (int d = 0; d < D; ++d) {
-                float acc = 0.0f;
-                for (int k = 0; k < kdim; ++k) acc = fmaf(col[k], patch_w[(int64_t)d * kdim + k], acc);
-                const float pre = patch_b[d] + pos[(int64_t)p * D + d];
-                vx[((int64_t)b * np + p) * D + d] = pre + acc;
-            }
-        }
-    free(col); free(patch_w); free(patch_b); free(pos);
+    {
+        patch_ctx pc = {m, images, vx};
+        orc_parallel_for(Mv, nth, patch_range, &pc);
+    }
 
     /* ---- ViT ---- */
     float *vqkv = (float *)malloc(sizeof(float) * (size_t)(Mv * 3 * D));
@@ -333,57 +452,34 @@ int orc_bitvla_forward(const b2s_bitvla_config *cfg, uint32_t seed, int batch, c
     float *tmp = (float *)malloc(sizeof(float) * (size_t)(Mv * D));
     const float vscale = 1.0f / sqrtf((float)(D / c.vit_heads));
     for (int l = 0; l < c.vit_layers; ++l) {
-        const uint32_t base = 0x100u + 16u * (uint32_t)l;
-        float *ln1_w = uniform_new(D, seed, base + 0, 0.9f, 1.1f), *ln1_b = uniform_new(D, seed, base + 1, -0.02f, 0.02f);
-        const int64_t rows3[3] = {D, D, D};
-        const uint32_t ids3[3] = {base + 2, base + 3, base + 4};
-        tern_w qkv = make_tern(3, rows3, ids3, D, seed, nth);
-        float *qkv_b = (float *)malloc(sizeof(float) * 3 * (size_t)D);
-        for (int j = 0; j < 3; ++j) orc_bv_gen_uniform(qkv_b + j * D, D, seed, base + 5 + j, -0.02f, 0.02f);
-        tern_w wo = make_tern1(D, base + 8, D, seed, nth);
-        float *o_b = uniform_new(D, seed, base + 9, -0.02f, 0.02f);
-        float *ln2_w = uniform_new(D, seed, base + 10, 0.9f, 1.1f), *ln2_b = uniform_new(D, seed, base + 11, -0.02f, 0.02f);
-        tern_w fc1 = make_tern1(F, base + 12, D, seed, nth);
-        float *fc1_b = uniform_new(F, seed, base + 13, -0.02f, 0.02f);
-        tern_w fc2 = make_tern1(D, base + 14, F, seed, nth);
-        float *fc2_b = uniform_new(D, seed, base + 15, -0.02f, 0.02f);
-
-        orc_layer_norm(vx, ln1_w, ln1_b, Mv, D, c.vit_eps, tmp);
+        const vit_layer *L = &m->vit[l];
+        orc_layer_norm(vx, L->ln1_w, L->ln1_b, Mv, D, c.vit_eps, tmp);
         quant(tmp, Mv, D, &qb, nth);
-        linear(&qkv, &qb, Mv, vqkv, 3 * D, qkv_b, 0, NULL, nth);
+        linear(&L->qkv, &qb, Mv, vqkv, 3 * D, L->qkv_b, 0, NULL, tmp_lin, nth);
         orc_attention(vqkv, 3 * D, 0, D, 2 * D, batch, c.vit_heads, c.vit_heads, D / c.vit_heads, np, 0, vscale,
                       vattn, D, nth);
         quant(vattn, Mv, D, &qb, nth);
-        linear(&wo, &qb, Mv, vx, D, o_b, 0, vx, nth);
-        orc_layer_norm(vx, ln2_w, ln2_b, Mv, D, c.vit_eps, tmp);
+        linear(&L->wo, &qb, Mv, vx, D, L->o_b, 0, vx, tmp_lin, nth);
+        orc_layer_norm(vx, L->ln2_w, L->ln2_b, Mv, D, c.vit_eps, tmp);
         quant(tmp, Mv, D, &qb, nth);
-        linear(&fc1, &qb, Mv, vh, F, fc1_b, 1, NULL, nth);
+        linear(&L->fc1, &qb, Mv, vh, F, L->fc1_b, 1, NULL, tmp_lin, nth);
         quant(vh, Mv, F, &qb, nth);
-        linear(&fc2, &qb, Mv, vx, D, fc2_b, 0, vx, nth);
-
-        free(ln1_w); free(ln1_b); free(qkv_b); free(o_b); free(ln2_w); free(ln2_b); free(fc1_b); free(fc2_b);
-        free_tern(&qkv); free_tern(&wo); free_tern(&fc1); free_tern(&fc2);
+        linear(&L->fc2, &qb, Mv, vx, D, L->fc2_b, 0, vx, tmp_lin, nth);
     }
 
     /* ---- connector ---- */
     float *dx = (float *)malloc(sizeof(float) * (size_t)(Md * H));
     {
-        float *post_w = uniform_new(D, seed, 4, 0.9f, 1.1f), *post_b = uniform_new(D, seed, 5, -0.02f, 0.02f);
-        tern_w c1 = make_tern1(c.conn_hidden, 6, D, seed, nth);
-        float *c1_b = uniform_new(c.conn_hidden, seed, 7, -0.02f, 0.02f);
-        tern_w c2 = make_tern1(H, 8, c.conn_hidden, seed, nth);
-        float *c2_b = uniform_new(H, seed, 9, -0.02f, 0.02f);
         float *ch = (float *)malloc(sizeof(float) * (size_t)(Mv * c.conn_hidden));
         float *co = (float *)malloc(sizeof(float) * (size_t)(Mv * H));
-        orc_layer_norm(vx, post_w, post_b, Mv, D, c.vit_eps, tmp);
+        orc_layer_norm(vx, m->post_w, m->post_b, Mv, D, c.vit_eps, tmp);
         quant(tmp, Mv, D, &qb, nth);
-        linear(&c1, &qb, Mv, ch, c.conn_hidden, c1_b, 1, NULL, nth);
+        linear(&m->c1, &qb, Mv, ch, c.conn_hidden, m->c1_b, 1, NULL, tmp_lin, nth);
         quant(ch, Mv, c.conn_hidden, &qb, nth);
-        linear(&c2, &qb, Mv, co, H, c2_b, 0, NULL, nth);
+        linear(&m->c2, &qb, Mv, co, H, m->c2_b, 0, NULL, tmp_lin, nth);
         for (int b = 0; b < batch; ++b)
             memcpy(dx + (int64_t)b * seq * H, co + (int64_t)b * np * H, sizeof(float) * (size_t)np * H);
-        free(post_w); free(post_b); free(c1_b); free(c2_b); free(ch); free(co);
-        free_tern(&c1); free_tern(&c2);
+        free(ch); free(co);
     }
     free(vqkv); free(vattn); free(vh); free(tmp); free(vx);
 
@@ -407,69 +503,58 @@ int orc_bitvla_forward(const b2s_bitvla_config *cfg, uint32_t seed, int batch, c
     orc_rope_table(c.rope_theta, c.head_dim, seq, cs);
     const float dscale = 1.0f / sqrtf((float)c.head_dim);
     for (int l = 0; l < c.dec_layers; ++l) {
-        const uint32_t base = 0x10000u + 16u * (uint32_t)l;
-        float *attn_norm = uniform_new(H, seed, base + 0, 0.9f, 1.1f);
-        const int64_t rows3[3] = {H, KV, KV};
-        const uint32_t ids3[3] = {base + 1, base + 2, base + 3};
-        tern_w qkv = make_tern(3, rows3, ids3, H, seed, nth);
-        float *attn_sub = uniform_new(H, seed, base + 4, 0.9f, 1.1f);
-        tern_w wo = make_tern1(H, base + 5, H, seed, nth);
-        float *ffn_norm = uniform_new(H, seed, base + 6, 0.9f, 1.1f);
-        tern_w gate = make_tern1(c.dec_ffn, base + 7, H, seed, nth);
-        tern_w up = make_tern1(c.dec_ffn, base + 8, H, seed, nth);
-        float *ffn_sub = uniform_new(c.dec_ffn, seed, base + 9, 0.9f, 1.1f);
-        tern_w down = make_tern1(H, base + 10, c.dec_ffn, seed, nth);
-
-        orc_rms_norm(dx, attn_norm, Md, H, c.dec_eps, dn);
+        const dec_layer *L = &m->dec[l];
+        orc_rms_norm(dx, L->attn_norm, Md, H, c.dec_eps, dn);
         quant(dn, Md, H, &qb, nth);
-        linear(&qkv, &qb, Md, dqkv, ldqkv, NULL, 0, NULL, nth);
+        linear(&L->qkv, &qb, Md, dqkv, ldqkv, NULL, 0, NULL, tmp_lin, nth);
         orc_rope_neox(dqkv, Md, c.dec_heads + c.dec_kv_heads, c.head_dim, ldqkv, cs, seq, 0);
         orc_attention(dqkv, ldqkv, 0, H, H + KV, batch, c.dec_heads, c.dec_kv_heads, c.head_dim, seq, 1, dscale, dattn,
                       H, nth);
-        orc_rms_norm(dattn, attn_sub, Md, H, c.dec_eps, dn);
+        orc_rms_norm(dattn, L->attn_sub, Md, H, c.dec_eps, dn);
         quant(dn, Md, H, &qb, nth);
-        linear(&wo, &qb, Md, dx, H, NULL, 0, dx, nth);
-        orc_rms_norm(dx, ffn_norm, Md, H, c.dec_eps, dn);
+        linear(&L->wo, &qb, Md, dx, H, NULL, 0, dx, tmp_lin, nth);
+        orc_rms_norm(dx, L->ffn_norm, Md, H, c.dec_eps, dn);
         quant(dn, Md, H, &qb, nth);
-        linear(&gate, &qb, Md, dg, c.dec_ffn, NULL, 0, NULL, nth);
-        linear(&up, &qb, Md, du, c.dec_ffn, NULL, 0, NULL, nth);
+        linear(&L->gate, &qb, Md, dg, c.dec_ffn, NULL, 0, NULL, tmp_lin, nth);
+        linear(&L->up, &qb, Md, du, c.dec_ffn, NULL, 0, NULL, tmp_lin, nth);
         orc_sqrelu_mul(dg, du, Md * c.dec_ffn, dg);
-        orc_rms_norm(dg, ffn_sub, Md, c.dec_ffn, c.dec_eps, dn);
+        orc_rms_norm(dg, L->ffn_sub, Md, c.dec_ffn, c.dec_eps, dn);
         quant(dn, Md, c.dec_ffn, &qb, nth);
-        linear(&down, &qb, Md, dx, H, NULL, 0, dx, nth);
-
-        free(attn_norm); free(attn_sub); free(ffn_norm); free(ffn_sub);
-        free_tern(&qkv); free_tern(&wo); free_tern(&gate); free_tern(&up); free_tern(&down);
+        linear(&L->down, &qb, Md, dx, H, NULL, 0, dx, tmp_lin, nth);
     }
-    float *fn = uniform_new(H, seed, 10, 0.9f, 1.1f);
     float *hid = hidden ? hidden : (float *)malloc(sizeof(float) * (size_t)(Md * H));
-    orc_rms_norm(dx, fn, Md, H, c.dec_eps, hid);
+    orc_rms_norm(dx, m->final_norm, Md, H, c.dec_eps, hid);
 
     /* ---- action head: lane l of a warp sums c = l, l + 32, ...; xor-butterfly; lane 0 + bias ---- */
     if (actions) {
         const int NA = c.action_chunk * c.action_dim;
-        const float aa = 1.0f / sqrtf((float)H);
-        float *aw = uniform_new((int64_t)NA * H, seed, 11, -aa, aa);
-        float *ab = uniform_new(NA, seed, 12, -0.02f, 0.02f);
         for (int b = 0; b < batch; ++b)
             for (int j = 0; j < NA; ++j) {
                 const float *hr = hid + ((int64_t)b * seq + seq - 1) * H;
                 float lanes[32], nxt[32];
                 for (int ln = 0; ln < 32; ++ln) {
                     float acc = 0.0f;
-                    for (int cc = ln; cc < H; cc += 32) acc = acc + hr[cc] * aw[(int64_t)j * H + cc];
+                    for (int cc = ln; cc < H; cc += 32) acc = acc + hr[cc] * m->act_w[(int64_t)j * H + cc];
                     lanes[ln] = acc;
                 }
                 for (int off = 16; off > 0; off >>= 1) {
                     for (int ln = 0; ln < 32; ++ln) nxt[ln] = lanes[ln] + lanes[ln ^ off];
                     memcpy(lanes, nxt, sizeof(lanes));
                 }
-                actions[(int64_t)b * NA + j] = lanes[0] + ab[j];
+                actions[(int64_t)b * NA + j] = lanes[0] + m->act_b[j];
             }
-        free(aw); free(ab);
     }
     if (!hidden) free(hid);
-    free(fn); free(cs); free(dqkv); free(dattn); free(dg); free(du); free(dn); free(dx);
+    free(cs); free(dqkv); free(dattn); free(dg); free(du); free(dn); free(dx); free(tmp_lin);
     free(qb.q); free(qb.s); free(qb.sums);
     return 0;
+}
+
+int orc_bitvla_forward(const b2s_bitvla_config *cfg, uint32_t seed, int batch, const float *images,
+                       const int32_t *tokens, float *hidden, float *actions, int nth) {
+    orc_bitvla_model *m = orc_bitvla_create(cfg, seed, nth);
+    if (!m) return -1;
+    const int rc = orc_bitvla_run(m, batch, images, tokens, hidden, actions, nth);
+    orc_bitvla_free(m);
+    return rc;
 }

@@ -92,6 +92,12 @@ def lib():
         L.orc_attention.restype = None
         L.orc_attention.argtypes = [_f32p, _i64, _i64, _i64, _i64, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
                                     C.c_int, C.c_float, _f32p, _i64, C.c_int]
+        L.orc_bitvla_create.restype = C.c_void_p
+        L.orc_bitvla_create.argtypes = [C.c_void_p, C.c_uint32, C.c_int]
+        L.orc_bitvla_free.restype = None
+        L.orc_bitvla_free.argtypes = [C.c_void_p]
+        L.orc_bitvla_run.restype = C.c_int
+        L.orc_bitvla_run.argtypes = [C.c_void_p, C.c_int, _f32p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int]
         L.orc_bitvla_forward.restype = C.c_int
         L.orc_bitvla_forward.argtypes = [C.c_void_p, C.c_uint32, C.c_int, _f32p, C.c_void_p, C.c_void_p,
                                          C.c_void_p, C.c_int]
@@ -281,6 +287,42 @@ def bitvla_forward(cfg: BitVLAConfig, seed: int, images: np.ndarray, tokens: np.
                                   hidden.ctypes.data_as(C.c_void_p), actions.ctypes.data_as(C.c_void_p), nth)
     assert rc == 0
     return hidden, actions
+
+
+class BitVLAModel:
+    """The oracle's BitVLA-shape model with every weight generated once (host memory), for repeated
+    forwards (the timed CPU baseline); bitvla_forward regenerates the weights on each call."""
+
+    def __init__(self, cfg: BitVLAConfig, seed: int, nthreads: int = 0):
+        self.cfg = cfg
+        self.nth = nthreads or (os.cpu_count() or 1)
+        self._h = lib().orc_bitvla_create(C.byref(cfg), seed & 0xFFFFFFFF, self.nth)
+        if not self._h:
+            raise MemoryError("orc_bitvla_create failed")
+
+    def forward(self, images: np.ndarray, tokens: np.ndarray, want_hidden: bool = False):
+        images = _c(images, np.float32)
+        tokens = _c(tokens, np.int32)
+        B = images.shape[0]
+        cfg = self.cfg
+        hidden = np.zeros((B * bitvla_seq_len(cfg), cfg.dec_hidden), np.float32) if want_hidden else None
+        actions = np.zeros((B, cfg.action_chunk * cfg.action_dim), np.float32)
+        rc = lib().orc_bitvla_run(self._h, B, images, tokens.ctypes.data_as(C.c_void_p),
+                                  hidden.ctypes.data_as(C.c_void_p) if hidden is not None else None,
+                                  actions.ctypes.data_as(C.c_void_p), self.nth)
+        assert rc == 0
+        return hidden, actions
+
+    def close(self):
+        if self._h:
+            lib().orc_bitvla_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 def bv_param_bits(seed: int, tensor: int, idx: int) -> int:

@@ -35,8 +35,10 @@ EXPORTED = [
     "b2s_mul_mat", "b2s_mul_mat_q8", "b2s_mul_mat_q8_ex", "b2s_ffn_gate_up_sqrelu_q8",
     "b2s_ffn_block_workspace_size", "b2s_ffn_block", "b2s_soft_max_ext", "b2s_mul_mat_static",
     "b2s_mul_mat_q8_epi", "b2s_norm", "b2s_norm_act_quant", "b2s_rope_neox", "b2s_attention",
-    "b2s_patch_embed", "b2s_embed_tokens_hash",
+    "b2s_patch_embed", "b2s_embed_tokens_hash", "b2s_nsplit_range", "b2s_i2s_shard_rows", "b2s_peer_export",
+    "b2s_peer_open", "b2s_peer_close", "b2s_debug_wait_timeout",
 ]
+PEER_HANDLE_BYTES = 64
 
 
 class B2SError(RuntimeError):
@@ -96,6 +98,12 @@ def lib():
             "b2s_patch_embed": (C.c_int, [_vp, C.c_int, C.c_int, C.c_int, C.c_int, _vp, _vp, _vp, C.c_int, _vp, _i64,
                                           _vp]),
             "b2s_embed_tokens_hash": (C.c_int, [_vp, C.c_int, C.c_int, C.c_uint32, _vp, _i64, _vp]),
+            "b2s_nsplit_range": (C.c_int, [_i64, C.c_int, C.c_int, C.POINTER(_i64), C.POINTER(_i64)]),
+            "b2s_i2s_shard_rows": (C.c_size_t, [_vp, C.c_int32, _i64, _i64, _i64, _i64, _vp]),
+            "b2s_peer_export": (C.c_int, [_vp, _vp, C.c_size_t]),
+            "b2s_peer_open": (C.c_int, [_vp, C.c_size_t, C.POINTER(_vp)]),
+            "b2s_peer_close": (C.c_int, [_vp]),
+            "b2s_debug_wait_timeout": (C.c_int, [_vp, C.c_size_t, C.c_uint64, _vp]),
         }
         for name, (res, args) in sig.items():
             f = getattr(L, name)
@@ -116,6 +124,12 @@ def check(status: int) -> None:
 
 def version() -> str:
     return lib().b2s_version().decode()
+
+
+def debug_wait_timeout(src, wait_limit_ns: int, stream=None) -> None:
+    """Runs the bounded-wait failure path once (b2s_debug_wait_timeout) on a device byte buffer `src`."""
+    check(lib().b2s_debug_wait_timeout(_ptr(src), src.numel() * src.element_size(), int(wait_limit_ns),
+                                       _stream(stream)))
 
 
 def device_error(clear: bool = True) -> int:
@@ -300,3 +314,43 @@ def embed_tokens_hash(tokens, dim: int, seed: int, y, stream=None) -> None:
     n = tokens.shape[0]
     check(lib().b2s_embed_tokens_hash(_ptr(tokens), n, int(dim), int(seed) & 0xFFFFFFFF, _ptr(y), y.stride(0),
                                       _stream(stream)))
+
+
+# ---------------------------------------------------------------------------------------------- N-split host side
+def nsplit_range(n_rows: int, world: int, rank: int) -> tuple[int, int]:
+    """Rows [n0, n1) of an n_rows-row weight owned by `rank` of `world` (balanced, contiguous)."""
+    n0, n1 = _i64(0), _i64(0)
+    check(lib().b2s_nsplit_range(int(n_rows), int(world), int(rank), C.byref(n0), C.byref(n1)))
+    return int(n0.value), int(n1.value)
+
+
+def i2s_shard_rows(packed, N: int, K: int, r0: int, r1: int, rowpadded: bool = False):
+    """Host: rows [r0, r1) of an i2_s tensor (numpy uint8 bytes) as a standalone tensor of the same type."""
+    import numpy as np
+    packed = np.ascontiguousarray(packed, dtype=np.uint8)
+    rb = ((K + 127) // 128 * 128 // 4) if rowpadded else K // 4
+    out = np.zeros(max(r1 - r0, 0) * rb + 32, np.uint8)
+    n = lib().b2s_i2s_shard_rows(packed.ctypes.data, TYPE_I2_S_R if rowpadded else TYPE_I2_S, int(N), int(K),
+                                 int(r0), int(r1), out.ctypes.data)
+    if n == 0:
+        raise B2SError(B2S_ERR_INVALID_ARG, last_error())
+    return out
+
+
+def peer_export(dev_ptr: int) -> bytes:
+    """CUDA IPC handle (64 bytes) of a device allocation of the current device."""
+    h = (C.c_uint8 * PEER_HANDLE_BYTES)()
+    check(lib().b2s_peer_export(int(dev_ptr), h, PEER_HANDLE_BYTES))
+    return bytes(h)
+
+
+def peer_open(handle: bytes) -> int:
+    """Device address (in this process, current device) of a peer's exported allocation."""
+    h = (C.c_uint8 * PEER_HANDLE_BYTES).from_buffer_copy(handle)
+    p = _vp()
+    check(lib().b2s_peer_open(h, PEER_HANDLE_BYTES, C.byref(p)))
+    return int(p.value)
+
+
+def peer_close(dev_ptr: int) -> None:
+    check(lib().b2s_peer_close(int(dev_ptr)))

@@ -347,14 +347,17 @@ size_t splitk_ws_bytes(int64_t M, int64_t n_out, int rows_per_cta) {
 
 int set_last_error(int code, const char* msg) { return fail(code, "%s", msg); }
 
-size_t mul_mat_scratch_bytes(const void* Wv, const void* Xv) {
+int mul_mat_scratch_bytes(const void* Wv, const void* Xv, size_t* need) {
     const b2s_tensor* W = static_cast<const b2s_tensor*>(Wv);
     const b2s_tensor* X = static_cast<const b2s_tensor*>(Xv);
     b2s::I2sWeight w{};
     int64_t M = 0, Kx = 0, ldx = 0;
-    if (weight_view(W, &w, "W") != B2S_OK) return 0;
-    if (f32_rows(X, "X", &M, &Kx, &ldx) != B2S_OK) return 0;
-    return act_ws(M, w.K).total;
+    int rc;
+    *need = 0;
+    if ((rc = weight_view(W, &w, "W"))) return rc;
+    if ((rc = f32_rows(X, "X", &M, &Kx, &ldx))) return rc;
+    *need = act_ws(M, w.K).total;
+    return B2S_OK;
 }
 
 int mul_mat_into_scratch(const void* Wv, const void* Xv, void* Yv, void* scratch, size_t capacity, cudaStream_t st) {
@@ -382,7 +385,11 @@ int mul_mat_into_scratch(const void* Wv, const void* Xv, void* Yv, void* scratch
                                              l.ldq, s, sums, st),
                        "act_quant launch")))
         return rc;
-    return mul_mat_q8_impl(w, q, l.ldq, s, sums, M, static_cast<float*>(Y->data), ldy, 0, st);
+    // The rest of the region (past the activation layout) holds split-K partials, as in b2s_mul_mat.
+    const size_t sk_off = a256(l.total);
+    void* sk = capacity > sk_off ? static_cast<void*>(ws + sk_off) : nullptr;
+    return mul_mat_q8_impl(w, q, l.ldq, s, sums, M, static_cast<float*>(Y->data), ldy, 0, st, b2s::Epilogue{}, sk,
+                           sk ? capacity - sk_off : 0);
 }
 
 }  // namespace b2s

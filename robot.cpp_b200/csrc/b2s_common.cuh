@@ -129,16 +129,17 @@ __device__ __forceinline__ uint64_t global_timer_ns() {
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
     return t;
 }
-// Bounded wait on one mbarrier phase: gives up after about one second of wall time (try_wait may
-// itself suspend for an implementation-defined interval, so the bound is on %globaltimer, not on a
-// poll count). Returns false on timeout and records it in g_device_error.
+// Bounded wait on one mbarrier phase: gives up after limit_ns of wall time (one second by default;
+// try_wait may itself suspend for an implementation-defined interval, so the bound is on %globaltimer,
+// not on a poll count). Returns false on timeout and records it in g_device_error.
 constexpr uint64_t kWaitLimitNs = 1000000000ull;
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned int err_bit = 1u) {
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned int err_bit = 1u,
+                                          uint64_t limit_ns = kWaitLimitNs) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = global_timer_ns();
     for (uint32_t i = 0;; ++i) {
         if (mbar_try_wait(bar, parity)) return true;
-        if ((i & 15u) == 15u && global_timer_ns() - t0 > kWaitLimitNs) break;
+        if ((i & 15u) == 15u && global_timer_ns() - t0 > limit_ns) break;
         if (i > 64) __nanosleep(64);
     }
     atomicOr(&g_device_error, err_bit);
@@ -151,6 +152,15 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const void* tmap, ui
         "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], "
         "[%2];" ::"r"(smem_u32(smem_dst)),
         "l"(tmap), "r"(smem_u32(bar)), "r"(x), "r"(y)
+        : "memory");
+}
+// Non-tensor bulk copy global -> shared completing on an mbarrier (addresses 16-byte aligned, bytes a
+// multiple of 16).
+__device__ __forceinline__ void bulk_load(void* smem_dst, const void* gsrc, uint32_t bytes, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(smem_dst)),
+        "l"(gsrc), "r"(bytes), "r"(smem_u32(bar))
         : "memory");
 }
 __device__ __forceinline__ void tma_prefetch_desc(const void* tmap) {

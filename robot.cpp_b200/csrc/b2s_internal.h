@@ -175,11 +175,13 @@ class GgufFile {
 int set_last_error(int code, const char* msg);
 
 // Scratch bytes the MUL_MAT node needs for its int8 activations, scales and sums (same layout as the
-// caller workspace of b2s_mul_mat); 0 with the error set if W or X is malformed.
-size_t mul_mat_scratch_bytes(const void* W, const void* X);
+// caller workspace of b2s_mul_mat) in *need; returns the same status (and message) b2s_mul_mat gives a
+// malformed W or X.
+int mul_mat_scratch_bytes(const void* W, const void* X, size_t* need);
 
 // The MUL_MAT node of b2s_mul_mat run into a scratch region the caller already owns
-// (`scratch` device pointer, `capacity` bytes, 256-byte aligned). Validates exactly like b2s_mul_mat.
+// (`scratch` device pointer, `capacity` bytes, 256-byte aligned): the activation layout first, the rest
+// for split-K partials. Validates exactly like b2s_mul_mat.
 int mul_mat_into_scratch(const void* W, const void* X, void* Y, void* scratch, size_t capacity, cudaStream_t st);
 
 }  // namespace b2s

@@ -1,6 +1,7 @@
 // bitvla_engine.cu -- random-init BitVLA-shape forward on the library's kernels (C ABI in b2s_bitvla.h).
 //
-// Per observation: patch embedding (cuBLAS SGEMM) -> vit_layers x ViT block -> post-LayerNorm ->
+// Per observation: patch embedding (the library's fixed-order fp32 kernel) -> vit_layers x ViT block ->
+// post-LayerNorm ->
 // two-layer ternary connector -> [image tokens | hash-embedded text tokens] -> dec_layers x decoder layer
 // -> final RMSNorm -> linear action head on the last token. The ViT block mirrors
 // src/models/smolvla/vision.cpp:305-345, the decoder layer src/models/pi0/vlm.cpp:196-246, with every

@@ -9,12 +9,16 @@
 //
 // Rules of this entry point:
 //   * Capacity: kStaticScratchBytes (4 MiB) per device, held by every GPU that loads the library until the
-//     process exits. A call whose scratch need (b2s_mul_mat_workspace_size for the same W and X: about
-//     M * roundup(K,16) + 8*M bytes, e.g. M <= 300 tokens at K = 6912 or M <= 1600 at K = 2560) exceeds
-//     it returns B2S_ERR_WORKSPACE with a message and launches nothing.
+//     process exits. The call's scratch need is its activation layout: a256(M * roundup(K,16)) bytes of
+//     int8 codes + a256(4*M) of scales + a256(4*M) of sums (a256 = rounded up to 256 bytes), e.g. M <= 300
+//     tokens at K = 6912 or M <= 1600 at K = 2560. A call that needs more returns B2S_ERR_WORKSPACE with a
+//     message and launches nothing. Whatever the activations leave free holds split-K partials, as the
+//     workspace of b2s_mul_mat does, so both entry points pick the same kernels.
 //   * Nothing here allocates: no cudaMalloc, no cudaFree, no allocating library routine.
 //   * The first call on a device looks up the array's device address (cudaGetSymbolAddress, with that
-//     device current) and caches it; make that first call before any stream capture begins.
+//     device current) and caches it for the life of the process; make that first call before any stream
+//     capture begins, and do not reset the device (cudaDeviceReset) after it: a new context reloads the
+//     module and the cached address would no longer name this array.
 //   * Every call on a device shares the one array, and the array keeps the previous call's contents.
 //     Calls whose work overlaps on the GPU (other streams, other host threads) race on it: serialize
 //     them, e.g. on one stream. Nothing in the array needs to start at zero: each call writes every
@@ -60,8 +64,8 @@ int scratch_address(void** out) {
 extern "C" int b2s_mul_mat_static(const b2s_tensor* W, const b2s_tensor* X, b2s_tensor* Y, void* stream) {
     int rc = b2s_device_check();
     if (rc) return rc;
-    const size_t need = b2s::mul_mat_scratch_bytes(W, X);
-    if (need == 0) return B2S_ERR_INVALID_ARG;  // message already set by the validation
+    size_t need = 0;
+    if ((rc = b2s::mul_mat_scratch_bytes(W, X, &need))) return rc;  // the status b2s_mul_mat gives
     if (need > kStaticScratchBytes) {
         char msg[200];
         snprintf(msg, sizeof(msg),

@@ -90,6 +90,34 @@ def test_full_depth_end_to_end(b2s, orc):
     assert np.array_equal(h, h_ref) and np.array_equal(a, a_ref)
 
 
+def test_full_depth_batch8_rows(b2s, orc):
+    """The benched batch: a full-depth forward of 8 observations equals each observation run alone (batch 1,
+    bit for bit), and one of them equals the oracle's forward within the end-to-end bar."""
+    from b2s import bitvla, device_error
+    cfg = bitvla.default_config()
+    img, tok = inputs(orc.bitvla_config(), 8, 51)
+    m = bitvla.Model(cfg, 1234, max_batch=8)
+    seq = m.seq_len
+    h8 = torch.full((8 * seq, cfg.dec_hidden), float("nan"), dtype=torch.float32, device="cuda")
+    a8 = torch.full((8, cfg.action_chunk * cfg.action_dim), float("nan"), dtype=torch.float32, device="cuda")
+    m.forward(torch.from_numpy(img).cuda(), torch.from_numpy(tok).cuda(), h8, a8)
+    h1 = torch.full((seq, cfg.dec_hidden), float("nan"), dtype=torch.float32, device="cuda")
+    a1 = torch.full((1, cfg.action_chunk * cfg.action_dim), float("nan"), dtype=torch.float32, device="cuda")
+    for b in range(8):
+        m.forward(torch.from_numpy(img[b:b + 1]).cuda(), torch.from_numpy(tok[b:b + 1]).cuda(), h1, a1)
+        torch.cuda.synchronize()
+        assert torch.equal(h8[b * seq:(b + 1) * seq], h1), b
+        assert torch.equal(a8[b], a1[0]), b
+    assert device_error() == 0
+    h8n, a8n = h8.cpu().numpy(), a8.cpu().numpy()
+    m.close()
+    om = orc.BitVLAModel(orc.bitvla_config(), 1234)
+    h_ref, a_ref = om.forward(img[5:6], tok[5:6], want_hidden=True)
+    om.close()
+    assert max_abs_rel(h8n[5 * seq:6 * seq], h_ref) <= 1e-3 and max_abs_rel(a8n[5:6], a_ref) <= 1e-3
+    assert np.array_equal(h8n[5 * seq:6 * seq], h_ref) and np.array_equal(a8n[5:6], a_ref)
+
+
 def test_predict_host_path(b2s):
     """predict() (uint8 HWC host images -> host actions) equals forward() on value/255 images."""
     from b2s import bitvla

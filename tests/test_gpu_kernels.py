@@ -5,6 +5,8 @@ max-abs-rel <= 1e-5 (max |y - y_ref| / max |y_ref|) and, because every fp32 step
 same IEEE operations in the same order, also checked for exact equality where stated. The softmax's exp
 is the library's deterministic det_expf on both sides, so softmax is compared exactly too.
 """
+import os
+
 import numpy as np
 import pytest
 
@@ -106,7 +108,7 @@ def run_q8(b2s, orc, M, K, N, path, seed):
         acc = orc.gemm_i32(w.t, q_ref)
         y_ref = orc.rescale(acc, s_ref, float(w.scale))
     else:
-        y_ref = orc.fast_mul_mat_i2s(w.packed, x, N, 8)
+        y_ref = orc.fast_mul_mat_i2s(w.packed, x, N, os.cpu_count() or 8)
     return y.cpu().numpy(), y_ref
 
 
@@ -129,6 +131,16 @@ def test_tensor_core_path(b2s, orc, M, K, N):
 @pytest.mark.parametrize("M,K,N", [(4096, 2560, 2560), (600, 2560, 6912), (513, 6912, 2560)])
 def test_tensor_core_large(b2s, orc, M, K, N):
     y, y_ref = run_q8(b2s, orc, M, K, N, path=2, seed=M + K + N)
+    assert max_abs_rel(y, y_ref) <= TOL
+    assert np.array_equal(y, y_ref)
+
+
+@pytest.mark.parametrize("M,K,N", [(16384, 2560, 2560), (16384, 2560, 6912), (16384, 6912, 2560),
+                                   (16384, 1152, 4304), (4096, 1152, 4304)])
+def test_persistent_gemm_sweep_sizes(b2s, orc, M, K, N):
+    """The roofline sweep's large points through the automatic path (the persistent tcgen05 kernel), bit for
+    bit against the oracle: every (K, N) of the sweep at M = 16384, and the K = 1152 ViT FFN shape at 4096."""
+    y, y_ref = run_q8(b2s, orc, M, K, N, path=0, seed=M + 3 * K + N)
     assert max_abs_rel(y, y_ref) <= TOL
     assert np.array_equal(y, y_ref)
 

@@ -42,8 +42,26 @@ def test_shard_i2s_rows_matches_oracle(orc):
         sh = shard_i2s_rows(packed, N, K, n0, n1)
         ts, sc = orc.i2s_unpack_ternary(sh, n1 - n0, K)
         assert sc == np.float32(1.75) and np.array_equal(ts, t[n0:n1])
-    with pytest.raises(ValueError):
-        shard_i2s_rows(packed, N, 100, 0, 10)
+    import b2s
+    with pytest.raises(b2s.B2SError):
+        shard_i2s_rows(packed, N, 100, 0, 10)  # flattened rows of K % 128 != 0 are not separable
+    with pytest.raises(b2s.B2SError):
+        shard_i2s_rows(packed, N, K, 5, 5)
+
+
+def test_shard_rowpadded_rows_matches_oracle(orc):
+    """K % 128 != 0 (the ViT FFN width): shards are cut from the row-padded layout (I2_S_R)."""
+    from b2s import workloads as wl
+    from b2s.nsplit import row_ranges, shard_i2s_rows
+    g = wl.rng(12)
+    N, K = 64, 4304
+    t = wl.ternary(g, N, K)
+    rp = orc.i2s_to_rowpadded(orc.i2s_pack_ternary(t, 0.625), N, K)
+    Kp = (K + 127) // 128 * 128
+    for n0, n1 in row_ranges(N, 4):
+        sh = shard_i2s_rows(rp, N, K, n0, n1, rowpadded=True)
+        assert sh.size == (n1 - n0) * Kp // 4 + 32
+        assert np.array_equal(sh[:-32], rp[n0 * Kp // 4: n1 * Kp // 4]) and np.array_equal(sh[-32:], rp[-32:])
 
 
 def _nsplit_worker(rank, world, port, out_q):

@@ -127,3 +127,17 @@ def test_softmax_oracle(orc):
     z = x * 0.5 + mask
     e = np.exp(z - z.max(1, keepdims=True))
     assert np.allclose(y, e / e.sum(1, keepdims=True), atol=1e-6)
+
+
+def test_bitvla_model_resident_weights_equal_forward(orc):
+    """The CPU baseline's model (weights generated once, several forwards) gives the one-shot forward's bytes."""
+    cfg = orc.bitvla_config(vit_layers=1, dec_layers=1)
+    g = np.random.Generator(np.random.PCG64(5))
+    img = g.random((2, 3, cfg.image_size, cfg.image_size), dtype=np.float32)
+    tok = g.integers(0, cfg.vocab, (2, cfg.n_text)).astype(np.int32)
+    h_ref, a_ref = orc.bitvla_forward(cfg, 77, img, tok)
+    m = orc.BitVLAModel(cfg, 77)
+    for _ in range(2):
+        h, a = m.forward(img, tok, want_hidden=True)
+        assert np.array_equal(h, h_ref) and np.array_equal(a, a_ref)
+    m.close()
