@@ -510,7 +510,8 @@ def run_ffn(a, D, local, steps: int, warmup: int):
 
     # The same four kernels as separate calls with CUDA events around the gate/up GEMM: the per-launch
     # duration of the roofline kernel, replayed after the timed region.
-    ev = [events() for _ in range(N_SETS)]
+    ev = [(torch.cuda.Event(enable_timing=True, external=True), torch.cuda.Event(enable_timing=True, external=True))
+          for _ in range(N_SETS)]  # recorded inside captured graphs
 
     def step_probe(i):
         ws, x = sets[i % N_SETS]

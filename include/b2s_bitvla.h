@@ -82,6 +82,9 @@ void b2s_bitvla_free(b2s_bitvla *m);
  * as b2s_bitvla_create(..., S, ...). */
 int b2s_bitvla_create_from_gguf(const char *path, int max_batch, b2s_bitvla **out);
 
+/* The model's shape (the config it was built with, or the one read from its GGUF file). */
+int b2s_bitvla_get_config(const b2s_bitvla *m, b2s_bitvla_config *cfg);
+
 /* Device bytes held by the packed ternary weights / by all weights / by activation buffers. */
 size_t b2s_bitvla_ternary_bytes(const b2s_bitvla *m);
 size_t b2s_bitvla_weight_bytes(const b2s_bitvla *m);

@@ -43,6 +43,7 @@ def _bind():
         "b2s_bitvla_forward": (C.c_int, [vp, C.c_int, vp, vp, vp, vp, vp]),
         "b2s_bitvla_predict": (C.c_int, [vp, C.c_int, vp, vp, vp, vp]),
         "b2s_bitvla_create_from_gguf": (C.c_int, [C.c_char_p, C.c_int, C.POINTER(vp)]),
+        "b2s_bitvla_get_config": (C.c_int, [vp, P]),
     }
     for name, (res, args) in sig.items():
         f = getattr(L, name)
@@ -54,7 +55,8 @@ def _bind():
 
 EXPORTED = ["b2s_bitvla_default_config", "b2s_bitvla_seq_len", "b2s_bitvla_ternary_ops", "b2s_bitvla_param_bits",
             "b2s_bitvla_create", "b2s_bitvla_free", "b2s_bitvla_ternary_bytes", "b2s_bitvla_weight_bytes",
-            "b2s_bitvla_activation_bytes", "b2s_bitvla_forward", "b2s_bitvla_predict", "b2s_bitvla_create_from_gguf"]
+            "b2s_bitvla_activation_bytes", "b2s_bitvla_forward", "b2s_bitvla_predict", "b2s_bitvla_create_from_gguf",
+            "b2s_bitvla_get_config"]
 
 
 def default_config(**over) -> Config:
@@ -89,9 +91,9 @@ class Model:
         if gguf_path is not None:
             check(L.b2s_bitvla_create_from_gguf(gguf_path.encode(), max_batch, C.byref(h)))
             from .gguf import GgufFile
-            kv = GgufFile(gguf_path).kv
-            cfg = default_config(vit_layers=kv["bitvla.vision.block_count"], dec_layers=kv["bitvla.block_count"])
-            seed = kv["bitvla.token_embd.seed"]
+            cfg = Config()
+            check(L.b2s_bitvla_get_config(h, C.byref(cfg)))
+            seed = GgufFile(gguf_path).kv["bitvla.token_embd.seed"]
         else:
             check(L.b2s_bitvla_create(C.byref(cfg), seed & 0xFFFFFFFF, max_batch, C.byref(h)))
         self.cfg = cfg

@@ -782,6 +782,12 @@ void b2s_bitvla_free(b2s_bitvla* m) {
     delete m;
 }
 
+int b2s_bitvla_get_config(const b2s_bitvla* m, b2s_bitvla_config* cfg) {
+    if (!m || !cfg) return errf(B2S_ERR_INVALID_ARG, "bitvla_get_config: bad arguments");
+    *cfg = m->cfg;
+    return B2S_OK;
+}
+
 size_t b2s_bitvla_ternary_bytes(const b2s_bitvla* m) { return m ? m->ternary_bytes : 0; }
 size_t b2s_bitvla_weight_bytes(const b2s_bitvla* m) { return m ? m->wbytes : 0; }
 size_t b2s_bitvla_activation_bytes(const b2s_bitvla* m) { return m ? m->abytes : 0; }
