@@ -380,10 +380,34 @@ def run_server(a, D, local):
     D.barrier()
     e_ms = e0.elapsed_time(e1)
     assert np.isfinite(h_act).all()
-    ms, e_ms = D.max([ms, e_ms])
     tern_mb = model.ternary_bytes() / 1e6
     model.close()
     del d_img, d_tok, d_act
+
+    # Through the request server (b2s_server: one engine on this rank's GPU, a bounded queue, batches of up to
+    # B requests): every observation is submitted as its own request, then all are waited for. Host wall
+    # clock around the job (the server runs its own threads and streams); per-request latency from submit to
+    # completion.
+    from b2s.server import Server
+    srv = Server.bitvla([local], cfg, SEED, max_batch=B, queue_capacity=max(256, mine))
+    for i in range(mine):  # warm-up: graph capture of the batch sizes the queue forms
+        srv.wait(srv.submit(u8[i], toks[i]))
+    ids = [srv.submit(u8[i], toks[i]) for i in range(mine)]
+    for r in ids:
+        srv.wait(r)
+    D.barrier()
+    s_lat = []
+    t_s = time.perf_counter()
+    for _ in range(steps):
+        ids = [srv.submit(u8[i], toks[i]) for i in range(mine)]
+        for r in ids:
+            s_lat.append(srv.wait(r)[1])
+    s_ms = (time.perf_counter() - t_s) * 1e3
+    D.barrier()
+    srv_batches = srv.engine_status()[0]["batches"]
+    srv.close()
+    ms, e_ms, s_ms = D.max([ms, e_ms, s_ms])
+    s_lat.sort()
     value = steps * total / (ms * 1e-3)
     fwd_ms = statistics.median(lat)
     line = {
@@ -398,6 +422,13 @@ def run_server(a, D, local):
                 "h2d_bytes_per_step": total * (3 * cfg.image_size ** 2 + 4 * cfg.n_text),
                 "d2h_bytes_per_step": total * A * 4, "ms_per_step": round(e_ms / steps, 4),
                 "api": "b2s_bitvla_predict (C ABI): uint8 HWC host images and token ids in, host actions out"},
+        "dispatcher": {"value": round(steps * total / (s_ms * 1e-3), 3), "unit": "obs/s",
+                       "request_latency_ms": {"p50": round(s_lat[len(s_lat) // 2], 3),
+                                              "p90": round(s_lat[int(0.9 * (len(s_lat) - 1))], 3)},
+                       "api": "b2s_server_create_bitvla / b2s_server_submit / b2s_server_wait, one engine per GPU, "
+                              f"up to {B} requests per batch",
+                       "timing": "host wall clock around the submit/wait job (max over ranks)",
+                       "batches_formed": int(srv_batches)},
         "gpu_launches": steps * len(batches) * kernels_per_forward(cfg),
         "ternary_weight_mb": round(tern_mb, 1),
         "clocks": clk.summary(),

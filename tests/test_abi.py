@@ -1,5 +1,5 @@
-"""The C ABI library without a GPU: it loads, exports every symbol include/b2s.h and include/b2s_bitvla.h
-declare, its host type traits agree with the oracle byte for byte, and device entry points fail cleanly
+"""The C ABI library without a GPU: it loads, exports every symbol include/b2s.h, include/b2s_bitvla.h and
+include/b2s_server.h declare, its host type traits agree with the oracle byte for byte, and device entry points fail cleanly
 (no compute calls)."""
 import os
 import re
@@ -33,6 +33,15 @@ def test_exports_bitvla_symbols(b2s):
     decl = declared_symbols("b2s_bitvla.h")
     assert decl and not [s for s in decl if not hasattr(lib, s)]
     assert sorted(bitvla.EXPORTED) == decl
+
+
+def test_exports_server_symbols(b2s):
+    import ctypes
+    from b2s import server
+    lib = ctypes.CDLL(b2s.LIB_PATH)
+    decl = declared_symbols("b2s_server.h")
+    assert decl and not [s for s in decl if not hasattr(lib, s)]
+    assert sorted(server.EXPORTED) == decl
 
 
 def test_bitvla_host_traits(b2s, orc):
