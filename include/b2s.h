@@ -205,6 +205,18 @@ int b2s_attention(const float *q, int64_t ldq, const float *k, int64_t ldk, cons
                   int n_heads, int n_kv_heads, int head_dim, float scale, int causal, float *o, int64_t ldo,
                   void *stream);
 
+/* The same attention on the tcgen05 tensor cores. Products are 3xTF32 (each fp32 operand split into a TF32
+ * part and its fp32 remainder; big*big + big*small + small*big accumulated in fp32, about 2^-21 relative
+ * error per product) and the softmax takes the exact row maximum before exponentiating (exp2 on the
+ * special-function unit), so results match b2s_attention to about 1e-6 relative, not bit for bit. One CTA
+ * holds 128 rows = (n_heads / n_kv_heads) query heads x the queries of a block, sharing one K/V head.
+ * Needs head_dim % 8 == 0 and <= 128, 128 % (n_heads / n_kv_heads) == 0, at most 384 keys visible to a
+ * query block (M <= 384 without the causal mask), leading dimensions % 4 == 0 and 16-byte aligned tensors
+ * (B2S_ERR_UNSUPPORTED otherwise). */
+int b2s_attention_tc(const float *q, int64_t ldq, const float *k, int64_t ldk, const float *v, int64_t ldv, int64_t M,
+                     int n_heads, int n_kv_heads, int head_dim, float scale, int causal, float *o, int64_t ldo,
+                     void *stream);
+
 /* Patch embedding of a CHW fp32 image: non-overlapping P x P patches (row-major patch order) times the
  * [D][C*P*P] weight, plus bias[D] and the position embedding pos[n_patches][D] (either may be NULL):
  * y = (bias + pos) + acc, acc fma-accumulated over k = c*P*P + ky*P + kx ascending. */

@@ -50,6 +50,9 @@ typedef struct b2s_bitvla_config {
     int n_text;       /* 32 */
     int action_chunk; /* 8 */
     int action_dim;   /* 7 */
+    int attention_fp32; /* 0 (default): attention on the tensor cores (b2s_attention_tc, 3xTF32 products);
+                           1: the fixed-order fp32 attention kernel (b2s_attention), which the CPU oracle
+                           repeats bit for bit */
 } b2s_bitvla_config;
 
 typedef struct b2s_bitvla b2s_bitvla;

@@ -36,7 +36,7 @@ EXPORTED = [
     "b2s_ffn_block_workspace_size", "b2s_ffn_block", "b2s_soft_max_ext", "b2s_mul_mat_static",
     "b2s_mul_mat_q8_epi", "b2s_norm", "b2s_norm_act_quant", "b2s_rope_neox", "b2s_attention",
     "b2s_patch_embed", "b2s_embed_tokens_hash", "b2s_nsplit_range", "b2s_i2s_shard_rows", "b2s_peer_export",
-    "b2s_peer_open", "b2s_peer_close", "b2s_debug_wait_timeout",
+    "b2s_peer_open", "b2s_peer_close", "b2s_debug_wait_timeout", "b2s_attention_tc",
 ]
 PEER_HANDLE_BYTES = 64
 
@@ -95,6 +95,8 @@ def lib():
             "b2s_rope_neox": (C.c_int, [_vp, _i64, C.c_int, C.c_int, _i64, C.c_float, C.c_int, _vp]),
             "b2s_attention": (C.c_int, [_vp, _i64, _vp, _i64, _vp, _i64, _i64, C.c_int, C.c_int, C.c_int, C.c_float,
                                         C.c_int, _vp, _i64, _vp]),
+            "b2s_attention_tc": (C.c_int, [_vp, _i64, _vp, _i64, _vp, _i64, _i64, C.c_int, C.c_int, C.c_int,
+                                           C.c_float, C.c_int, _vp, _i64, _vp]),
             "b2s_patch_embed": (C.c_int, [_vp, C.c_int, C.c_int, C.c_int, C.c_int, _vp, _vp, _vp, C.c_int, _vp, _i64,
                                           _vp]),
             "b2s_embed_tokens_hash": (C.c_int, [_vp, C.c_int, C.c_int, C.c_uint32, _vp, _i64, _vp]),
@@ -301,6 +303,15 @@ def attention(q, k, v, n_heads: int, n_kv_heads: int, head_dim: int, scale: floa
     check(lib().b2s_attention(_ptr(q), q.stride(0), _ptr(k), k.stride(0), _ptr(v), v.stride(0), M, int(n_heads),
                               int(n_kv_heads), int(head_dim), float(scale), int(bool(causal)), _ptr(o), o.stride(0),
                               _stream(stream)))
+
+
+def attention_tc(q, k, v, n_heads: int, n_kv_heads: int, head_dim: int, scale: float, causal: bool, o,
+                 stream=None) -> None:
+    """Tensor-core attention (3xTF32 products, exact-max softmax); same operands as attention()."""
+    M = q.shape[0]
+    check(lib().b2s_attention_tc(_ptr(q), q.stride(0), _ptr(k), k.stride(0), _ptr(v), v.stride(0), M, int(n_heads),
+                                 int(n_kv_heads), int(head_dim), float(scale), int(bool(causal)), _ptr(o), o.stride(0),
+                                 _stream(stream)))
 
 
 def patch_embed(img, P: int, w, bias, pos, y, stream=None) -> None:

@@ -701,6 +701,27 @@ int b2s_attention(const float* q, int64_t ldq, const float* k, int64_t ldk, cons
                     "attention");
 }
 
+int b2s_attention_tc(const float* q, int64_t ldq, const float* k, int64_t ldk, const float* v, int64_t ldv, int64_t M,
+                     int n_heads, int n_kv_heads, int head_dim, float scale, int causal, float* o, int64_t ldo,
+                     void* stream) {
+    int rc = check_device();
+    if (rc) return rc;
+    if (!q || !k || !v || !o) return fail(B2S_ERR_INVALID_ARG, "attention_tc: NULL tensor");
+    if (M <= 0 || M > 65536 || n_heads <= 0 || n_kv_heads <= 0 || n_heads % n_kv_heads || head_dim <= 0)
+        return fail(B2S_ERR_INVALID_ARG, "attention_tc: bad shape");
+    if (ldq < (int64_t)n_heads * head_dim || ldo < (int64_t)n_heads * head_dim || ldk < (int64_t)n_kv_heads * head_dim ||
+        ldv < (int64_t)n_kv_heads * head_dim)
+        return fail(B2S_ERR_INVALID_ARG, "attention_tc: leading dimensions too small");
+    if (!b2s::attention_tc_supported((int)M, n_heads, n_kv_heads, head_dim, causal != 0, ldq, ldk, ldv, ldo, q, k, v,
+                                     o))
+        return fail(B2S_ERR_UNSUPPORTED,
+                    "attention_tc: needs head_dim %% 8 == 0 and <= 128, 128 %% (n_heads / n_kv_heads) == 0, at most "
+                    "384 keys per query block, leading dimensions %% 4 == 0 and 16-byte aligned tensors");
+    return launched(b2s::launch_attention_tc(q, ldq, k, ldk, v, ldv, 1, (int)M, n_heads, n_kv_heads, head_dim, scale,
+                                             causal != 0, o, ldo, static_cast<cudaStream_t>(stream)),
+                    "attention_tc");
+}
+
 int b2s_patch_embed(const float* img, int C, int H, int W, int P, const float* w, const float* bias, const float* pos,
                     int D, float* y, int64_t ldy, void* stream) {
     int rc = check_device();

@@ -124,6 +124,15 @@ cudaError_t launch_attention(const float* q, int64_t ldq, const float* k, int64_
                              int batch, int T, int heads, int kv_heads, int hd, float scale, bool causal, float* o,
                              int64_t ldo, cudaStream_t st);
 
+// Tensor-core attention (attention_tc.cu): same contract, products as 3xTF32 on tcgen05, exact-max softmax.
+// Needs hd % 8 == 0, hd <= 128, 128 % (heads / kv_heads) == 0, at most 384 keys per query block, leading
+// dimensions % 4 == 0 and 16-byte aligned tensors.
+bool attention_tc_supported(int T, int heads, int kv_heads, int hd, bool causal, int64_t ldq, int64_t ldk, int64_t ldv,
+                            int64_t ldo, const void* q, const void* k, const void* v, const void* o);
+cudaError_t launch_attention_tc(const float* q, int64_t ldq, const float* k, int64_t ldk, const float* v, int64_t ldv,
+                                int batch, int T, int heads, int kv_heads, int hd, float scale, bool causal, float* o,
+                                int64_t ldo, cudaStream_t st);
+
 // The library's mul_mat dispatch (b2s status codes; failures recorded for b2s_last_error()).
 // path 0 = auto (M <= 16: GEMV, else tensor cores), 1 = GEMV, 2 = tensor cores.
 int dispatch_mul_mat_q8(const I2sWeight& w, const int8_t* q, int64_t ldq, const float* s, const int32_t* sums,

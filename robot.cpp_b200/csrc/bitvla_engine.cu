@@ -475,6 +475,17 @@ int enqueue_forward(b2s_bitvla* m, int B, cudaStream_t st) {
         return b2s::dispatch_mul_mat_q8(t.w, m->q8, ldq, m->qs, m->qsum, M, y, ldy, 2, e, st, m->splitk_ws,
                                         m->splitk_bytes);
     };
+    // Tensor-core attention unless the config asks for the bit-reproducible fp32 kernel (or the shape is
+    // outside what the tensor-core kernel takes).
+    auto attention = [&](const float* q, int64_t ldq_, const float* k, int64_t ldk, const float* v, int64_t ldv, int batch,
+                         int T, int heads, int kv_heads, int hd, float scale, bool causal, float* o, int64_t ldo) {
+        if (!c.attention_fp32 &&
+            b2s::attention_tc_supported(T, heads, kv_heads, hd, causal, ldq_, ldk, ldv, ldo, q, k, v, o))
+            return b2s::launch_attention_tc(q, ldq_, k, ldk, v, ldv, batch, T, heads, kv_heads, hd, scale, causal, o,
+                                            ldo, st);
+        return b2s::launch_attention(q, ldq_, k, ldk, v, ldv, batch, T, heads, kv_heads, hd, scale, causal, o, ldo,
+                                     st);
+    };
     // ---------------------------------------------------------------- vision tower
     TRY_CUDA(b2s::launch_patch_embed(m->img, B, 3, c.image_size, c.image_size, c.patch, m->patch_w, m->patch_b, m->pos,
                                      D, m->vx, D, st),
@@ -486,8 +497,8 @@ int enqueue_forward(b2s_bitvla* m, int B, cudaStream_t st) {
                                   m->qsum, st),
                  "vit ln1");
         TRY_B2S(gemm(L.qkv, Mv, m->vqkv, 3 * D, L.qkv_b, nullptr, 0));
-        TRY_CUDA(b2s::launch_attention(m->vqkv, 3 * D, m->vqkv + D, 3 * D, m->vqkv + 2 * D, 3 * D, B, m->np,
-                                       c.vit_heads, c.vit_heads, D / c.vit_heads, vit_scale, false, m->vattn, D, st),
+        TRY_CUDA(attention(m->vqkv, 3 * D, m->vqkv + D, 3 * D, m->vqkv + 2 * D, 3 * D, B, m->np, c.vit_heads,
+                           c.vit_heads, D / c.vit_heads, vit_scale, false, m->vattn, D),
                  "vit attention");
         TRY_CUDA(b2s::launch_act_quant(m->vattn, D, nullptr, false, 0.0f, Mv, D, m->q8, ldq, m->qs, m->qsum, st),
                  "vit o act_quant");
@@ -533,8 +544,8 @@ int enqueue_forward(b2s_bitvla* m, int B, cudaStream_t st) {
         TRY_CUDA(b2s::launch_rope_apply(m->dqkv, Md, c.dec_heads + c.dec_kv_heads, c.head_dim, ldqkv, m->rope, m->seq,
                                         st),
                  "rope");
-        TRY_CUDA(b2s::launch_attention(m->dqkv, ldqkv, m->dqkv + H, ldqkv, m->dqkv + H + KV, ldqkv, B, m->seq,
-                                       c.dec_heads, c.dec_kv_heads, c.head_dim, dec_scale, true, m->dattn, H, st),
+        TRY_CUDA(attention(m->dqkv, ldqkv, m->dqkv + H, ldqkv, m->dqkv + H + KV, ldqkv, B, m->seq, c.dec_heads,
+                           c.dec_kv_heads, c.head_dim, dec_scale, true, m->dattn, H),
                  "decoder attention");
         TRY_CUDA(b2s::launch_act_quant(m->dattn, H, L.attn_sub, true, c.dec_eps, Md, H, m->q8, ldq, m->qs, m->qsum, st),
                  "attn_sub_norm");
@@ -616,6 +627,7 @@ void b2s_bitvla_default_config(b2s_bitvla_config* c) {
     c->n_text = 32;
     c->action_chunk = 8;
     c->action_dim = 7;
+    c->attention_fp32 = 0;
 }
 
 int b2s_bitvla_seq_len(const b2s_bitvla_config* c) {

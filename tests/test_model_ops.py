@@ -100,6 +100,48 @@ def test_attention(b2s, orc, M, heads, kv, hd, causal):
     assert np.array_equal(got, ref)
 
 
+@pytest.mark.parametrize("M,heads,kv,hd,causal", [(256, 16, 16, 72, False), (288, 20, 5, 128, True),
+                                                  (33, 4, 2, 64, True), (1, 2, 1, 8, True), (300, 8, 8, 32, False),
+                                                  (384, 4, 4, 128, False), (100, 32, 4, 16, True),
+                                                  (77, 6, 3, 40, False)])
+def test_attention_tensor_cores(b2s, orc, M, heads, kv, hd, causal):
+    """b2s_attention_tc (3xTF32 tcgen05 products, exact-max softmax) against the oracle's fp32 attention and a
+    float64 evaluation: within the 1e-5 per-operator bar (max |o - ref| / max |ref|)."""
+    g = wl.rng(3 * M + heads + hd)
+    H, KV = heads * hd, kv * hd
+    qkv = wl.activations(g, M, H + 2 * KV) * 2.0
+    scale = 1.0 / np.sqrt(hd)
+    qkvd = dev(qkv)
+    o = torch.full((M, H), float("nan"), dtype=torch.float32, device="cuda")
+    b2s.attention_tc(qkvd[:, :H], qkvd[:, H:H + KV], qkvd[:, H + KV:], heads, kv, hd, float(scale), causal, o)
+    sync_ok(b2s)
+    got = o.cpu().numpy()
+    ref = orc.attention(qkv, 0, H, H + KV, 1, heads, kv, hd, M, causal, float(scale))
+    q64 = qkv[:, :H].astype(np.float64).reshape(M, heads, hd)
+    k64 = qkv[:, H:H + KV].astype(np.float64).reshape(M, kv, hd)
+    v64 = qkv[:, H + KV:].astype(np.float64).reshape(M, kv, hd)
+    rep = heads // kv
+    s64 = np.einsum("mhd,nhd->hmn", q64, np.repeat(k64, rep, axis=1)) * scale
+    if causal:
+        s64 = np.where(np.tril(np.ones((M, M), bool))[None], s64, -np.inf)
+    p64 = np.exp(s64 - s64.max(axis=2, keepdims=True))
+    p64 /= p64.sum(axis=2, keepdims=True)
+    o64 = np.einsum("hmn,nhd->mhd", p64, np.repeat(v64, rep, axis=1)).reshape(M, H)
+    assert np.isfinite(got).all()
+    assert max_abs_rel(got, o64) <= TOL, max_abs_rel(got, o64)
+    assert max_abs_rel(got, ref) <= TOL, max_abs_rel(got, ref)
+
+
+def test_attention_tensor_cores_unsupported(b2s):
+    qkv = torch.zeros((400, 3 * 64), dtype=torch.float32, device="cuda")
+    o = torch.zeros((400, 64), dtype=torch.float32, device="cuda")
+    with pytest.raises(b2s.B2SError):  # 400 keys visible to one query block (no causal mask): above 384
+        b2s.attention_tc(qkv[:, :64], qkv[:, 64:128], qkv[:, 128:], 1, 1, 64, 0.125, False, o)
+    with pytest.raises(b2s.B2SError):  # 3 query heads per K/V head does not divide the 128 MMA rows
+        q3 = torch.zeros((8, 3 * 64), dtype=torch.float32, device="cuda")
+        b2s.attention_tc(q3, qkv[:8, :64], qkv[:8, 64:128], 3, 1, 64, 0.125, True, o[:8].repeat(1, 3))
+
+
 def test_attention_unsupported(b2s):
     qkv = torch.zeros((8, 3 * 36), dtype=torch.float32, device="cuda")
     o = torch.zeros((8, 36), dtype=torch.float32, device="cuda")
