@@ -18,7 +18,7 @@ class Config(C.Structure):
                 ("dec_layers", C.c_int), ("dec_hidden", C.c_int), ("dec_ffn", C.c_int), ("dec_heads", C.c_int),
                 ("dec_kv_heads", C.c_int), ("head_dim", C.c_int), ("rope_theta", C.c_float), ("dec_eps", C.c_float),
                 ("vocab", C.c_int), ("n_text", C.c_int), ("action_chunk", C.c_int), ("action_dim", C.c_int),
-                ("attention_fp32", C.c_int)]
+                ("attention_tc", C.c_int)]
 
 
 _bound = False

@@ -475,11 +475,11 @@ int enqueue_forward(b2s_bitvla* m, int B, cudaStream_t st) {
         return b2s::dispatch_mul_mat_q8(t.w, m->q8, ldq, m->qs, m->qsum, M, y, ldy, 2, e, st, m->splitk_ws,
                                         m->splitk_bytes);
     };
-    // Tensor-core attention unless the config asks for the bit-reproducible fp32 kernel (or the shape is
-    // outside what the tensor-core kernel takes).
+    // The bit-reproducible fp32 attention kernel unless the config asks for the tensor-core one (and the
+    // shape is one it takes).
     auto attention = [&](const float* q, int64_t ldq_, const float* k, int64_t ldk, const float* v, int64_t ldv, int batch,
                          int T, int heads, int kv_heads, int hd, float scale, bool causal, float* o, int64_t ldo) {
-        if (!c.attention_fp32 &&
+        if (c.attention_tc &&
             b2s::attention_tc_supported(T, heads, kv_heads, hd, causal, ldq_, ldk, ldv, ldo, q, k, v, o))
             return b2s::launch_attention_tc(q, ldq_, k, ldk, v, ldv, batch, T, heads, kv_heads, hd, scale, causal, o,
                                             ldo, st);
@@ -627,7 +627,7 @@ void b2s_bitvla_default_config(b2s_bitvla_config* c) {
     c->n_text = 32;
     c->action_chunk = 8;
     c->action_dim = 7;
-    c->attention_fp32 = 0;
+    c->attention_tc = 0;
 }
 
 int b2s_bitvla_seq_len(const b2s_bitvla_config* c) {
