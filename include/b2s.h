@@ -236,11 +236,11 @@ int b2s_soft_max_ext(const float *x, const float *mask, int64_t mask_rows, int64
  * A MUL_MAT of very many tokens split over the output rows of W across g GPUs (one process per GPU): rank r
  * computes Y[:, n0_r:n1_r) and its GEMM epilogue stores the slice straight into the root GPU's output over
  * NVLink (plain peer stores; no gather kernel, no collective). The root exports its output buffer with
- * b2s_peer_export, the handle's 64 bytes reach the other ranks by any transport, each opens it with
+ * b2s_peer_export, the handle's 72 bytes reach the other ranks by any transport, each opens it with
  * b2s_peer_open and passes (peer_ptr + n0_r floats, ldy = N) as the Y of b2s_mul_mat_q8. The reference
  * has no multi-GPU path (one ggml CUDA backend on device 0, src/models/ggml_backend.cpp:62-202); these
  * calls are the plumbing that replaces a ggml tensor split plus gather for this op. */
-#define B2S_PEER_HANDLE_BYTES 64
+#define B2S_PEER_HANDLE_BYTES 72
 /* Balanced contiguous split of n_rows over `world` ranks: rank gets [*n0, *n1) (sizes differ by <= 1). */
 int b2s_nsplit_range(int64_t n_rows, int world, int rank, int64_t *n0, int64_t *n1);
 /* Host: rows [r0, r1) of an I2_S (n_per_row % 128 == 0) or I2_S_R tensor as a standalone tensor of the same
@@ -248,11 +248,13 @@ int b2s_nsplit_range(int64_t n_rows, int world, int rank, int64_t *n0, int64_t *
  * error. */
 size_t b2s_i2s_shard_rows(const void *src, int32_t type, int64_t nrow, int64_t n_per_row, int64_t r0, int64_t r1,
                           void *dst);
-/* CUDA IPC export of a device allocation of the current device into B2S_PEER_HANDLE_BYTES bytes. */
+/* Export of a device buffer of the current device into B2S_PEER_HANDLE_BYTES bytes: the CUDA IPC handle of the
+ * allocation that contains dev_ptr and dev_ptr's offset in it (so pointers from a sub-allocating allocator
+ * work). */
 int b2s_peer_export(const void *dev_ptr, void *handle, size_t handle_bytes);
 /* Maps a peer's exported allocation into the current device's address space (peer access enabled). */
 int b2s_peer_open(const void *handle, size_t handle_bytes, void **dev_ptr);
-/* Unmaps a pointer returned by b2s_peer_open. */
+/* Unmaps a pointer returned by b2s_peer_open (B2S_ERR_INVALID_ARG for any other pointer). */
 int b2s_peer_close(void *dev_ptr);
 
 #ifdef __cplusplus

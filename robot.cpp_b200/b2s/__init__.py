@@ -38,7 +38,7 @@ EXPORTED = [
     "b2s_patch_embed", "b2s_embed_tokens_hash", "b2s_nsplit_range", "b2s_i2s_shard_rows", "b2s_peer_export",
     "b2s_peer_open", "b2s_peer_close", "b2s_debug_wait_timeout", "b2s_attention_tc",
 ]
-PEER_HANDLE_BYTES = 64
+PEER_HANDLE_BYTES = 72
 
 
 class B2SError(RuntimeError):
@@ -349,7 +349,7 @@ def i2s_shard_rows(packed, N: int, K: int, r0: int, r1: int, rowpadded: bool = F
 
 
 def peer_export(dev_ptr: int) -> bytes:
-    """CUDA IPC handle (64 bytes) of a device allocation of the current device."""
+    """Peer handle (72 bytes: the enclosing allocation's CUDA IPC handle and the offset) of a device buffer."""
     h = (C.c_uint8 * PEER_HANDLE_BYTES)()
     check(lib().b2s_peer_export(int(dev_ptr), h, PEER_HANDLE_BYTES))
     return bytes(h)

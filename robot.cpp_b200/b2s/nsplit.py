@@ -5,7 +5,7 @@ N-split (very large M, e.g. 16384 tokens): rank r of g owns weight rows [n0_r, n
 a contiguous byte range of the i2_s tensor, cut out with its fp32 scale by b2s_i2s_shard_rows. The
 activations are replicated (every rank quantizes the full X). Each rank's GEMM epilogue writes its column
 slice straight into the root GPU's output buffer over NVLink: the root exports the buffer
-(b2s_peer_export), the 64 handle bytes are broadcast through the process group (transport only), every
+(b2s_peer_export), the 72 handle bytes are broadcast through the process group (transport only), every
 other rank maps it (b2s_peer_open) and passes `root_ptr + n0_r` with row stride N as the kernel's output
 (plain peer stores; no multicast, no separate gather kernel or collective). A process-group barrier after
 the ranks' streams complete makes the gathered Y readable on the root.
