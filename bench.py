@@ -832,8 +832,33 @@ def run_gemm_c0(local):
             "peak_basis": basis}
 
 
+def batched_weights(dev, K, N, seed, min_bytes):
+    """One i2_s tensor of R copies of a seeded weight back to back (rotated in bytes; shared scale trailer),
+    R chosen so that the tensor holds more than min_bytes; row-padded when K % 128 != 0."""
+    import torch
+    import b2s
+    from b2s import workloads as wl
+    w = wl.weight(wl.rng(seed), N, K)
+    base = torch.from_numpy(w.packed).to(dev)
+    Kp = (K + 127) // 128 * 128
+    if K % 128:
+        rb = torch.empty(b2s.i2s_r_nbytes(N, K), dtype=torch.uint8, device=dev)
+        b2s.repack_rows(base, rb, N, K)
+        torch.cuda.synchronize()
+        base = rb
+    wbytes = N * Kp // 4
+    R = max(2, -(-min_bytes // wbytes))
+    big = torch.empty(R * wbytes + 32, dtype=torch.uint8, device=dev)
+    for r in range(R):
+        big[r * wbytes:(r + 1) * wbytes] = torch.roll(base[:wbytes], shifts=r * 4099) if r else base[:wbytes]
+    big[R * wbytes:] = base[wbytes:wbytes + 32]
+    return big, b2s.i2s_tensor_batched(big, N, K, R, rowpadded=bool(K % 128)), R, wbytes
+
+
 def run_sweep(local, ms_list=None, reps=5):
-    """Config 4 on one GPU: per point TOP/s and algorithmic GB/s per launch of b2s_mul_mat_q8."""
+    """Config 4 on one GPU: per point TOP/s and algorithmic GB/s per launch of b2s_mul_mat_q8; for the decode
+    sizes (M <= 16) also the batched form (b2s_mul_mat_q8_batched: one GEMV launch streaming R matrices of the
+    shape, > 2x L2 of weights), per matrix."""
     import torch
     import b2s
     dev = torch.device("cuda", local)
@@ -861,9 +886,23 @@ def run_sweep(local, ms_list=None, reps=5):
             byts = wbytes + Mt * K + 8 * Mt + 4 * Mt * N
             tops, gbs = ops / us / 1e6, byts / us / 1e3
             bound = "hbm" if Mt <= 16 else "tensor"
-            rows.append({"M": Mt, "K": K, "N": N, "path": "gemv" if Mt <= 16 else "tcgen05", "us": round(us, 3),
-                         "TOP/s": round(tops, 1), "GB/s": round(gbs, 1), "bound": bound,
-                         "frac": round(gbs / hbm if bound == "hbm" else tops / peak, 4)})
+            row = {"M": Mt, "K": K, "N": N, "path": "gemv" if Mt <= 16 else "tcgen05", "us": round(us, 3),
+                   "TOP/s": round(tops, 1), "GB/s": round(gbs, 1), "bound": bound,
+                   "frac": round(gbs / hbm if bound == "hbm" else tops / peak, 4)}
+            if Mt <= 16:
+                big, Wb, Rb, _ = batched_weights(dev, K, N, K + N, 2 * 126 * 2**20 + 8 * 2**20)
+                qb = torch.randint(-127, 128, (Rb, Mt, ldq), dtype=torch.int8, device=dev)[:, :, :K]
+                sb = torch.rand((Rb, Mt), device=dev) + 0.5
+                ub = qb.to(torch.int32).sum(dim=2).to(torch.int32)
+                yb = torch.empty((Rb, Mt, N), dtype=torch.float32, device=dev)
+                us_b = time_graph(lambda: b2s.mul_mat_q8_batched(Wb, qb, sb, ub, yb, stream=stream), stream, 1,
+                                  reps) / Rb
+                assert b2s.device_error() == 0
+                row.update({"batched_matrices": Rb, "us_per_matrix_batched": round(us_b, 4),
+                            "GB/s_batched": round(byts / us_b / 1e3, 1),
+                            "frac_batched": round(byts / us_b / 1e3 / hbm, 4)})
+                del big, qb, sb, ub, yb
+            rows.append(row)
             del q, s, u, y
         del copies
         torch.cuda.empty_cache()

@@ -123,7 +123,8 @@ int b2s_rms_norm_act_quant(const float *x, const float *g, int64_t M, int64_t K,
  * distributed shared memory otherwise). Any size >= the activation part is accepted. */
 size_t b2s_mul_mat_workspace_size(const b2s_tensor *W, const b2s_tensor *X);
 
-/* The MUL_MAT node: Y = mul_mat(W, X). W: I2_S (ne0 % 128 == 0) or I2_S_R, ne=[K,N], contiguous;
+/* The MUL_MAT node: Y = mul_mat(W, X). W: I2_S (ne0 % 128 == 0) or I2_S_R, ne=[K,N], contiguous (or
+ * ne=[K,N,B] with X ne=[K,M,B] and Y ne=[N,M,B]: ggml's batched matmul, see b2s_mul_mat_q8_batched);
  * X: F32 ne=[K,M], rows contiguous (nb[0] = 4); Y: F32 ne=[N,M], rows contiguous. Uses the caller's
  * workspace for the quantized activations; allocates nothing. Decode sizes run a GEMV (M = 1: dp4a on
  * CUDA cores; M = 2..16: warp-level int8 MMAs), larger M the tcgen05 tensor-core GEMM. */
@@ -149,6 +150,15 @@ int b2s_mul_mat_static(const b2s_tensor *W, const b2s_tensor *X, b2s_tensor *Y, 
  * 16-byte aligned), s [M], sums [M] from b2s_act_quant / b2s_rms_norm_act_quant. Y [M x ldy] f32. */
 int b2s_mul_mat_q8(const b2s_tensor *W, const int8_t *q, int64_t ldq, const float *s, const int32_t *sums,
                    int64_t M, float *Y, int64_t ldy, void *stream);
+/* ggml's batched MUL_MAT (ne[2] > 1) on quantized activations: B independent problems, problem b = weight
+ * matrix b times activations b. W ne=[K,N,B] (I2_S with K % 128 == 0, or I2_S_R): the B matrices back to back
+ * (nb[2] = N*K/4 bytes, N*Kp/4 row-padded) sharing the tensor's one fp32 scale, which follows all B*N rows
+ * (the flattened i2_s layout over B*N rows). Activations of problem b at q + b*q_bstride bytes, scales and sums
+ * at + b*a_bstride elements; outputs at Y + b*y_bstride floats. Decode sizes (M <= 16) stream every matrix in
+ * one GEMV launch (grid over rows x problems); larger M runs one tensor-core GEMM per matrix. */
+int b2s_mul_mat_q8_batched(const b2s_tensor *W, const int8_t *q, int64_t ldq, int64_t q_bstride, const float *s,
+                           const int32_t *sums, int64_t a_bstride, int64_t M, float *Y, int64_t ldy, int64_t y_bstride,
+                           void *stream);
 /* Same with the kernel chosen explicitly: path 0 = automatic, 1 = GEMV (any M, run in token groups of up to
  * 16: one token on dp4a, 2..16 on warp int8 MMAs), 2 = tcgen05 tensor-core GEMM (any M). For tests and
  * tuning; results are identical. */

@@ -36,7 +36,7 @@ EXPORTED = [
     "b2s_ffn_block_workspace_size", "b2s_ffn_block", "b2s_soft_max_ext", "b2s_mul_mat_static",
     "b2s_mul_mat_q8_epi", "b2s_norm", "b2s_norm_act_quant", "b2s_rope_neox", "b2s_attention",
     "b2s_patch_embed", "b2s_embed_tokens_hash", "b2s_nsplit_range", "b2s_i2s_shard_rows", "b2s_peer_export",
-    "b2s_peer_open", "b2s_peer_close", "b2s_debug_wait_timeout", "b2s_attention_tc",
+    "b2s_peer_open", "b2s_peer_close", "b2s_debug_wait_timeout", "b2s_attention_tc", "b2s_mul_mat_q8_batched",
 ]
 PEER_HANDLE_BYTES = 72
 
@@ -95,6 +95,7 @@ def lib():
             "b2s_rope_neox": (C.c_int, [_vp, _i64, C.c_int, C.c_int, _i64, C.c_float, C.c_int, _vp]),
             "b2s_attention": (C.c_int, [_vp, _i64, _vp, _i64, _vp, _i64, _i64, C.c_int, C.c_int, C.c_int, C.c_float,
                                         C.c_int, _vp, _i64, _vp]),
+            "b2s_mul_mat_q8_batched": (C.c_int, [_TP, _vp, _i64, _i64, _vp, _vp, _i64, _i64, _vp, _i64, _i64, _vp]),
             "b2s_attention_tc": (C.c_int, [_vp, _i64, _vp, _i64, _vp, _i64, _i64, C.c_int, C.c_int, C.c_int,
                                            C.c_float, C.c_int, _vp, _i64, _vp]),
             "b2s_patch_embed": (C.c_int, [_vp, C.c_int, C.c_int, C.c_int, C.c_int, _vp, _vp, _vp, C.c_int, _vp, _i64,
@@ -242,6 +243,21 @@ def mul_mat_q8(W: Tensor, q, s, sums, y, path: int = 0, stream=None) -> None:
     M = q.shape[0]
     check(lib().b2s_mul_mat_q8_ex(C.byref(W), _ptr(q), q.stride(0), _ptr(s), _ptr(sums), M, _ptr(y), y.stride(0),
                                   int(path), _stream(stream)))
+
+
+def i2s_tensor_batched(buf, N: int, K: int, B: int, rowpadded: bool = False) -> Tensor:
+    """Descriptor of B i2_s matrices (ne=[K,N,B]) stored back to back in ``buf`` with one trailing scale."""
+    t = i2s_tensor(buf, N, K, rowpadded)
+    t.ne[:] = [K, N, B, 1]
+    t.nb[3] = t.nb[2] * B
+    return t
+
+
+def mul_mat_q8_batched(W: Tensor, q, s, sums, y, stream=None) -> None:
+    """q [B, M, ldq] int8 (a strided view), s/sums [B, M], y [B, M, N] f32: y[b] = mul_mat(W[b], q[b])."""
+    B, M = q.shape[0], q.shape[1]
+    check(lib().b2s_mul_mat_q8_batched(C.byref(W), _ptr(q), q.stride(1), q.stride(0), _ptr(s), _ptr(sums), s.stride(0),
+                                       M, _ptr(y), y.stride(1), y.stride(0), _stream(stream)))
 
 
 def ffn_gate_up_sqrelu_q8(Wg: Tensor, Wu: Tensor, q, s, sums, p, stream=None) -> None:

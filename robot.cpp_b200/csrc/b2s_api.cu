@@ -136,6 +136,27 @@ int weight_view(const b2s_tensor* W, b2s::I2sWeight* out, const char* name) {
     return B2S_OK;
 }
 
+// A batched i2_s weight, ne = [K, N, B, 1]: B matrices of N rows stored back to back (matrix b at byte
+// b * N * Kp / 4, nb[2] = N * Kp / 4) with the tensor's one fp32 scale after all B * N rows -- the flattened
+// i2_s layout over B * N rows. Returns the view of matrix 0 and the byte stride between matrices.
+int weight_view_batched(const b2s_tensor* W, b2s::I2sWeight* out, int64_t* count, int64_t* stride, const char* name) {
+    if (!W) return fail(B2S_ERR_INVALID_ARG, "%s is NULL", name);
+    if (W->ne[2] <= 0 || W->ne[3] != 1)
+        return fail(B2S_ERR_INVALID_ARG, "%s: batched weight needs ne[2] >= 1 and ne[3] == 1", name);
+    b2s_tensor flat = *W;  // the B * N rows as one 2-D tensor validates every byte-level rule
+    flat.ne[1] = W->ne[1] * W->ne[2];
+    flat.ne[2] = 1;
+    int rc = weight_view(&flat, out, name);
+    if (rc) return rc;
+    out->N = W->ne[1];
+    *count = W->ne[2];
+    *stride = out->N * out->Kp / 4;
+    if (W->ne[2] > 1 && W->nb[2] != (size_t)*stride)
+        return fail(B2S_ERR_UNSUPPORTED, "%s: nb[2] (%zu) must be N * K / 4 = %lld (matrices back to back)", name,
+                    W->nb[2], (long long)*stride);
+    return B2S_OK;
+}
+
 // Rows of a ggml f32 tensor as a 2-D [rows x ne0] view with row stride ld (elements).
 int f32_rows(const b2s_tensor* T, const char* name, int64_t* rows, int64_t* cols, int64_t* ld) {
     if (!T) return fail(B2S_ERR_INVALID_ARG, "%s is NULL", name);
@@ -317,6 +338,33 @@ int mul_mat_q8_impl(const b2s::I2sWeight& w, const int8_t* q, int64_t ldq, const
     return run_tc(w, nullptr, q, ldq, s, sums, M, Y, ldy, 0, st, epi, splitk_ws, splitk_bytes);
 }
 
+// B independent problems: decode sizes (M <= 16) as one batched GEMV launch, larger M one tensor-core GEMM
+// per matrix.
+int mul_mat_q8_batched_impl(const b2s::I2sWeight& w, int64_t B, int64_t w_stride, const int8_t* q, int64_t ldq,
+                            int64_t q_bstride, const float* s, const int32_t* sums, int64_t a_bstride, int64_t M, float* Y,
+                            int64_t ldy, int64_t y_bstride, cudaStream_t st, void* splitk_ws = nullptr,
+                            size_t splitk_bytes = 0) {
+    if (M <= 0 || B <= 0) return B2S_OK;
+    if (M <= 16 && B <= 65535) {
+        b2s::GemvBatch bt;
+        bt.count = (int)B;
+        bt.w_stride = w_stride;
+        bt.q_stride = q_bstride;
+        bt.a_stride = a_bstride;
+        bt.y_stride = y_bstride;
+        b2s::Q8Act a{q, s, sums, M, w.K, ldq};
+        return launched(b2s::launch_gemv_i2s(w, a, Y, ldy, b2s::Epilogue{}, st, bt), "gemv_i2s batched launch");
+    }
+    for (int64_t b = 0; b < B; ++b) {
+        b2s::I2sWeight wb = w;
+        wb.codes = w.codes + b * w_stride;
+        const int rc = mul_mat_q8_impl(wb, q + b * q_bstride, ldq, s + b * a_bstride, sums + b * a_bstride, M,
+                                       Y + b * y_bstride, ldy, 0, st, b2s::Epilogue{}, splitk_ws, splitk_bytes);
+        if (rc) return rc;
+    }
+    return B2S_OK;
+}
+
 }  // namespace
 
 namespace b2s {
@@ -393,6 +441,46 @@ int mul_mat_into_scratch(const void* Wv, const void* Xv, void* Yv, void* scratch
 }
 
 }  // namespace b2s
+
+namespace {
+
+// MUL_MAT over ne[2] (ggml's batched matmul, one weight matrix per batch entry): W ne=[K,N,B], X ne=[K,M,B],
+// Y ne=[N,M,B], X and Y rows contiguous across the batch. All B*M tokens are quantized in one launch.
+int mul_mat_batched(const b2s_tensor* W, const b2s_tensor* X, const b2s_tensor* Y, void* workspace,
+                    size_t workspace_bytes, cudaStream_t st) {
+    b2s::I2sWeight w{};
+    int64_t B = 0, wstride = 0;
+    int rc;
+    if ((rc = weight_view_batched(W, &w, &B, &wstride, "W"))) return rc;
+    if (!X || !Y) return fail(B2S_ERR_INVALID_ARG, "X and Y must be non-NULL");
+    if (X->ne[2] != B || Y->ne[2] != B || X->ne[3] != 1 || Y->ne[3] != 1)
+        return fail(B2S_ERR_INVALID_ARG, "batched mul_mat: X and Y need ne[2] == W ne[2] (%lld) and ne[3] == 1",
+                    (long long)B);
+    int64_t rows, Kx, ldx, yrows, Ny, ldy;
+    if ((rc = f32_rows(X, "X", &rows, &Kx, &ldx))) return rc;
+    if ((rc = f32_rows(Y, "Y", &yrows, &Ny, &ldy))) return rc;
+    if (Kx != w.K) return fail(B2S_ERR_INVALID_ARG, "X ne0 (%lld) != W ne0 (%lld)", (long long)Kx, (long long)w.K);
+    const int64_t M = X->ne[1];
+    if (Ny != w.N || Y->ne[1] != M) return fail(B2S_ERR_INVALID_ARG, "Y must be ne=[N, M, B]");
+    const WsLayout l = act_ws(rows, w.K);
+    if (!workspace || workspace_bytes < l.total)
+        return fail(B2S_ERR_WORKSPACE, "mul_mat needs %zu workspace bytes, got %zu", l.total, workspace_bytes);
+    if ((reinterpret_cast<uintptr_t>(workspace) & 255) != 0) return fail(B2S_ERR_WORKSPACE, "workspace must be 256-byte aligned");
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    int8_t* q = reinterpret_cast<int8_t*>(ws + l.q_off);
+    float* s = reinterpret_cast<float*>(ws + l.s_off);
+    int32_t* sums = reinterpret_cast<int32_t*>(ws + l.sum_off);
+    if ((rc = launched(b2s::launch_act_quant(static_cast<const float*>(X->data), ldx, nullptr, false, 0.0f, rows, w.K,
+                                             q, l.ldq, s, sums, st),
+                       "act_quant launch")))
+        return rc;
+    const size_t sk_off = a256(l.total);
+    void* sk = workspace_bytes > sk_off ? ws + sk_off : nullptr;
+    return mul_mat_q8_batched_impl(w, B, wstride, q, l.ldq, M * l.ldq, s, sums, M, M, static_cast<float*>(Y->data),
+                                   ldy, M * ldy, st, sk, sk ? workspace_bytes - sk_off : 0);
+}
+
+}  // namespace
 
 // ==================================================================================================
 extern "C" {
@@ -524,6 +612,21 @@ int b2s_mul_mat_q8_ex(const b2s_tensor* W, const int8_t* q, int64_t ldq, const f
     return mul_mat_q8_impl(w, q, ldq, s, sums, M, Y, ldy, path, static_cast<cudaStream_t>(stream));
 }
 
+int b2s_mul_mat_q8_batched(const b2s_tensor* W, const int8_t* q, int64_t ldq, int64_t q_bstride, const float* s,
+                           const int32_t* sums, int64_t a_bstride, int64_t M, float* Y, int64_t ldy, int64_t y_bstride,
+                           void* stream) {
+    int rc = check_device();
+    if (rc) return rc;
+    b2s::I2sWeight w;
+    int64_t B = 0, wstride = 0;
+    if ((rc = weight_view_batched(W, &w, &B, &wstride, "W"))) return rc;
+    if (!q || !s || !sums || !Y) return fail(B2S_ERR_INVALID_ARG, "mul_mat_q8_batched: q, s, sums and Y must be non-NULL");
+    if (M < 0 || ldq < w.K || ldy < w.N || q_bstride < M * ldq || a_bstride < M || y_bstride < M * ldy)
+        return fail(B2S_ERR_INVALID_ARG, "mul_mat_q8_batched: bad M / leading dimensions / batch strides");
+    return mul_mat_q8_batched_impl(w, B, wstride, q, ldq, q_bstride, s, sums, a_bstride, M, Y, ldy, y_bstride,
+                                   static_cast<cudaStream_t>(stream));
+}
+
 int b2s_mul_mat_q8(const b2s_tensor* W, const int8_t* q, int64_t ldq, const float* s, const int32_t* sums, int64_t M,
                    float* Y, int64_t ldy, void* stream) {
     return b2s_mul_mat_q8_ex(W, q, ldq, s, sums, M, Y, ldy, 0, stream);
@@ -548,6 +651,7 @@ int b2s_mul_mat(const b2s_tensor* W, const b2s_tensor* X, b2s_tensor* Y, void* w
                 void* stream) {
     int rc = check_device();
     if (rc) return rc;
+    if (W && W->ne[2] > 1) return mul_mat_batched(W, X, Y, workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
     b2s::I2sWeight w;
     if ((rc = weight_view(W, &w, "W"))) return rc;
     int64_t M, Kx, ldx, My, Ny, ldy;

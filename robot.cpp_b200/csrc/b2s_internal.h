@@ -59,8 +59,15 @@ __device__ __forceinline__ float gelu_tanh(float x) {
     return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, det_tanhf(inner)));
 }
 
+// Independent problems of one GEMV launch (grid dimension y): problem b reads the weight codes at
+// codes + b * w_stride bytes (the tensor's one scale is shared), activations at q + b * q_stride bytes, scales
+// and sums at + b * a_stride elements, and writes y + b * y_stride floats. count = 1 is a plain call.
+struct GemvBatch {
+    int count = 1;
+    int64_t w_stride = 0, q_stride = 0, a_stride = 0, y_stride = 0;
+};
 cudaError_t launch_gemv_i2s(const I2sWeight& w, const Q8Act& a, float* y, int64_t ldy, const Epilogue& epi,
-                            cudaStream_t st);
+                            cudaStream_t st, const GemvBatch& bt = GemvBatch{});
 
 // Tensor-core path. mode 0: Y = W*q (+ epilogue). mode 1 (gate/up): P = relu(Wg*q)^2 * (Wu*q).
 // tmap_* are built by the caller (host) for these exact buffers.

@@ -50,9 +50,14 @@ template <int MT>
 __global__ void __launch_bounds__(kGemvWarps * 32)
 gemv_i2s_kernel(const uint8_t* __restrict__ codes, const float* __restrict__ wscale, int N, int Kp,
                 const int8_t* __restrict__ q, int64_t ldq, int K, int mrows, const float* __restrict__ s,
-                const int32_t* __restrict__ sums, float* y, int64_t ldy, const Epilogue epi) {
+                const int32_t* __restrict__ sums, float* y, int64_t ldy, const Epilogue epi, const GemvBatch bt) {
     extern __shared__ __align__(16) uint8_t q_sm[];  // MT x Kp int8, zero beyond K and beyond mrows
     __shared__ int red[kGemvWarps][kGemvRows][MT];
+    codes += (int64_t)blockIdx.y * bt.w_stride;  // problem blockIdx.y of a batched launch
+    q += (int64_t)blockIdx.y * bt.q_stride;
+    s += (int64_t)blockIdx.y * bt.a_stride;
+    sums += (int64_t)blockIdx.y * bt.a_stride;
+    y += (int64_t)blockIdx.y * bt.y_stride;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int r = lane >> 1, h = lane & 1;
@@ -202,10 +207,15 @@ template <int NT, int ROWT>  // NT n-tiles of 8 tokens; ROWT row tiles of 16 row
 __global__ void __launch_bounds__(kGemvWarps * 32)
 gemv_i2s_mma_kernel(const uint8_t* __restrict__ codes, const float* __restrict__ wscale, int N, int Kp,
                     const int8_t* __restrict__ q, int64_t ldq, int K, int mrows, const float* __restrict__ s,
-                    const int32_t* __restrict__ sums, float* y, int64_t ldy, const Epilogue epi) {
+                    const int32_t* __restrict__ sums, float* y, int64_t ldy, const Epilogue epi, const GemvBatch bt) {
     constexpr int MT = 8 * NT, WPT = kGemvWarps / ROWT;  // warps per row tile
     extern __shared__ __align__(16) uint8_t q_sm[];  // MT rows of (Kp + kMmaQPad) int8, zero past K / mrows
     __shared__ int red[kGemvWarps][kGemvRows][MT];
+    codes += (int64_t)blockIdx.y * bt.w_stride;  // problem blockIdx.y of a batched launch
+    q += (int64_t)blockIdx.y * bt.q_stride;
+    s += (int64_t)blockIdx.y * bt.a_stride;
+    sums += (int64_t)blockIdx.y * bt.a_stride;
+    y += (int64_t)blockIdx.y * bt.y_stride;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int rt = warp / WPT, ws = warp - rt * WPT;  // row tile, K share within it
@@ -329,7 +339,8 @@ gemv_i2s_mma_kernel(const uint8_t* __restrict__ codes, const float* __restrict__
 
 template <int NT, int ROWT>
 static cudaError_t launch_mma_nt(const I2sWeight& w, const int8_t* q, int64_t ldq, int mrows, const float* s,
-                                 const int32_t* sums, float* y, int64_t ldy, const Epilogue& epi, cudaStream_t st) {
+                                 const int32_t* sums, float* y, int64_t ldy, const Epilogue& epi, const GemvBatch& bt,
+                                 cudaStream_t st) {
     const size_t smem = (size_t)(8 * NT) * (size_t)(w.Kp + kMmaQPad);
     auto kfn = gemv_i2s_mma_kernel<NT, ROWT>;
     static int opted_in = 0;
@@ -339,7 +350,7 @@ static cudaError_t launch_mma_nt(const I2sWeight& w, const int8_t* q, int64_t ld
         opted_in = (int)smem;
     }
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)ceil_div(w.N, ROWT * kGemvRows));
+    cfg.gridDim = dim3((unsigned)ceil_div(w.N, ROWT * kGemvRows), (unsigned)bt.count);
     cfg.blockDim = dim3(kGemvWarps * 32);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
@@ -349,13 +360,13 @@ static cudaError_t launch_mma_nt(const I2sWeight& w, const int8_t* q, int64_t ld
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     return cudaLaunchKernelEx(&cfg, kfn, w.codes, w.scale, (int)w.N, (int)w.Kp, q, ldq, (int)w.K, mrows, s, sums, y,
-                              ldy, epi);
+                              ldy, epi, bt);
 }
 
 // Row tiles per CTA for the MMA GEMV: enough CTAs to keep about one per SM streaming weights, and as few
 // as that allows, so the activations (staged by every CTA) are re-read as little as possible.
-static int mma_row_tiles(int64_t N) {
-    const int64_t tiles = ceil_div(N, kGemvRows);
+static int mma_row_tiles(int64_t N, int count) {
+    const int64_t tiles = ceil_div(N, kGemvRows) * count;
     if (tiles >= 4 * 148) return 4;
     if (tiles >= 2 * 148) return 2;
     return 1;
@@ -363,17 +374,19 @@ static int mma_row_tiles(int64_t N) {
 
 template <int NT>
 static cudaError_t launch_mma(const I2sWeight& w, const int8_t* q, int64_t ldq, int mrows, const float* s,
-                              const int32_t* sums, float* y, int64_t ldy, const Epilogue& epi, cudaStream_t st) {
-    switch (mma_row_tiles(w.N)) {
-        case 4: return launch_mma_nt<NT, 4>(w, q, ldq, mrows, s, sums, y, ldy, epi, st);
-        case 2: return launch_mma_nt<NT, 2>(w, q, ldq, mrows, s, sums, y, ldy, epi, st);
-        default: return launch_mma_nt<NT, 1>(w, q, ldq, mrows, s, sums, y, ldy, epi, st);
+                              const int32_t* sums, float* y, int64_t ldy, const Epilogue& epi, const GemvBatch& bt,
+                              cudaStream_t st) {
+    switch (mma_row_tiles(w.N, bt.count)) {
+        case 4: return launch_mma_nt<NT, 4>(w, q, ldq, mrows, s, sums, y, ldy, epi, bt, st);
+        case 2: return launch_mma_nt<NT, 2>(w, q, ldq, mrows, s, sums, y, ldy, epi, bt, st);
+        default: return launch_mma_nt<NT, 1>(w, q, ldq, mrows, s, sums, y, ldy, epi, bt, st);
     }
 }
 
 template <int MT>
 static cudaError_t launch_mt(const I2sWeight& w, const int8_t* q, int64_t ldq, int mrows, const float* s,
-                             const int32_t* sums, float* y, int64_t ldy, const Epilogue& epi, cudaStream_t st) {
+                             const int32_t* sums, float* y, int64_t ldy, const Epilogue& epi, const GemvBatch& bt,
+                             cudaStream_t st) {
     const size_t smem = (size_t)MT * (size_t)w.Kp;
     auto kfn = gemv_i2s_kernel<MT>;
     // Dynamic + static shared memory above 48 KB needs the opt-in attribute (raised once per size).
@@ -384,7 +397,7 @@ static cudaError_t launch_mt(const I2sWeight& w, const int8_t* q, int64_t ldq, i
         opted_in = (int)smem;
     }
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)ceil_div(w.N, kGemvRows));
+    cfg.gridDim = dim3((unsigned)ceil_div(w.N, kGemvRows), (unsigned)bt.count);
     cfg.blockDim = dim3(kGemvWarps * 32);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
@@ -394,13 +407,14 @@ static cudaError_t launch_mt(const I2sWeight& w, const int8_t* q, int64_t ldq, i
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     return cudaLaunchKernelEx(&cfg, kfn, w.codes, w.scale, (int)w.N, (int)w.Kp, q, ldq, (int)w.K, mrows, s, sums, y,
-                              ldy, epi);
+                              ldy, epi, bt);
 }
 
 cudaError_t launch_gemv_i2s(const I2sWeight& w, const Q8Act& a, float* y, int64_t ldy, const Epilogue& epi,
-                            cudaStream_t st) {
+                            cudaStream_t st, const GemvBatch& bt) {
     // Token groups of up to 16, each one pass over the weights; a group of m tokens runs the smallest
-    // power-of-two variant >= m with the extra token rows zero.
+    // power-of-two variant >= m with the extra token rows zero. A batched call (bt.count problems) runs each
+    // token group of every problem in the same launch.
     for (int64_t m0 = 0; m0 < a.M; m0 += 16) {
         const int mt = (int)((a.M - m0) < 16 ? (a.M - m0) : 16);
         const int8_t* q = a.q + m0 * a.ldq;
@@ -410,9 +424,9 @@ cudaError_t launch_gemv_i2s(const I2sWeight& w, const Q8Act& a, float* y, int64_
         Epilogue ep = epi;  // the residual rows move with the token group
         if (ep.residual) ep.residual += m0 * ep.ld_res;
         cudaError_t e;
-        if (mt == 1) e = launch_mt<1>(w, q, a.ldq, mt, s, sums, yy, ldy, ep, st);
-        else if (mt <= 8) e = launch_mma<1>(w, q, a.ldq, mt, s, sums, yy, ldy, ep, st);
-        else e = launch_mma<2>(w, q, a.ldq, mt, s, sums, yy, ldy, ep, st);
+        if (mt == 1) e = launch_mt<1>(w, q, a.ldq, mt, s, sums, yy, ldy, ep, bt, st);
+        else if (mt <= 8) e = launch_mma<1>(w, q, a.ldq, mt, s, sums, yy, ldy, ep, bt, st);
+        else e = launch_mma<2>(w, q, a.ldq, mt, s, sums, yy, ldy, ep, bt, st);
         if (e != cudaSuccess) return e;
     }
     return cudaGetLastError();

@@ -339,3 +339,66 @@ def test_errors_before_launch(b2s):
         b2s.mul_mat(W, torch.zeros((4, K + 16), dtype=torch.float32, device="cuda"), y, ws)
     assert e.value.status == b2s.B2S_ERR_INVALID_ARG
     sync_ok(b2s)
+
+
+# ------------------------------------------------------------------------------------------ batched (ggml ne[2])
+@pytest.mark.parametrize("M", [1, 5, 16, 40])
+@pytest.mark.parametrize("K,N,B", [(2560, 2560, 3), (1152, 4304, 2), (256, 40, 5), (208, 64, 3)])
+def test_mul_mat_q8_batched(b2s, orc, M, K, N, B):
+    """B independent problems in one call (one GEMV launch for M <= 16, a GEMM per matrix above): problem b
+    equals the oracle's mul_mat of matrix b alone, bit for bit."""
+    g = wl.rng(900 + M + K + N + B)
+    ws = [wl.weight(g, N, K) for _ in range(B)]
+    # One tensor: the B matrices' codes back to back, then the shared 32-byte scale trailer (all matrices
+    # carry the first matrix's scale).
+    sc = np.float32(ws[0].scale)
+    packed = [orc.i2s_pack_ternary(w.t, float(sc)) for w in ws]
+    body = np.concatenate([p[:-32] for p in packed] + [packed[0][-32:]])
+    rp = K % 128 != 0
+    buf = dev(body)
+    if rp:  # row-pad every matrix (the flattened layout of B*N rows) on the device
+        rbuf = torch.zeros(b2s.i2s_r_nbytes(B * N, K), dtype=torch.uint8, device="cuda")
+        b2s.repack_rows(buf, rbuf, B * N, K)
+        buf = rbuf
+    W = b2s.i2s_tensor_batched(buf, N, K, B, rowpadded=rp)
+    xs = [wl.activations(g, M, K) for _ in range(B)]
+    ldq = (K + 15) // 16 * 16
+    q = torch.zeros((B, M, ldq), dtype=torch.int8, device="cuda")[:, :, :K]
+    s = torch.zeros((B, M), dtype=torch.float32, device="cuda")
+    u = torch.zeros((B, M), dtype=torch.int32, device="cuda")
+    for b in range(B):
+        b2s.act_quant(dev(xs[b]), q[b], s[b], u[b])
+    y = torch.full((B, M, N), float("nan"), dtype=torch.float32, device="cuda")
+    b2s.mul_mat_q8_batched(W, q, s, u, y)
+    sync_ok(b2s)
+    got = y.cpu().numpy()
+    for b in range(B):
+        ref = orc.mul_mat_i2s(packed[b], xs[b], N) if M * N * K <= 64 * 1024 * 1024 else \
+            orc.fast_mul_mat_i2s(packed[b], xs[b], N, os.cpu_count() or 8)
+        assert np.array_equal(got[b], ref), b
+
+
+def test_mul_mat_batched_ne2(b2s, orc):
+    """b2s_mul_mat with ne[2] = 4 (fp32 X in, act-quant of all 4x7 tokens in one launch)."""
+    B, M, K, N = 4, 7, 2560, 640
+    g = wl.rng(950)
+    ws = [wl.weight(g, N, K) for _ in range(B)]
+    sc = float(ws[0].scale)
+    packed = [orc.i2s_pack_ternary(w.t, sc) for w in ws]
+    buf = dev(np.concatenate([p[:-32] for p in packed] + [packed[0][-32:]]))
+    W = b2s.i2s_tensor_batched(buf, N, K, B)
+    x = np.stack([wl.activations(g, M, K) for _ in range(B)])
+    xd = dev(x.reshape(B * M, K))
+    y = torch.full((B * M, N), float("nan"), dtype=torch.float32, device="cuda")
+    X, Y = b2s.f32_tensor(xd), b2s.f32_tensor(y)
+    for T_, rows in ((X, M), (Y, M)):
+        T_.ne[1], T_.ne[2] = rows, B
+        T_.nb[2] = T_.nb[1] * rows
+        T_.nb[3] = T_.nb[2] * B
+    ws_buf = torch.empty(b2s.mul_mat_workspace_size(W, X), dtype=torch.uint8, device="cuda")
+    import ctypes as C
+    b2s.check(b2s.lib().b2s_mul_mat(C.byref(W), C.byref(X), C.byref(Y), ws_buf.data_ptr(), ws_buf.numel(), None))
+    sync_ok(b2s)
+    got = y.cpu().numpy().reshape(B, M, N)
+    for b in range(B):
+        assert np.array_equal(got[b], orc.mul_mat_i2s(packed[b], x[b], N)), b
