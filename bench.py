@@ -67,6 +67,8 @@ def parse():
     p.add_argument("--observations", type=int, default=64, help="server: observations in the whole job")
     p.add_argument("--obs-batch", type=int, default=8, help="server: observations per forward")
     p.add_argument("--sweep-m", default="", help="sweep: comma-separated M values (default: all five)")
+    p.add_argument("--sweep-kn", default="", help="sweep: comma-separated KxN shapes (default: all four)")
+    p.add_argument("--batched-only", action="store_true", help="sweep: decode sizes as batched launches only")
     p.add_argument("--no-extras", action="store_true", help="server: headline only, no sub-objects")
     a = p.parse_args()
     if a.workload == "bitvla":
@@ -855,7 +857,7 @@ def batched_weights(dev, K, N, seed, min_bytes):
     return big, b2s.i2s_tensor_batched(big, N, K, R, rowpadded=bool(K % 128)), R, wbytes
 
 
-def run_sweep(local, ms_list=None, reps=5):
+def run_sweep(local, ms_list=None, reps=5, kn_list=None, batched_only=False):
     """Config 4 on one GPU: per point TOP/s and algorithmic GB/s per launch of b2s_mul_mat_q8; for the decode
     sizes (M <= 16) also the batched form (b2s_mul_mat_q8_batched: one GEMV launch streaming R matrices of the
     shape, > 2x L2 of weights), per matrix."""
@@ -866,10 +868,12 @@ def run_sweep(local, ms_list=None, reps=5):
     hbm = peaks()[0]["hbm_gbs"]
     stream = torch.cuda.Stream(device=dev)
     rows = []
-    for K, N in SWEEP_KN:
+    for K, N in (kn_list or SWEEP_KN):
         copies, wbytes = rotating_weights(dev, K, N, K + N)
         R = len(copies)
         for Mt in (ms_list or SWEEP_M):
+            if batched_only and Mt > 16:
+                continue
             ldq = (K + 15) // 16 * 16
             q = torch.randint(-127, 128, (Mt, ldq), dtype=torch.int8, device=dev)[:, :K]
             s = torch.rand(Mt, device=dev) + 0.5
@@ -880,7 +884,7 @@ def run_sweep(local, ms_list=None, reps=5):
             def seq():
                 for r in range(launches):
                     b2s.mul_mat_q8(copies[r % R][1], q, s, u, y, stream=stream)
-            us = time_graph(seq, stream, launches, reps)
+            us = time_graph(seq, stream, launches, reps) if not batched_only else float("nan")
             assert b2s.device_error() == 0
             ops = 2.0 * Mt * N * K
             byts = wbytes + Mt * K + 8 * Mt + 4 * Mt * N
@@ -1061,7 +1065,8 @@ def main_sweep(a, world, rank, local):
         return
     D.close()
     ms_list = [int(x) for x in a.sweep_m.split(",")] if a.sweep_m else None
-    sub = run_sweep(local, ms_list)
+    kn_list = [tuple(int(v) for v in s_.split("x")) for s_ in a.sweep_kn.split(",")] if a.sweep_kn else None
+    sub = run_sweep(local, ms_list, kn_list=kn_list, batched_only=a.batched_only)
     big = [r["TOP/s"] for r in sub["rows"] if r["M"] >= 4096]
     print(json.dumps({"metric": METRIC, "value": round(sum(big) / max(1, len(big)), 1),
                       "unit": "TOP/s (mean over M >= 4096)", "n_gpus": 1, "steps": 5, "warmup": 3,
