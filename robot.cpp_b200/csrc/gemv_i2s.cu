@@ -383,6 +383,138 @@ static cudaError_t launch_mma(const I2sWeight& w, const int8_t* q, int64_t ldq, 
     }
 }
 
+// ------------------------------------------------------------------------------------------------
+// One token, streaming form for launches with many rows (batched problems): every warp owns 16 weight
+// rows at a time over the full K (lane pair per row, 16 bytes of each 32-byte block per lane, 8 loads in
+// flight per lane), loops over row groups g = blockIdx.x * 8 + warp + i * 8 * gridDim.x, and issues the
+// next group's first loads before it reduces and stores the current group. The token's codes are staged
+// once per CTA; there is no K split across warps and no shared-memory reduction, so a CTA's fixed costs
+// (one activation staging, one barrier) are paid once for many rows. Same arithmetic as gemv_i2s_kernel.
+__global__ void __launch_bounds__(kGemvWarps * 32)
+gemv1_stream_kernel(const uint8_t* __restrict__ codes, const float* __restrict__ wscale, int N, int Kp,
+                    const int8_t* __restrict__ q, int K, const float* __restrict__ s, const int32_t* __restrict__ sums,
+                    float* y, const Epilogue epi, const GemvBatch bt) {
+    extern __shared__ __align__(16) uint8_t q1_sm[];  // Kp int8, zero beyond K
+    codes += (int64_t)blockIdx.y * bt.w_stride;
+    q += (int64_t)blockIdx.y * bt.q_stride;
+    s += (int64_t)blockIdx.y * bt.a_stride;
+    sums += (int64_t)blockIdx.y * bt.a_stride;
+    y += (int64_t)blockIdx.y * bt.y_stride;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int r = lane >> 1, h = lane & 1;
+    const int nblk = Kp / kQK;
+    const int64_t rbytes = Kp / 4;
+    const int ngroups = (N + kGemvRows - 1) / kGemvRows;
+    const int gstride = (int)gridDim.x * kGemvWarps;
+    auto row_ptr = [&](int gg) {
+        const int row = gg * kGemvRows + r;
+        return codes + (int64_t)(row < N ? row : 0) * rbytes + 16 * h;
+    };
+    int g = (int)blockIdx.x * kGemvWarps + warp;
+    bool live = g < ngroups;
+    const uint8_t* wr = row_ptr(live ? g : 0);
+    uint4 wv[kGemvUnroll];
+    int b = 0, cnt = live ? min(kGemvUnroll, nblk) : 0;
+#pragma unroll
+    for (int u = 0; u < kGemvUnroll; ++u)
+        if (u < cnt) wv[u] = ld_stream_v4(wr + 32 * u);
+    griddep_launch();
+    griddep_wait();  // the token's codes come from the preceding kernel
+    const bool q_vec = ((reinterpret_cast<uintptr_t>(q) & 15) == 0) && (K % 16 == 0);
+    for (int i = threadIdx.x; i < Kp / 16; i += blockDim.x) {
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (q_vec) {
+            if (16 * i < K) v = *reinterpret_cast<const uint4*>(q + 16 * i);
+        } else {
+            uint8_t tmp[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) tmp[j] = (16 * i + j < K) ? (uint8_t)q[16 * i + j] : 0;
+            v = *reinterpret_cast<uint4*>(tmp);
+        }
+        reinterpret_cast<uint4*>(q1_sm)[i] = v;
+    }
+    const float s0 = s[0];
+    const int32_t sum0 = sums[0];
+    __syncthreads();
+    const uint4* q4 = reinterpret_cast<const uint4*>(q1_sm);
+    int acc = 0;
+    while (live) {
+#pragma unroll
+        for (int u = 0; u < kGemvUnroll; ++u) {
+            if (u < cnt) {
+                const int bb = b + u;
+                const uint32_t w[4] = {wv[u].x, wv[u].y, wv[u].z, wv[u].w};
+#pragma unroll
+                for (int gp = 0; gp < 4; ++gp) {
+                    const uint4 qv = q4[8 * bb + 2 * gp + h];
+                    acc = dp4a_us((w[0] >> (6 - 2 * gp)) & 0x03030303u, (int)qv.x, acc);
+                    acc = dp4a_us((w[1] >> (6 - 2 * gp)) & 0x03030303u, (int)qv.y, acc);
+                    acc = dp4a_us((w[2] >> (6 - 2 * gp)) & 0x03030303u, (int)qv.z, acc);
+                    acc = dp4a_us((w[3] >> (6 - 2 * gp)) & 0x03030303u, (int)qv.w, acc);
+                }
+            }
+        }
+        b += cnt;
+        if (b < nblk) {  // next chunk of this group
+            cnt = min(kGemvUnroll, nblk - b);
+#pragma unroll
+            for (int u = 0; u < kGemvUnroll; ++u)
+                if (u < cnt) wv[u] = ld_stream_v4(wr + 32 * (b + u));
+            continue;
+        }
+        // Group done: start the next group's loads, then reduce and store this one.
+        const int row = g * kGemvRows + r;
+        const int gn = g + gstride;
+        const bool live_n = gn < ngroups;
+        const uint8_t* wr_n = row_ptr(live_n ? gn : 0);
+        const int cnt_n = live_n ? min(kGemvUnroll, nblk) : 0;
+#pragma unroll
+        for (int u = 0; u < kGemvUnroll; ++u)
+            if (u < cnt_n) wv[u] = ld_stream_v4(wr_n + 32 * u);
+        const int tot = acc + __shfl_xor_sync(0xffffffffu, acc, 1);
+        if (h == 0 && row < N) {
+            const float rs = __fdiv_rn(__ldg(wscale + (epi.scale_rows ? row / epi.scale_rows : 0)), s0);
+            float v = __fmul_rn((float)(tot - sum0), rs);
+            if (epi.bias) v = __fadd_rn(v, epi.bias[row]);
+            if (epi.act == 1) v = gelu_tanh(v);
+            if (epi.residual) v = __fadd_rn(epi.residual[row], v);
+            y[row] = v;
+        }
+        acc = 0;
+        g = gn;
+        wr = wr_n;
+        b = 0;
+        cnt = cnt_n;
+        live = live_n;
+    }
+}
+
+// Row groups of 16 per warp: the streaming kernel serves launches with at least this many groups in total
+// (every SM busy with 8-warp CTAs); smaller launches use the K-split kernel, which spreads few rows over
+// more warps.
+constexpr int64_t kStreamMinGroups = 148 * 8 * 2;
+
+static cudaError_t launch_stream1(const I2sWeight& w, const int8_t* q, const float* s, const int32_t* sums, float* y,
+                                  const Epilogue& epi, const GemvBatch& bt, cudaStream_t st) {
+    const int64_t ngroups = ceil_div(w.N, kGemvRows);
+    const int64_t total = ngroups * bt.count;
+    // Groups per warp: enough that a CTA's fixed costs are amortized, while keeping ~8 CTAs per SM.
+    int64_t gpw = total / (148 * 8 * 8);
+    gpw = gpw < 1 ? 1 : (gpw > 8 ? 8 : gpw);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)ceil_div(ngroups, kGemvWarps * gpw), (unsigned)bt.count);
+    cfg.blockDim = dim3(kGemvWarps * 32);
+    cfg.dynamicSmemBytes = (size_t)w.Kp;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, gemv1_stream_kernel, w.codes, w.scale, (int)w.N, (int)w.Kp, q, (int)w.K, s, sums,
+                              y, epi, bt);
+}
+
 template <int MT>
 static cudaError_t launch_mt(const I2sWeight& w, const int8_t* q, int64_t ldq, int mrows, const float* s,
                              const int32_t* sums, float* y, int64_t ldy, const Epilogue& epi, const GemvBatch& bt,
@@ -424,7 +556,9 @@ cudaError_t launch_gemv_i2s(const I2sWeight& w, const Q8Act& a, float* y, int64_
         Epilogue ep = epi;  // the residual rows move with the token group
         if (ep.residual) ep.residual += m0 * ep.ld_res;
         cudaError_t e;
-        if (mt == 1) e = launch_mt<1>(w, q, a.ldq, mt, s, sums, yy, ldy, ep, bt, st);
+        if (mt == 1 && ceil_div(w.N, kGemvRows) * bt.count >= kStreamMinGroups && w.Kp <= 48 * 1024)
+            e = launch_stream1(w, q, s, sums, yy, ep, bt, st);
+        else if (mt == 1) e = launch_mt<1>(w, q, a.ldq, mt, s, sums, yy, ldy, ep, bt, st);
         else if (mt <= 8) e = launch_mma<1>(w, q, a.ldq, mt, s, sums, yy, ldy, ep, bt, st);
         else e = launch_mma<2>(w, q, a.ldq, mt, s, sums, yy, ldy, ep, bt, st);
         if (e != cudaSuccess) return e;
