@@ -337,6 +337,171 @@ gemv_i2s_mma_kernel(const uint8_t* __restrict__ codes, const float* __restrict__
     }
 }
 
+// ------------------------------------------------------------------------------------------------
+// 2..16 tokens, streaming form for launches with many rows (batched problems): the warp MMA arithmetic of
+// gemv_i2s_mma_kernel, but every warp owns one 16-row tile over the full K and loops over row tiles
+// (tile i = blockIdx.x * 8 + warp + i * 8 * gridDim.x), issuing the next tile's first weight loads before it
+// writes the current tile's outputs. All token rows are staged once per CTA; no K split, no shared-memory
+// reduction.
+template <int NT>
+__global__ void __launch_bounds__(kGemvWarps * 32)
+gemv_mma_stream_kernel(const uint8_t* __restrict__ codes, const float* __restrict__ wscale, int N, int Kp,
+                       const int8_t* __restrict__ q, int64_t ldq, int K, int mrows, const float* __restrict__ s,
+                       const int32_t* __restrict__ sums, float* y, int64_t ldy, const Epilogue epi,
+                       const GemvBatch bt) {
+    extern __shared__ __align__(16) uint8_t qs_sm[];  // mrows rows of (Kp + kMmaQPad) int8, zero past K
+    __shared__ float s_sm[8 * NT];
+    __shared__ int32_t u_sm[8 * NT];
+    codes += (int64_t)blockIdx.y * bt.w_stride;
+    q += (int64_t)blockIdx.y * bt.q_stride;
+    s += (int64_t)blockIdx.y * bt.a_stride;
+    sums += (int64_t)blockIdx.y * bt.a_stride;
+    y += (int64_t)blockIdx.y * bt.y_stride;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int g = lane >> 2, t = lane & 3;
+    const int nblk = Kp / kQK;
+    const int64_t rbytes = Kp / 4;
+    const int ntiles = (N + kGemvRows - 1) / kGemvRows;
+    const int tstride = (int)gridDim.x * kGemvWarps;
+    int tile = (int)blockIdx.x * kGemvWarps + warp;
+    bool live = tile < ntiles;
+    auto rows_of = [&](int tt, const uint8_t*& wa, const uint8_t*& wb, bool& oka, bool& okb) {
+        const int ra = tt * kGemvRows + g, rb = ra + 8;
+        oka = ra < N;
+        okb = rb < N;
+        wa = codes + (int64_t)(oka ? ra : 0) * rbytes + 8 * t;
+        wb = codes + (int64_t)(okb ? rb : 0) * rbytes + 8 * t;
+    };
+    const uint8_t *wa, *wb;
+    bool ok_a, ok_b;
+    rows_of(live ? tile : 0, wa, wb, ok_a, ok_b);
+    uint2 va[kGemvUnroll], vb[kGemvUnroll];
+    int b = 0, cnt = live ? min(kGemvUnroll, nblk) : 0;
+    auto load = [&](int b0, int c) {
+#pragma unroll
+        for (int u = 0; u < kGemvUnroll; ++u) {
+            if (u < c) {
+                va[u] = ok_a ? ld_stream_v2(wa + 32 * (b0 + u)) : make_uint2(0x55555555u, 0x55555555u);
+                vb[u] = ok_b ? ld_stream_v2(wb + 32 * (b0 + u)) : make_uint2(0x55555555u, 0x55555555u);
+            }
+        }
+    };
+    load(0, cnt);
+    griddep_launch();
+    griddep_wait();  // activations, scales and sums come from the preceding kernel
+    const int qstride = Kp + kMmaQPad;
+    const int cpr = Kp / 16;
+    const bool q_vec = ((ldq & 15) == 0) && ((reinterpret_cast<uintptr_t>(q) & 15) == 0) && (K % 16 == 0);
+    for (int i = threadIdx.x; i < mrows * cpr; i += blockDim.x) {
+        const int m = i / cpr, k0 = 16 * (i - m * cpr);
+        if (q_vec) {
+            const bool in = k0 < K;
+            cp_async_16(qs_sm + (size_t)m * qstride + k0, in ? (const void*)(q + (int64_t)m * ldq + k0) : (const void*)q,
+                        in ? 16u : 0u);
+        } else {
+            uint8_t tmp[16];
+            const int8_t* src = q + (int64_t)m * ldq + k0;
+#pragma unroll
+            for (int j = 0; j < 16; ++j) tmp[j] = (k0 + j < K) ? (uint8_t)src[j] : 0;
+            *reinterpret_cast<uint4*>(qs_sm + (size_t)m * qstride + k0) = *reinterpret_cast<uint4*>(tmp);
+        }
+    }
+    if (threadIdx.x < 8 * NT) {
+        s_sm[threadIdx.x] = threadIdx.x < mrows ? s[threadIdx.x] : 1.0f;
+        u_sm[threadIdx.x] = threadIdx.x < mrows ? sums[threadIdx.x] : 0;
+    }
+    cp_async_wait_all();
+    __syncthreads();
+    const uint8_t* qg = qs_sm + (size_t)g * qstride + 8 * t;
+    int acc[NT][4];
+#pragma unroll
+    for (int n = 0; n < NT; ++n)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) acc[n][i] = 0;
+    while (live) {
+#pragma unroll
+        for (int u = 0; u < kGemvUnroll; ++u) {
+            if (u < cnt) {
+                const int bb = b + u;
+#pragma unroll
+                for (int p = 0; p < 4; ++p) {
+                    const int sh = 6 - 2 * p;
+                    const uint32_t a0 = (va[u].x >> sh) & 0x03030303u, a2 = (va[u].y >> sh) & 0x03030303u;
+                    const uint32_t a1 = (vb[u].x >> sh) & 0x03030303u, a3 = (vb[u].y >> sh) & 0x03030303u;
+#pragma unroll
+                    for (int n = 0; n < NT; ++n) {
+                        const uint2 bv = (8 * n + g < mrows)
+                            ? *reinterpret_cast<const uint2*>(qg + (size_t)(8 * n) * qstride + 128 * bb + 32 * p)
+                            : make_uint2(0u, 0u);
+                        mma_u8s8_16832(acc[n], a0, a1, a2, a3, bv.x, bv.y);
+                    }
+                }
+            }
+        }
+        b += cnt;
+        if (b < nblk) {
+            cnt = min(kGemvUnroll, nblk - b);
+            load(b, cnt);
+            continue;
+        }
+        // Tile done: start the next tile's loads, then write this tile's outputs.
+        const int row_a = tile * kGemvRows + g;
+        const int tn = tile + tstride;
+        live = tn < ntiles;
+        rows_of(live ? tn : 0, wa, wb, ok_a, ok_b);
+        cnt = live ? min(kGemvUnroll, nblk) : 0;
+        b = 0;
+        load(0, cnt);
+        // D fragment: acc[n][0..1] = row g, tokens 8n + 2t + {0,1}; acc[n][2..3] = row g + 8, same tokens.
+#pragma unroll
+        for (int n = 0; n < NT; ++n)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const int m = 8 * n + 2 * t + (i & 1), row = row_a + 8 * (i >> 1);
+                if (m < mrows && row < N) {
+                    const float rs = __fdiv_rn(__ldg(wscale + (epi.scale_rows ? row / epi.scale_rows : 0)), s_sm[m]);
+                    float v = __fmul_rn((float)(acc[n][i] - u_sm[m]), rs);
+                    if (epi.bias) v = __fadd_rn(v, epi.bias[row]);
+                    if (epi.act == 1) v = gelu_tanh(v);
+                    if (epi.residual) v = __fadd_rn(epi.residual[(int64_t)m * epi.ld_res + row], v);
+                    y[(int64_t)m * ldy + row] = v;
+                }
+                acc[n][i] = 0;
+            }
+        tile = tn;
+    }
+}
+
+template <int NT>
+static cudaError_t launch_mma_stream(const I2sWeight& w, const int8_t* q, int64_t ldq, int mrows, const float* s,
+                                     const int32_t* sums, float* y, int64_t ldy, const Epilogue& epi,
+                                     const GemvBatch& bt, cudaStream_t st) {
+    const size_t smem = (size_t)mrows * (size_t)(w.Kp + kMmaQPad);
+    auto kfn = gemv_mma_stream_kernel<NT>;
+    static int opted_in = 0;
+    if (smem > 48 * 1024 && (int)smem > opted_in) {
+        cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+        opted_in = (int)smem;
+    }
+    const int64_t ntiles = ceil_div(w.N, kGemvRows);
+    const int64_t total = ntiles * bt.count;
+    int64_t tpw = total / (148 * 8 * 8);
+    tpw = tpw < 1 ? 1 : (tpw > 8 ? 8 : tpw);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)ceil_div(ntiles, kGemvWarps * tpw), (unsigned)bt.count);
+    cfg.blockDim = dim3(kGemvWarps * 32);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kfn, w.codes, w.scale, (int)w.N, (int)w.Kp, q, ldq, (int)w.K, mrows, s, sums, y,
+                              ldy, epi, bt);
+}
+
 template <int NT, int ROWT>
 static cudaError_t launch_mma_nt(const I2sWeight& w, const int8_t* q, int64_t ldq, int mrows, const float* s,
                                  const int32_t* sums, float* y, int64_t ldy, const Epilogue& epi, const GemvBatch& bt,
@@ -559,6 +724,10 @@ cudaError_t launch_gemv_i2s(const I2sWeight& w, const Q8Act& a, float* y, int64_
         if (mt == 1 && ceil_div(w.N, kGemvRows) * bt.count >= kStreamMinGroups && w.Kp <= 48 * 1024)
             e = launch_stream1(w, q, s, sums, yy, ep, bt, st);
         else if (mt == 1) e = launch_mt<1>(w, q, a.ldq, mt, s, sums, yy, ldy, ep, bt, st);
+        else if (ceil_div(w.N, kGemvRows) * bt.count >= kStreamMinGroups &&
+                 (size_t)mt * (size_t)(w.Kp + kMmaQPad) <= 200 * 1024)
+            e = (mt <= 8) ? launch_mma_stream<1>(w, q, a.ldq, mt, s, sums, yy, ldy, ep, bt, st)
+                          : launch_mma_stream<2>(w, q, a.ldq, mt, s, sums, yy, ldy, ep, bt, st);
         else if (mt <= 8) e = launch_mma<1>(w, q, a.ldq, mt, s, sums, yy, ldy, ep, bt, st);
         else e = launch_mma<2>(w, q, a.ldq, mt, s, sums, yy, ldy, ep, bt, st);
         if (e != cudaSuccess) return e;
