@@ -413,11 +413,13 @@ gemv_mma_stream_kernel(const uint8_t* __restrict__ codes, const float* __restric
     cp_async_wait_all();
     __syncthreads();
     const uint8_t* qg = qs_sm + (size_t)g * qstride + 8 * t;
-    int acc[NT][4];
+    int acc[2][NT][4];  // two MMA chains per n-tile (even / odd bit-planes), summed at the end of a tile
 #pragma unroll
-    for (int n = 0; n < NT; ++n)
+    for (int c = 0; c < 2; ++c)
 #pragma unroll
-        for (int i = 0; i < 4; ++i) acc[n][i] = 0;
+        for (int n = 0; n < NT; ++n)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) acc[c][n][i] = 0;
     while (live) {
 #pragma unroll
         for (int u = 0; u < kGemvUnroll; ++u) {
@@ -433,7 +435,7 @@ gemv_mma_stream_kernel(const uint8_t* __restrict__ codes, const float* __restric
                         const uint2 bv = (8 * n + g < mrows)
                             ? *reinterpret_cast<const uint2*>(qg + (size_t)(8 * n) * qstride + 128 * bb + 32 * p)
                             : make_uint2(0u, 0u);
-                        mma_u8s8_16832(acc[n], a0, a1, a2, a3, bv.x, bv.y);
+                        mma_u8s8_16832(acc[p & 1][n], a0, a1, a2, a3, bv.x, bv.y);
                     }
                 }
             }
@@ -460,13 +462,13 @@ gemv_mma_stream_kernel(const uint8_t* __restrict__ codes, const float* __restric
                 const int m = 8 * n + 2 * t + (i & 1), row = row_a + 8 * (i >> 1);
                 if (m < mrows && row < N) {
                     const float rs = __fdiv_rn(__ldg(wscale + (epi.scale_rows ? row / epi.scale_rows : 0)), s_sm[m]);
-                    float v = __fmul_rn((float)(acc[n][i] - u_sm[m]), rs);
+                    float v = __fmul_rn((float)(acc[0][n][i] + acc[1][n][i] - u_sm[m]), rs);
                     if (epi.bias) v = __fadd_rn(v, epi.bias[row]);
                     if (epi.act == 1) v = gelu_tanh(v);
                     if (epi.residual) v = __fadd_rn(epi.residual[(int64_t)m * epi.ld_res + row], v);
                     y[(int64_t)m * ldy + row] = v;
                 }
-                acc[n][i] = 0;
+                acc[0][n][i] = acc[1][n][i] = 0;
             }
         tile = tn;
     }
@@ -602,7 +604,7 @@ gemv1_stream_kernel(const uint8_t* __restrict__ codes, const float* __restrict__
     const int32_t sum0 = sums[0];
     __syncthreads();
     const uint4* q4 = reinterpret_cast<const uint4*>(q1_sm);
-    int acc = 0;
+    int acc[4] = {0, 0, 0, 0};  // one chain per bit-plane (exact int32 sums: any order gives the same total)
     while (live) {
 #pragma unroll
         for (int u = 0; u < kGemvUnroll; ++u) {
@@ -612,10 +614,12 @@ gemv1_stream_kernel(const uint8_t* __restrict__ codes, const float* __restrict__
 #pragma unroll
                 for (int gp = 0; gp < 4; ++gp) {
                     const uint4 qv = q4[8 * bb + 2 * gp + h];
-                    acc = dp4a_us((w[0] >> (6 - 2 * gp)) & 0x03030303u, (int)qv.x, acc);
-                    acc = dp4a_us((w[1] >> (6 - 2 * gp)) & 0x03030303u, (int)qv.y, acc);
-                    acc = dp4a_us((w[2] >> (6 - 2 * gp)) & 0x03030303u, (int)qv.z, acc);
-                    acc = dp4a_us((w[3] >> (6 - 2 * gp)) & 0x03030303u, (int)qv.w, acc);
+                    int a = acc[gp];
+                    a = dp4a_us((w[0] >> (6 - 2 * gp)) & 0x03030303u, (int)qv.x, a);
+                    a = dp4a_us((w[1] >> (6 - 2 * gp)) & 0x03030303u, (int)qv.y, a);
+                    a = dp4a_us((w[2] >> (6 - 2 * gp)) & 0x03030303u, (int)qv.z, a);
+                    a = dp4a_us((w[3] >> (6 - 2 * gp)) & 0x03030303u, (int)qv.w, a);
+                    acc[gp] = a;
                 }
             }
         }
@@ -636,7 +640,8 @@ gemv1_stream_kernel(const uint8_t* __restrict__ codes, const float* __restrict__
 #pragma unroll
         for (int u = 0; u < kGemvUnroll; ++u)
             if (u < cnt_n) wv[u] = ld_stream_v4(wr_n + 32 * u);
-        const int tot = acc + __shfl_xor_sync(0xffffffffu, acc, 1);
+        const int part = (acc[0] + acc[1]) + (acc[2] + acc[3]);
+        const int tot = part + __shfl_xor_sync(0xffffffffu, part, 1);
         if (h == 0 && row < N) {
             const float rs = __fdiv_rn(__ldg(wscale + (epi.scale_rows ? row / epi.scale_rows : 0)), s0);
             float v = __fmul_rn((float)(tot - sum0), rs);
@@ -645,7 +650,7 @@ gemv1_stream_kernel(const uint8_t* __restrict__ codes, const float* __restrict__
             if (epi.residual) v = __fadd_rn(epi.residual[row], v);
             y[row] = v;
         }
-        acc = 0;
+        acc[0] = acc[1] = acc[2] = acc[3] = 0;
         g = gn;
         wr = wr_n;
         b = 0;
