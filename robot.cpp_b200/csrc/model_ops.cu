@@ -325,7 +325,7 @@ cudaError_t launch_embed_tokens(const int32_t* tokens, int n, int D, uint32_t se
 
 // ------------------------------------------------------------------------------------------------ attention
 // softmax(Q K^T * scale [+ causal mask]) V for `batch` sequences of T tokens (sequence b at rows
-// [b T, (b+1) T) of every operand), one CTA per (128-query block, head, sequence).
+// [b T, (b+1) T) of every operand), one CTA per (64-query block, head, sequence), two CTAs per SM.
 // Keys are visited in chunks of 64 (chunk c = keys [64c, 64c + 64)) with an online softmax, in a fixed
 // fp32 operation order that the CPU oracle repeats exactly. For query row i (n_i = i + 1 keys if causal,
 // else T; keys j >= n_i count as masked):
@@ -337,40 +337,26 @@ cudaError_t launch_embed_tokens(const int32_t* tokens, int n, int D, uint32_t se
 //              chunk's keys in ascending order
 //   (m starts at -inf, l and o at +0); finally out[d] = o[d] * (1 / l). A chunk where the row has no
 // key leaves l and o unchanged (alpha = 1, p = 0), so each row's result depends only on its own keys.
-// Query head h reads K/V head h / (heads / kv_heads) (GQA). hd % 8 == 0, hd <= 128.
-constexpr int kAtQ = 128, kAtC = 64, kAtThreads = 256, kAtPP = kAtC + 4;  // P row stride (floats)
+// Query head h reads K/V head h / (heads / kv_heads) (GQA). Shared memory: Q^T [hd][64], one K^T or V
+// chunk, the 64 x 64 probability tile and per-row factors; hd % 8 == 0, hd <= 128.
+constexpr int kAtQ = 64, kAtThreads = 256, kAtPP = kAtQ + 4;  // P row stride (floats)
 
-// Shared memory: Q^T [hd][128], one K^T chunk [hd][64], two V chunks [64][hd] (the next one lands by
-// cp.async while the current is consumed), the 128 x 64 probability tile and per-row factors.
 size_t attention_smem_bytes(int /*T*/, int hd) {
-    return sizeof(float) * ((size_t)hd * kAtQ + (size_t)hd * kAtC + 2 * (size_t)kAtC * hd + (size_t)kAtQ * kAtPP +
-                            2 * kAtQ);
+    return sizeof(float) * ((size_t)hd * kAtQ * 2 + (size_t)kAtQ * kAtPP + 2 * kAtQ);
 }
 
-__device__ __forceinline__ void at_cp_async_16(float* smem_dst, const float* src, uint32_t src_bytes) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(smem_dst)), "l"(src), "r"(src_bytes)
-                 : "memory");
-}
-
-// One CTA per (128-query block, head, sequence), 256 threads, one CTA per SM. Score threads own 8 rows x 4
-// keys of a 64-key chunk (the 16 threads of a half-warp cover one row's 64 keys, so the chunk's max and
-// butterfly sum stay inside the half-warp); output threads own 8 rows x 8 head dimensions. The next chunk's
-// K (to be transposed) is loaded into registers and its V copied by cp.async while the current chunk is
-// computed. Every row sees the same fp32 operation sequence as with 64-query blocks: chunks lie on the
-// same 64-key boundaries, and the extra keys a bigger block visits past a row's last key are exact no-ops
-// (p = 0, fma(0, v, o) = o, a fully masked chunk has alpha = det_exp(0) = 1).
-__global__ void __launch_bounds__(kAtThreads, 1)
+__global__ void __launch_bounds__(kAtThreads, 2)
 attention_kernel(const float* __restrict__ q, int64_t ldq, const float* __restrict__ k, int64_t ldk,
                  const float* __restrict__ v, int64_t ldv, float* __restrict__ o, int64_t ldo, int T, int heads,
                  int kv_heads, int hd, float scale, int causal) {
     extern __shared__ __align__(16) float at_sm[];
-    float* Qt = at_sm;                      // [hd][128]
-    float* Kt = Qt + hd * kAtQ;             // [hd][64]
-    float* Vb = Kt + hd * kAtC;             // 2 x [64][hd]
-    float* P = Vb + 2 * kAtC * hd;          // [128][kAtPP]
-    float* alpha_sm = P + kAtQ * kAtPP;     // [128]
-    float* inv_sm = alpha_sm + kAtQ;        // [128]
-    // Grid (heads, batch, query blocks), the last (heaviest under a causal mask) query block first.
+    float* Qt = at_sm;                 // [hd][64]
+    float* KV = Qt + hd * kAtQ;        // K^T chunk [hd][64] or V chunk [64][hd]
+    float* P = KV + hd * kAtQ;         // [64][kAtPP] probabilities of the chunk
+    float* alpha_sm = P + kAtQ * kAtPP;   // [64] per-row rescale of the chunk
+    float* inv_sm = alpha_sm + kAtQ;      // [64] 1 / l at the end
+    // Grid (heads, batch, query blocks) with the last query block first: under a causal mask block b
+    // visits b + 1 key chunks, so launching the heaviest blocks first shortens the grid's tail.
     const int h = blockIdx.x, g = h / (heads / kv_heads);
     const int q0 = (int)(gridDim.z - 1u - blockIdx.z) * kAtQ;
     const int64_t row0 = (int64_t)blockIdx.y * T;
@@ -392,89 +378,58 @@ attention_kernel(const float* __restrict__ q, int64_t ldq, const float* __restri
         Qt[(d4 + 3) * kAtQ + i] = x.w;
     }
     const int kend = causal ? min(T, q0 + kAtQ) : T;  // keys any query of this block can see
-    const int nchunks = (kend + kAtC - 1) / kAtC;
+    const int nchunks = (kend + kAtQ - 1) / kAtQ;
 
-    constexpr int kKreg = kAtC * 32 / kAtThreads;  // float4 per thread of a K chunk (hd <= 128)
-    float4 kreg[kKreg];
-    auto load_k = [&](int k0) {
-#pragma unroll
-        for (int i = 0; i < kKreg; ++i) {
-            const int e = t + i * kAtThreads;
-            kreg[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (e < kAtC * hd4) {
-                const int j = e % kAtC, d4 = 4 * (e / kAtC);
-                if (k0 + j < T) kreg[i] = *reinterpret_cast<const float4*>(kh + (int64_t)(k0 + j) * ldk + d4);
-            }
-        }
-    };
-    auto copy_v = [&](int k0, float* dst) {
-        for (int e = t; e < kAtC * hd4; e += kAtThreads) {
-            const int j = e / hd4, d4 = 4 * (e % hd4);
-            const bool in = k0 + j < T;
-            at_cp_async_16(dst + j * hd + d4, in ? vh + (int64_t)(k0 + j) * ldv + d4 : vh, in ? 16u : 0u);
-        }
-        asm volatile("cp.async.commit_group;" ::: "memory");
-    };
-    load_k(0);
-    copy_v(0, Vb);
-
-    // score threads: rows 8 ty .. 8 ty + 7, keys 4 tx .. 4 tx + 3 of the chunk
+    // score threads: rows 4 ty .. 4 ty + 3, keys 4 tx .. 4 tx + 3 of the chunk (the 16 tx of a row are
+    // 16 consecutive lanes of one warp)
     const int ty = t / 16, tx = t % 16;
-    float m_r[8], l_r[8];
+    float m_r[4], l_r[4];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
+    for (int i = 0; i < 4; ++i) {
         m_r[i] = -INFINITY;
         l_r[i] = 0.0f;
     }
-    // output threads: rows 8 rg .. 8 rg + 7, head dimensions 8 cg .. 8 cg + 7
+    // output threads: rows 4 rg .. 4 rg + 3, columns 8 cg .. 8 cg + 7
     const int ncg = hd / 8;
-    const int rg = t / 16, cg = t % 16;
-    const bool active = cg < ncg;
-    float acc[8][8];
+    const bool active = t < 16 * ncg;
+    const int rg = active ? t / ncg : 0, cg = active ? t % ncg : 0;
+    float acc[4][8];
 #pragma unroll
-    for (int i = 0; i < 8; ++i)
+    for (int i = 0; i < 4; ++i)
 #pragma unroll
         for (int j = 0; j < 8; ++j) acc[i][j] = 0.0f;
 
     for (int c = 0; c < nchunks; ++c) {
-        const int k0 = c * kAtC;
-        float* Vc = Vb + (c & 1) * kAtC * hd;
-        __syncthreads();  // the previous chunk's K^T, P and V reads are done (and Q^T is written)
-#pragma unroll
-        for (int i = 0; i < kKreg; ++i) {
-            const int e = t + i * kAtThreads;
-            if (e < kAtC * hd4) {
-                const int j = e % kAtC, d4 = 4 * (e / kAtC);
-                Kt[(d4 + 0) * kAtC + j] = kreg[i].x;
-                Kt[(d4 + 1) * kAtC + j] = kreg[i].y;
-                Kt[(d4 + 2) * kAtC + j] = kreg[i].z;
-                Kt[(d4 + 3) * kAtC + j] = kreg[i].w;
-            }
+        const int k0 = c * kAtQ;
+        __syncthreads();  // Qt written; the previous chunk's V and P reads are done
+        for (int e = t; e < kAtQ * hd4; e += kAtThreads) {
+            const int j = e % kAtQ, d4 = 4 * (e / kAtQ);
+            float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (k0 + j < T) x = *reinterpret_cast<const float4*>(kh + (int64_t)(k0 + j) * ldk + d4);
+            KV[(d4 + 0) * kAtQ + j] = x.x;
+            KV[(d4 + 1) * kAtQ + j] = x.y;
+            KV[(d4 + 2) * kAtQ + j] = x.z;
+            KV[(d4 + 3) * kAtQ + j] = x.w;
         }
-        if (c + 1 < nchunks) {
-            copy_v(k0 + kAtC, Vb + ((c + 1) & 1) * kAtC * hd);
-            load_k(k0 + kAtC);
-        }
-        __syncthreads();  // K^T of this chunk is in place
-        float sc[8][4];
+        __syncthreads();
+        float sc[4][4];
 #pragma unroll
-        for (int i = 0; i < 8; ++i)
+        for (int i = 0; i < 4; ++i)
 #pragma unroll
             for (int j = 0; j < 4; ++j) sc[i][j] = 0.0f;
 #pragma unroll 4
         for (int d = 0; d < hd; ++d) {
-            const float4 a0 = *reinterpret_cast<const float4*>(&Qt[d * kAtQ + 8 * ty]);
-            const float4 a1 = *reinterpret_cast<const float4*>(&Qt[d * kAtQ + 8 * ty + 4]);
-            const float4 b = *reinterpret_cast<const float4*>(&Kt[d * kAtC + 4 * tx]);
-            const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w}, bv[4] = {b.x, b.y, b.z, b.w};
+            const float4 a = *reinterpret_cast<const float4*>(&Qt[d * kAtQ + 4 * ty]);
+            const float4 b = *reinterpret_cast<const float4*>(&KV[d * kAtQ + 4 * tx]);
+            const float av[4] = {a.x, a.y, a.z, a.w}, bv[4] = {b.x, b.y, b.z, b.w};
 #pragma unroll
-            for (int i = 0; i < 8; ++i)
+            for (int i = 0; i < 4; ++i)
 #pragma unroll
                 for (int j = 0; j < 4; ++j) sc[i][j] = __fmaf_rn(av[i], bv[j], sc[i][j]);
         }
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            const int row = 8 * ty + i, qi = q0 + row;
+        for (int i = 0; i < 4; ++i) {
+            const int row = 4 * ty + i, qi = q0 + row;
             const int nk = (qi < T) ? (causal ? qi + 1 : T) : 0;
             float cm = -INFINITY;
 #pragma unroll
@@ -500,30 +455,36 @@ attention_kernel(const float* __restrict__ q, int64_t ldq, const float* __restri
             *reinterpret_cast<float4*>(&P[row * kAtPP + 4 * tx]) = pv;
             if (tx == 0) alpha_sm[row] = alpha;
         }
-        if (c + 1 < nchunks) asm volatile("cp.async.wait_group 1;" ::: "memory");
-        else asm volatile("cp.async.wait_group 0;" ::: "memory");
-        __syncthreads();  // P, alpha and this chunk's V are in place
+        __syncthreads();  // P and alpha written; K^T chunk consumed
+        for (int e = t; e < kAtQ * hd4; e += kAtThreads) {
+            const int j = e / hd4, d4 = 4 * (e % hd4);
+            float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (k0 + j < T) x = *reinterpret_cast<const float4*>(vh + (int64_t)(k0 + j) * ldv + d4);
+            *reinterpret_cast<float4*>(&KV[j * hd + d4]) = x;
+        }
+        __syncthreads();
         if (active) {
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                const float al = alpha_sm[8 * rg + i];
+            for (int i = 0; i < 4; ++i) {
+                const float al = alpha_sm[4 * rg + i];
 #pragma unroll
                 for (int j = 0; j < 8; ++j) acc[i][j] = __fmul_rn(acc[i][j], al);
             }
-            const int jn = min(kAtC, kend - k0);
+            const int jn = min(kAtQ, kend - k0);
+            // four keys per step: each row's four probabilities are one 16-byte load (the P row stride keeps
+            // 4-key groups aligned); keys past jn are skipped, so every output sees the same fma sequence
             for (int j4 = 0; j4 < jn; j4 += 4) {
-                float4 p4[8];
+                float4 p4[4];
 #pragma unroll
-                for (int i = 0; i < 8; ++i) p4[i] = *reinterpret_cast<const float4*>(&P[(8 * rg + i) * kAtPP + j4]);
+                for (int i = 0; i < 4; ++i) p4[i] = *reinterpret_cast<const float4*>(&P[(4 * rg + i) * kAtPP + j4]);
 #pragma unroll
                 for (int kk = 0; kk < 4; ++kk) {
                     if (j4 + kk < jn) {
-                        const float* vr = Vc + (j4 + kk) * hd + 8 * cg;
-                        const float4 v0 = *reinterpret_cast<const float4*>(vr);
-                        const float4 v1 = *reinterpret_cast<const float4*>(vr + 4);
+                        const float4 v0 = *reinterpret_cast<const float4*>(&KV[(j4 + kk) * hd + 8 * cg]);
+                        const float4 v1 = *reinterpret_cast<const float4*>(&KV[(j4 + kk) * hd + 8 * cg + 4]);
                         const float vv[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
 #pragma unroll
-                        for (int i = 0; i < 8; ++i) {
+                        for (int i = 0; i < 4; ++i) {
                             const float pr = (kk == 0) ? p4[i].x : (kk == 1) ? p4[i].y : (kk == 2) ? p4[i].z : p4[i].w;
 #pragma unroll
                             for (int j = 0; j < 8; ++j) acc[i][j] = __fmaf_rn(pr, vv[j], acc[i][j]);
@@ -535,15 +496,15 @@ attention_kernel(const float* __restrict__ q, int64_t ldq, const float* __restri
     }
     if (tx == 0) {
 #pragma unroll
-        for (int i = 0; i < 8; ++i) inv_sm[8 * ty + i] = (l_r[i] > 0.0f) ? __fdiv_rn(1.0f, l_r[i]) : 0.0f;
+        for (int i = 0; i < 4; ++i) inv_sm[4 * ty + i] = (l_r[i] > 0.0f) ? __fdiv_rn(1.0f, l_r[i]) : 0.0f;
     }
     __syncthreads();
     if (active) {
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            const int qi = q0 + 8 * rg + i;
+        for (int i = 0; i < 4; ++i) {
+            const int qi = q0 + 4 * rg + i;
             if (qi >= T) continue;
-            const float inv = inv_sm[8 * rg + i];
+            const float inv = inv_sm[4 * rg + i];
             float* orow = o + (row0 + qi) * ldo + (int64_t)h * hd + 8 * cg;
             *reinterpret_cast<float4*>(orow) = make_float4(__fmul_rn(acc[i][0], inv), __fmul_rn(acc[i][1], inv),
                                                            __fmul_rn(acc[i][2], inv), __fmul_rn(acc[i][3], inv));
