@@ -29,8 +29,8 @@ Sub-objects of the same line (each with its own timing, described in its keys):
 kernels (BitNet's ggml fork) are not in the reference tree, so this is the oracle port (the CPU
 restatement), on all host threads, on the same workload and config; it never loads the CUDA library.
 
---workload ffn / sweep run one sub-workload alone (the commands some profiles under profiles/ were taken
-with).
+--workload ffn / sweep / roofline run one sub-workload alone (the commands some profiles under profiles/ were
+taken with); roofline is the headline's GEMM measurement at the 8-observation decoder shape.
 """
 from __future__ import annotations
 
@@ -62,7 +62,7 @@ def parse():
                    help="timed steps (default: 5 jobs of --observations for server, 2000 FFN blocks for ffn)")
     p.add_argument("--warmup", type=int, default=None, help="untimed warm-up steps (default: 3 server, 20 ffn)")
     p.add_argument("--impl", default="b2s", choices=["b2s", "reference"])
-    p.add_argument("--workload", default="server", choices=["server", "bitvla", "ffn", "sweep"])
+    p.add_argument("--workload", default="server", choices=["server", "bitvla", "ffn", "sweep", "roofline"])
     p.add_argument("--cpu-seconds", type=float, default=6.0, help="bounded CPU-baseline sample length (FFN)")
     p.add_argument("--observations", type=int, default=64, help="server: observations in the whole job")
     p.add_argument("--obs-batch", type=int, default=8, help="server: observations per forward")
@@ -1075,11 +1075,24 @@ def main_sweep(a, world, rank, local):
                       "config": {"workload": "i2s_gemm_sweep"}, "sweep": sub}), flush=True)
 
 
+def main_roofline(a, world, rank, local):
+    D, dev = setup(world, rank, local)
+    r = gemm_roofline(dev, a.obs_batch * 288)
+    D.close()
+    if rank == 0:
+        print(json.dumps({"metric": METRIC, "value": r["achieved"], "unit": r["unit"], "n_gpus": 1, "steps": 128,
+                          "warmup": 32, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                          "dtype": "int8xternary->int32", "data": "synthetic",
+                          "config": {"workload": "gemm_gate_up_m2304"}, "roofline": r}), flush=True)
+
+
 def main():
     a = parse()
     world, rank, local = dist_env()
     if a.impl == "reference":
         run_reference(a, world, rank)
+    elif a.workload == "roofline":
+        main_roofline(a, world, rank, local)
     elif a.workload == "sweep":
         main_sweep(a, world, rank, local)
     elif a.workload == "ffn":
