@@ -73,9 +73,12 @@ EncodeTiledFn encode_fn() {
     return fn;
 }
 
-// 2D u8 tensor map: inner dim `cols` bytes, `rows` rows of stride `ld` bytes, box box_c x box_r.
+// 2D u8 tensor map: inner dim `cols` bytes, `rows` rows of stride `ld` bytes, box box_c x box_r, shared-memory
+// swizzle `swz` (the activation tiles use 128-byte swizzle for the MMA descriptors; the 32-byte packed weight
+// rows use 32-byte swizzle, which swaps the two 16-byte halves of every other group of four rows so that the
+// converter warps' row reads are free of bank conflicts).
 int make_tmap_u8(CUtensorMap* m, const void* ptr, uint64_t cols, uint64_t rows, uint64_t ld, uint32_t box_c,
-                 uint32_t box_r, bool swizzle128) {
+                 uint32_t box_r, CUtensorMapSwizzle swz) {
     EncodeTiledFn fn = encode_fn();
     if (!fn) return fail(B2S_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
     if ((reinterpret_cast<uintptr_t>(ptr) & 15) != 0) return fail(B2S_ERR_UNSUPPORTED, "TMA base not 16-byte aligned");
@@ -86,8 +89,7 @@ int make_tmap_u8(CUtensorMap* m, const void* ptr, uint64_t cols, uint64_t rows, 
     cuuint32_t box[2] = {box_c, box_r};
     cuuint32_t estr[2] = {1, 1};
     CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(ptr), dims, strides, box, estr,
-                    CU_TENSOR_MAP_INTERLEAVE_NONE,
-                    swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return fail(B2S_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
     return B2S_OK;
@@ -284,14 +286,15 @@ int run_tc(const b2s::I2sWeight& w0, const b2s::I2sWeight* w1, const int8_t* q, 
     b2s::TcGemmArgs a;
     memset(&a, 0, sizeof(a));
     int rc;
-    if ((rc = make_tmap_u8(&a.tmap_q, q, (uint64_t)w0.K, (uint64_t)M, (uint64_t)ldq, 128, (uint32_t)t.bn_sub, true)))
+    if ((rc = make_tmap_u8(&a.tmap_q, q, (uint64_t)w0.K, (uint64_t)M, (uint64_t)ldq, 128, (uint32_t)t.bn_sub,
+                           CU_TENSOR_MAP_SWIZZLE_128B)))
         return rc;
     if ((rc = make_tmap_u8(&a.tmap_w0, w0.codes, (uint64_t)(w0.Kp / 4), (uint64_t)w0.N, (uint64_t)(w0.Kp / 4), 32,
-                           (uint32_t)rows, false)))
+                           (uint32_t)rows, CU_TENSOR_MAP_SWIZZLE_32B)))
         return rc;
     if (mode == 1) {
         if ((rc = make_tmap_u8(&a.tmap_w1, w1->codes, (uint64_t)(w1->Kp / 4), (uint64_t)w1->N, (uint64_t)(w1->Kp / 4),
-                               32, (uint32_t)rows, false)))
+                               32, (uint32_t)rows, CU_TENSOR_MAP_SWIZZLE_32B)))
             return rc;
         a.y_tma = make_tmap_f32(&a.tmap_y, Y, (uint64_t)w0.N, (uint64_t)M, (uint64_t)ldy, 64, 16) ? 1 : 0;
     } else {

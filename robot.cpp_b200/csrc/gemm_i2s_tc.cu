@@ -316,8 +316,11 @@ gemm_i2s_tc_kernel(const __grid_constant__ CUtensorMap tmap_w0, const __grid_con
             // Every lane acquires the completed phase itself before reading the TMA-written bytes (the
             // phase cannot advance: stage s is refilled only after this warp arrives on afull[s]).
             (void)mbar_try_wait(&bars->wfull[s], ph);
-            const uint4* src = reinterpret_cast<const uint4*>(w_sm + (size_t)s * kWStageBytes + r_sm * 32);
-            const uint4 p0 = src[0], p1 = src[1];
+            // 32-byte swizzle: rows 4-7 of every 8 have their 16-byte halves swapped (TMA SWIZZLE_32B)
+            const uint8_t* rowp = w_sm + (size_t)s * kWStageBytes + r_sm * 32;
+            const int sw = (r_sm >> 2) & 1;
+            const uint4 p0 = *reinterpret_cast<const uint4*>(rowp + 16 * sw);
+            const uint4 p1 = *reinterpret_cast<const uint4*>(rowp + 16 * (1 - sw));
             if (lane == 0) good = mbar_wait(&bars->consumed[s], ph ^ 1u);  // TMEM A stage s is free
             if (!__shfl_sync(0xffffffffu, good, 0)) { ok = false; break; }
             const uint32_t w[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};

@@ -196,8 +196,11 @@ gemm_i2s_tcp_kernel(const __grid_constant__ CUtensorMap tmap_w0, const __grid_co
                 if (lane == 0) good = (*abort_flag == 0) && mbar_wait(&bars->full[s], (g / kStages) & 1u);
                 if (!__shfl_sync(0xffffffffu, good, 0)) { ok = false; break; }
                 (void)mbar_try_wait(&bars->full[s], (g / kStages) & 1u);  // each lane acquires the phase
-                const uint4* src = reinterpret_cast<const uint4*>(w_sm + (size_t)s * kWStageBytes + r_sm * 32);
-                const uint4 p0 = src[0], p1 = src[1];
+                // 32-byte swizzle: rows 4-7 of every 8 have their 16-byte halves swapped (TMA SWIZZLE_32B)
+                const uint8_t* rowp = w_sm + (size_t)s * kWStageBytes + r_sm * 32;
+                const int sw = (r_sm >> 2) & 1;
+                const uint4 p0 = *reinterpret_cast<const uint4*>(rowp + 16 * sw);
+                const uint4 p1 = *reinterpret_cast<const uint4*>(rowp + 16 * (1 - sw));
                 if (lane == 0 && ua > 0) good = mbar_wait(&bars->afree[a], (ua - 1) & 1u);
                 if (!__shfl_sync(0xffffffffu, good, 0)) { ok = false; break; }
                 const uint32_t w[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
