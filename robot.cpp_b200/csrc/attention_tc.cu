@@ -398,13 +398,8 @@ cudaError_t launch_attention_tc(const float* q, int64_t ldq, const float* k, int
                                 int batch, int T, int heads, int kv_heads, int hd, float scale, bool causal, float* o,
                                 int64_t ldo, cudaStream_t st) {
     if (batch <= 0 || T <= 0) return cudaSuccess;
-    static bool attr_set = false;
-    if (!attr_set) {
-        cudaError_t e = cudaFuncSetAttribute(attention_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)atc::kSmemBytes);
-        if (e != cudaSuccess) return e;
-        attr_set = true;
-    }
+    cudaError_t e = ensure_dynamic_smem(reinterpret_cast<const void*>(attention_tc_kernel), atc::kSmemBytes);
+    if (e != cudaSuccess) return e;
     const int G = heads / kv_heads, QB = atc::kRows / G;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)kv_heads, (unsigned)batch, (unsigned)((T + QB - 1) / QB));

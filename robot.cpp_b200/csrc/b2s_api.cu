@@ -10,8 +10,11 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <atomic>
+#include <map>
 #include <mutex>
 #include <string>
+#include <utility>
 
 #include "b2s.h"
 #include "b2s_common.cuh"
@@ -37,7 +40,7 @@ int cuda_fail(cudaError_t e, const char* what) {
 
 // ---------------------------------------------------------------- device check (cached per device)
 int check_device() {
-    static int cache[128];  // 0 unknown, 1 ok, 2 bad
+    static std::atomic<int> cache[128];  // 0 unknown, 1 ok, 2 bad
     int dev = -1;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
@@ -239,7 +242,7 @@ TcTiling pick_tiling(int64_t M, int64_t n_out, int rows_per_cta, int64_t Kp, int
 }
 
 int num_sms_current() {
-    static int cache[128];
+    static std::atomic<int> cache[128];
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 128) return 148;
     if (!cache[dev]) {
@@ -861,3 +864,21 @@ int b2s_soft_max_ext(const float* x, const float* mask, int64_t mask_rows, int64
 }
 
 }  // extern "C"
+
+namespace b2s {
+
+cudaError_t ensure_dynamic_smem(const void* kfn, size_t bytes) {
+    static std::mutex mu;
+    static std::map<std::pair<const void*, int>, size_t> done;  // (kernel, device) -> size set
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    std::lock_guard<std::mutex> lk(mu);
+    size_t& have = done[{kfn, dev}];
+    if (have >= bytes) return cudaSuccess;
+    e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+    if (e == cudaSuccess) have = bytes;
+    return e;
+}
+
+}  // namespace b2s

@@ -11,6 +11,11 @@
 
 namespace b2s {
 
+// Raises kernel `kfn`'s dynamic shared memory limit to at least `bytes` on the current device. The attribute
+// belongs to the function in one device's context, so the size already set is remembered per (function,
+// device); thread-safe, for engines driving several GPUs from one process.
+cudaError_t ensure_dynamic_smem(const void* kfn, size_t bytes);
+
 // Weight operand as the kernels see it: row-padded i2_s bytes (row stride Kp/4, Kp = roundup(K,128)),
 // the per-tensor fp32 scale living in device memory right after the codes.
 struct I2sWeight {
@@ -123,13 +128,16 @@ cudaError_t launch_embed_tokens(const int32_t* tokens, int n, int D, uint32_t se
                                 cudaStream_t st);
 cudaError_t launch_patch_embed(const float* img, int batch, int C, int H, int W, int P, const float* w,
                                const float* bias, const float* pos, int D, float* y, int64_t ldy, cudaStream_t st);
-// Fused fp32 attention of `batch` sequences of T tokens (operation order in model_ops.cu).
+// Fused fp32 attention of `batch` sequences of T tokens (operation order in model_ops.cu). A non-NULL
+// `rope` (the launch_rope_table table of at least T positions, 16-byte aligned) applies NEOX RoPE to Q and K
+// while they are staged, with the same result as launch_rope_apply(period T) on q and k beforehand; q and k
+// in memory are left unrotated.
 size_t attention_smem_bytes(int T, int hd);
 bool attention_supported(int T, int hd, int64_t ldq, int64_t ldk, int64_t ldv, int64_t ldo, const void* q,
                          const void* k, const void* v, const void* o);
 cudaError_t launch_attention(const float* q, int64_t ldq, const float* k, int64_t ldk, const float* v, int64_t ldv,
                              int batch, int T, int heads, int kv_heads, int hd, float scale, bool causal, float* o,
-                             int64_t ldo, cudaStream_t st);
+                             int64_t ldo, cudaStream_t st, const float2* rope = nullptr);
 
 // Tensor-core attention (attention_tc.cu): same contract, products as 3xTF32 on tcgen05, exact-max softmax.
 // Needs hd % 8 == 0, hd <= 128, 128 % (heads / kv_heads) == 0, at most 384 keys per query block, leading

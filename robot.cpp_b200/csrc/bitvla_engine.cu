@@ -477,14 +477,22 @@ int enqueue_forward(b2s_bitvla* m, int B, cudaStream_t st) {
     };
     // The bit-reproducible fp32 attention kernel unless the config asks for the tensor-core one (and the
     // shape is one it takes).
-    auto attention = [&](const float* q, int64_t ldq_, const float* k, int64_t ldk, const float* v, int64_t ldv, int batch,
-                         int T, int heads, int kv_heads, int hd, float scale, bool causal, float* o, int64_t ldo) {
+    // With `rope` (decoder layers) the fp32 kernel rotates Q and K as it stages them; the tensor-core one reads
+    // them rotated in place by a separate pass over the q and k heads.
+    auto attention = [&](float* q, int64_t ldq_, float* k, int64_t ldk, const float* v, int64_t ldv, int batch, int T,
+                         int heads, int kv_heads, int hd, float scale, bool causal, float* o, int64_t ldo,
+                         const float2* rope) {
         if (c.attention_tc &&
-            b2s::attention_tc_supported(T, heads, kv_heads, hd, causal, ldq_, ldk, ldv, ldo, q, k, v, o))
+            b2s::attention_tc_supported(T, heads, kv_heads, hd, causal, ldq_, ldk, ldv, ldo, q, k, v, o)) {
+            if (rope) {  // q heads then k heads, adjacent columns of one row
+                cudaError_t e = b2s::launch_rope_apply(q, (int64_t)batch * T, heads + kv_heads, hd, ldq_, rope, T, st);
+                if (e != cudaSuccess) return e;
+            }
             return b2s::launch_attention_tc(q, ldq_, k, ldk, v, ldv, batch, T, heads, kv_heads, hd, scale, causal, o,
                                             ldo, st);
+        }
         return b2s::launch_attention(q, ldq_, k, ldk, v, ldv, batch, T, heads, kv_heads, hd, scale, causal, o, ldo,
-                                     st);
+                                     st, rope);
     };
     // ---------------------------------------------------------------- vision tower
     TRY_CUDA(b2s::launch_patch_embed(m->img, B, 3, c.image_size, c.image_size, c.patch, m->patch_w, m->patch_b, m->pos,
@@ -498,7 +506,7 @@ int enqueue_forward(b2s_bitvla* m, int B, cudaStream_t st) {
                  "vit ln1");
         TRY_B2S(gemm(L.qkv, Mv, m->vqkv, 3 * D, L.qkv_b, nullptr, 0));
         TRY_CUDA(attention(m->vqkv, 3 * D, m->vqkv + D, 3 * D, m->vqkv + 2 * D, 3 * D, B, m->np, c.vit_heads,
-                           c.vit_heads, D / c.vit_heads, vit_scale, false, m->vattn, D),
+                           c.vit_heads, D / c.vit_heads, vit_scale, false, m->vattn, D, nullptr),
                  "vit attention");
         TRY_CUDA(b2s::launch_act_quant(m->vattn, D, nullptr, false, 0.0f, Mv, D, m->q8, ldq, m->qs, m->qsum, st),
                  "vit o act_quant");
@@ -541,11 +549,8 @@ int enqueue_forward(b2s_bitvla* m, int B, cudaStream_t st) {
         TRY_CUDA(b2s::launch_act_quant(m->dx, H, L.attn_norm, true, c.dec_eps, Md, H, m->q8, ldq, m->qs, m->qsum, st),
                  "attn_norm");
         TRY_B2S(gemm(L.qkv, Md, m->dqkv, ldqkv, nullptr, nullptr, 0));
-        TRY_CUDA(b2s::launch_rope_apply(m->dqkv, Md, c.dec_heads + c.dec_kv_heads, c.head_dim, ldqkv, m->rope, m->seq,
-                                        st),
-                 "rope");
         TRY_CUDA(attention(m->dqkv, ldqkv, m->dqkv + H, ldqkv, m->dqkv + H + KV, ldqkv, B, m->seq, c.dec_heads,
-                           c.dec_kv_heads, c.head_dim, dec_scale, true, m->dattn, H),
+                           c.dec_kv_heads, c.head_dim, dec_scale, true, m->dattn, H, m->rope),
                  "decoder attention");
         TRY_CUDA(b2s::launch_act_quant(m->dattn, H, L.attn_sub, true, c.dec_eps, Md, H, m->q8, ldq, m->qs, m->qsum, st),
                  "attn_sub_norm");

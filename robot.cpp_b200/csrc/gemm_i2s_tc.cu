@@ -38,6 +38,7 @@
 // All mbarrier waits are bounded (about one second); on a timeout the kernel records the error in
 // g_device_error, drains what it issued (bounded), still takes part in the cluster barriers, frees its
 // TMEM and returns.
+#include <atomic>
 #include "b2s_common.cuh"
 #include "b2s_internal.h"
 
@@ -582,13 +583,9 @@ gemm_i2s_tc_kernel(const __grid_constant__ CUtensorMap tmap_w0, const __grid_con
 
 template <int MODE, int EPI>
 static cudaError_t launch_variant(const TcGemmArgs& a, cudaStream_t st) {
-    static bool attr_set = false;  // per process and variant; the attribute is per function
     auto kfn = gemm_i2s_tc_kernel<MODE, EPI>;
-    if (!attr_set) {
-        cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tc::kSmemBytes);
-        if (e != cudaSuccess) return e;
-        attr_set = true;
-    }
+    cudaError_t e = ensure_dynamic_smem(reinterpret_cast<const void*>(kfn), tc::kSmemBytes);
+    if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)a.n_tiles, (unsigned)a.m_tiles, (unsigned)a.splits);
     cfg.blockDim = dim3(tc::kThreads);
@@ -611,13 +608,12 @@ static cudaError_t launch_variant(const TcGemmArgs& a, cudaStream_t st) {
 // Clusters of `size` CTAs of this kernel that can be resident at once on the current device (a cluster
 // must fit inside one GPC, so e.g. 7-CTA clusters leave SMs of every GPC idle). Cached per device/size.
 int tc_max_active_clusters(int size) {
-    static int cache[64][9];
+    static std::atomic<int> cache[64][9];
     int dev = 0;
     if (size < 1 || size > 8 || cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
     if (cache[dev][size]) return cache[dev][size];
     auto kfn = gemm_i2s_tc_kernel<0, 0>;
-    if (cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tc::kSmemBytes) != cudaSuccess)
-        return 0;
+    if (ensure_dynamic_smem(reinterpret_cast<const void*>(kfn), tc::kSmemBytes) != cudaSuccess) return 0;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(1, 1, (unsigned)size);
     cfg.blockDim = dim3(tc::kThreads);

@@ -339,13 +339,9 @@ gemm_i2s_tcp_kernel(const __grid_constant__ CUtensorMap tmap_w0, const __grid_co
 
 template <int MODE, int EPI>
 static cudaError_t launch_tcp_variant(const TcGemmArgs& a, int grid, cudaStream_t st) {
-    static bool attr_set = false;  // per process and variant; the attribute is per function
     auto kfn = gemm_i2s_tcp_kernel<MODE, EPI>;
-    if (!attr_set) {
-        cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tcp::kSmemBytes);
-        if (e != cudaSuccess) return e;
-        attr_set = true;
-    }
+    cudaError_t e = ensure_dynamic_smem(reinterpret_cast<const void*>(kfn), tcp::kSmemBytes);
+    if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)grid);
     cfg.blockDim = dim3(tcp::kThreads);

@@ -345,10 +345,51 @@ size_t attention_smem_bytes(int /*T*/, int hd) {
     return sizeof(float) * ((size_t)hd * kAtQ * 2 + (size_t)kAtQ * kAtPP + 2 * kAtQ);
 }
 
+// Rows r0 .. r0 + 63 of one head (hd floats at src + r ldsrc; rows >= T read as zero) into dst[d][64]. With
+// a rotation table (rows are positions 0 .. T-1 of their sequence) each (d, d + hd/2) pair is rotated on the
+// way in, by the same fp32 operations as rope_rotate, so Q and K arrive exactly as a separate NEOX RoPE pass
+// would have left them.
+__device__ __forceinline__ void stage_transposed(float* __restrict__ dst, const float* __restrict__ src,
+                                                 int64_t ldsrc, int r0, int T, int hd,
+                                                 const float2* __restrict__ rope) {
+    const int half = hd / 2, h4 = half / 4;
+    for (int e = threadIdx.x; e < kAtQ * h4; e += kAtThreads) {
+        const int i = e % kAtQ, d4 = 4 * (e / kAtQ);
+        float4 a = make_float4(0.f, 0.f, 0.f, 0.f), b = a;
+        if (r0 + i < T) {
+            const float* row = src + (int64_t)(r0 + i) * ldsrc;
+            a = *reinterpret_cast<const float4*>(row + d4);
+            b = *reinterpret_cast<const float4*>(row + half + d4);
+            if (rope) {
+                const float4* cs = reinterpret_cast<const float4*>(rope + (int64_t)(r0 + i) * half + d4);
+                const float4 c01 = cs[0], c23 = cs[1];  // (cos, sin) of pairs d4 .. d4 + 3
+                const float x0[4] = {a.x, a.y, a.z, a.w}, x1[4] = {b.x, b.y, b.z, b.w};
+                const float cv[4] = {c01.x, c01.z, c23.x, c23.z}, sv[4] = {c01.y, c01.w, c23.y, c23.w};
+                float y0[4], y1[4];
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    y0[c] = __fsub_rn(__fmul_rn(x0[c], cv[c]), __fmul_rn(x1[c], sv[c]));
+                    y1[c] = __fadd_rn(__fmul_rn(x0[c], sv[c]), __fmul_rn(x1[c], cv[c]));
+                }
+                a = make_float4(y0[0], y0[1], y0[2], y0[3]);
+                b = make_float4(y1[0], y1[1], y1[2], y1[3]);
+            }
+        }
+        dst[(d4 + 0) * kAtQ + i] = a.x;
+        dst[(d4 + 1) * kAtQ + i] = a.y;
+        dst[(d4 + 2) * kAtQ + i] = a.z;
+        dst[(d4 + 3) * kAtQ + i] = a.w;
+        dst[(half + d4 + 0) * kAtQ + i] = b.x;
+        dst[(half + d4 + 1) * kAtQ + i] = b.y;
+        dst[(half + d4 + 2) * kAtQ + i] = b.z;
+        dst[(half + d4 + 3) * kAtQ + i] = b.w;
+    }
+}
+
 __global__ void __launch_bounds__(kAtThreads, 2)
 attention_kernel(const float* __restrict__ q, int64_t ldq, const float* __restrict__ k, int64_t ldk,
                  const float* __restrict__ v, int64_t ldv, float* __restrict__ o, int64_t ldo, int T, int heads,
-                 int kv_heads, int hd, float scale, int causal) {
+                 int kv_heads, int hd, float scale, int causal, const float2* __restrict__ rope) {
     extern __shared__ __align__(16) float at_sm[];
     float* Qt = at_sm;                 // [hd][64]
     float* KV = Qt + hd * kAtQ;        // K^T chunk [hd][64] or V chunk [64][hd]
@@ -368,15 +409,7 @@ attention_kernel(const float* __restrict__ q, int64_t ldq, const float* __restri
     griddep_wait();  // q/k/v are written by the preceding kernel
     griddep_launch();
 
-    for (int e = t; e < kAtQ * hd4; e += kAtThreads) {
-        const int i = e % kAtQ, d4 = 4 * (e / kAtQ);
-        float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (q0 + i < T) x = *reinterpret_cast<const float4*>(qh + (int64_t)(q0 + i) * ldq + d4);
-        Qt[(d4 + 0) * kAtQ + i] = x.x;
-        Qt[(d4 + 1) * kAtQ + i] = x.y;
-        Qt[(d4 + 2) * kAtQ + i] = x.z;
-        Qt[(d4 + 3) * kAtQ + i] = x.w;
-    }
+    stage_transposed(Qt, qh, ldq, q0, T, hd, rope);
     const int kend = causal ? min(T, q0 + kAtQ) : T;  // keys any query of this block can see
     const int nchunks = (kend + kAtQ - 1) / kAtQ;
 
@@ -402,15 +435,7 @@ attention_kernel(const float* __restrict__ q, int64_t ldq, const float* __restri
     for (int c = 0; c < nchunks; ++c) {
         const int k0 = c * kAtQ;
         __syncthreads();  // Qt written; the previous chunk's V and P reads are done
-        for (int e = t; e < kAtQ * hd4; e += kAtThreads) {
-            const int j = e % kAtQ, d4 = 4 * (e / kAtQ);
-            float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (k0 + j < T) x = *reinterpret_cast<const float4*>(kh + (int64_t)(k0 + j) * ldk + d4);
-            KV[(d4 + 0) * kAtQ + j] = x.x;
-            KV[(d4 + 1) * kAtQ + j] = x.y;
-            KV[(d4 + 2) * kAtQ + j] = x.z;
-            KV[(d4 + 3) * kAtQ + j] = x.w;
-        }
+        stage_transposed(KV, kh, ldk, k0, T, hd, rope);
         __syncthreads();
         float sc[4][4];
 #pragma unroll
@@ -523,14 +548,12 @@ bool attention_supported(int T, int hd, int64_t ldq, int64_t ldk, int64_t ldv, i
 
 cudaError_t launch_attention(const float* q, int64_t ldq, const float* k, int64_t ldk, const float* v, int64_t ldv,
                              int batch, int T, int heads, int kv_heads, int hd, float scale, bool causal, float* o,
-                             int64_t ldo, cudaStream_t st) {
+                             int64_t ldo, cudaStream_t st, const float2* rope) {
     if (batch <= 0 || T <= 0) return cudaSuccess;
     const size_t smem = attention_smem_bytes(T, hd);
-    static size_t opted = 0;  // largest dynamic shared memory size enabled so far (attribute is per function)
-    if (smem > 48 * 1024 && smem > opted) {
-        cudaError_t e = cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (smem > 48 * 1024) {
+        cudaError_t e = ensure_dynamic_smem(reinterpret_cast<const void*>(attention_kernel), smem);
         if (e != cudaSuccess) return e;
-        opted = smem;
     }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)heads, (unsigned)batch, (unsigned)ceil_div(T, kAtQ));
@@ -543,7 +566,7 @@ cudaError_t launch_attention(const float* q, int64_t ldq, const float* k, int64_
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     return cudaLaunchKernelEx(&cfg, attention_kernel, q, ldq, k, ldk, v, ldv, o, ldo, T, heads, kv_heads, hd, scale,
-                              causal ? 1 : 0);
+                              causal ? 1 : 0, rope);
 }
 
 }  // namespace b2s
