@@ -867,6 +867,19 @@ int b2s_soft_max_ext(const float* x, const float* mask, int64_t mask_rows, int64
 
 namespace b2s {
 
+bool tmap_u8_2d(CUtensorMap* m, const void* ptr, uint64_t cols, uint64_t rows, uint64_t ld, uint32_t box_c,
+                uint32_t box_r, CUtensorMapSwizzle swz) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn || (reinterpret_cast<uintptr_t>(ptr) & 15) != 0 || ld % 16 != 0) return false;
+    cuuint64_t dims[2] = {cols, rows};
+    cuuint64_t strides[1] = {ld};
+    cuuint32_t box[2] = {box_c, box_r};
+    cuuint32_t estr[2] = {1, 1};
+    return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 cudaError_t ensure_dynamic_smem(const void* kfn, size_t bytes) {
     static std::mutex mu;
     static std::map<std::pair<const void*, int>, size_t> done;  // (kernel, device) -> size set

@@ -16,6 +16,11 @@ namespace b2s {
 // device); thread-safe, for engines driving several GPUs from one process.
 cudaError_t ensure_dynamic_smem(const void* kfn, size_t bytes);
 
+// 2D u8 tensor map (inner dim `cols` bytes, `rows` rows of stride `ld` bytes, box box_c x box_r, swizzle
+// swz); false when the driver entry point is missing or the base / stride is not TMA-compatible.
+bool tmap_u8_2d(CUtensorMap* m, const void* ptr, uint64_t cols, uint64_t rows, uint64_t ld, uint32_t box_c,
+                uint32_t box_r, CUtensorMapSwizzle swz);
+
 // Weight operand as the kernels see it: row-padded i2_s bytes (row stride Kp/4, Kp = roundup(K,128)),
 // the per-tensor fp32 scale living in device memory right after the codes.
 struct I2sWeight {

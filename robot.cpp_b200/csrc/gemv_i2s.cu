@@ -13,6 +13,12 @@
 // M tokens sit in shared memory and are read as broadcasts (every row of the warp reads the same
 // 32 bytes per bit-plane).
 //
+// Launches with many rows (batched decode problems, ggml ne[2]) use streaming forms instead: for one
+// token a TMA-fed kernel (per-warp shared-memory rings of 64-row x 128-byte stages, one persistent wave)
+// or, where its requirements do not hold, a register-ring kernel; for 2..16 tokens a register-ring MMA
+// kernel. A bit-plane may also be masked in place (byte & (3 << (6-2g))): its dot product then comes
+// out scaled by 4^(3-g), exactly, and is shifted back once per row.
+//
 // Weight loads for the first range are issued before griddepcontrol.wait, so when launched with
 // programmatic stream serialization the weight stream overlaps the tail of the kernel that produces
 // the activations.
@@ -24,6 +30,7 @@ namespace b2s {
 constexpr int kGemvRows = 16;   // rows per CTA
 constexpr int kGemvWarps = 8;   // warps per CTA (split K)
 constexpr int kGemvUnroll = 8;  // 16-byte loads in flight per lane
+constexpr int kS1R = 4, kS1D = 2;  // one-token streaming kernel: rows per lane, register ring depth
 
 __device__ __forceinline__ uint4 ld_stream_v4(const void* p) {
     uint4 v;
@@ -363,30 +370,32 @@ gemv_mma_stream_kernel(const uint8_t* __restrict__ codes, const float* __restric
     const int64_t rbytes = Kp / 4;
     const int ntiles = (N + kGemvRows - 1) / kGemvRows;
     const int tstride = (int)gridDim.x * kGemvWarps;
-    int tile = (int)blockIdx.x * kGemvWarps + warp;
-    bool live = tile < ntiles;
-    auto rows_of = [&](int tt, const uint8_t*& wa, const uint8_t*& wb, bool& oka, bool& okb) {
+    // The warp's blocks form one stream (tile tile0 blocks 0..nblk-1, then tile tile0 + tstride, ...); slot
+    // u of the rings va / vb holds item i with i % 8 == u and is refilled with item i + 8 as soon as item i
+    // is consumed, so eight loads per lane and row stay in flight across tile boundaries. Rows past N read
+    // row 0 (their outputs are not stored).
+    int tile = (int)blockIdx.x * kGemvWarps + warp, b = 0;  // next item to consume
+    int lt = tile, lb = 0;                                  // next item to load
+    const uint8_t *la, *lbp;
+    auto rows_of = [&](int tt) {
         const int ra = tt * kGemvRows + g, rb = ra + 8;
-        oka = ra < N;
-        okb = rb < N;
-        wa = codes + (int64_t)(oka ? ra : 0) * rbytes + 8 * t;
-        wb = codes + (int64_t)(okb ? rb : 0) * rbytes + 8 * t;
+        la = codes + (int64_t)(ra < N ? ra : 0) * rbytes + 8 * t;
+        lbp = codes + (int64_t)(rb < N ? rb : 0) * rbytes + 8 * t;
     };
-    const uint8_t *wa, *wb;
-    bool ok_a, ok_b;
-    rows_of(live ? tile : 0, wa, wb, ok_a, ok_b);
+    rows_of(lt < ntiles ? lt : 0);
     uint2 va[kGemvUnroll], vb[kGemvUnroll];
-    int b = 0, cnt = live ? min(kGemvUnroll, nblk) : 0;
-    auto load = [&](int b0, int c) {
-#pragma unroll
-        for (int u = 0; u < kGemvUnroll; ++u) {
-            if (u < c) {
-                va[u] = ok_a ? ld_stream_v2(wa + 32 * (b0 + u)) : make_uint2(0x55555555u, 0x55555555u);
-                vb[u] = ok_b ? ld_stream_v2(wb + 32 * (b0 + u)) : make_uint2(0x55555555u, 0x55555555u);
-            }
+    auto load_next = [&](int u) {
+        va[u] = ld_stream_v2(la + 32 * lb);
+        vb[u] = ld_stream_v2(lbp + 32 * lb);
+        if (++lb == nblk) {
+            lb = 0;
+            lt += tstride;
+            rows_of(lt < ntiles ? lt : 0);
         }
     };
-    load(0, cnt);
+#pragma unroll
+    for (int u = 0; u < kGemvUnroll; ++u)
+        if (lt < ntiles) load_next(u);
     griddep_launch();
     griddep_wait();  // activations, scales and sums come from the preceding kernel
     const int qstride = Kp + kMmaQPad;
@@ -413,64 +422,56 @@ gemv_mma_stream_kernel(const uint8_t* __restrict__ codes, const float* __restric
     cp_async_wait_all();
     __syncthreads();
     const uint8_t* qg = qs_sm + (size_t)g * qstride + 8 * t;
-    int acc[2][NT][4];  // two MMA chains per n-tile (even / odd bit-planes), summed at the end of a tile
+    int acc[2][NT][4];  // two MMA chains per n-tile (even / odd bit-planes), summed when a tile is done
 #pragma unroll
     for (int c = 0; c < 2; ++c)
 #pragma unroll
         for (int n = 0; n < NT; ++n)
 #pragma unroll
             for (int i = 0; i < 4; ++i) acc[c][n][i] = 0;
-    while (live) {
+    while (tile < ntiles) {
 #pragma unroll
         for (int u = 0; u < kGemvUnroll; ++u) {
-            if (u < cnt) {
-                const int bb = b + u;
+            if (tile < ntiles) {
+                const uint2 xa = va[u], xb = vb[u];
+                if (lt < ntiles) load_next(u);
 #pragma unroll
                 for (int p = 0; p < 4; ++p) {
                     const int sh = 6 - 2 * p;
-                    const uint32_t a0 = (va[u].x >> sh) & 0x03030303u, a2 = (va[u].y >> sh) & 0x03030303u;
-                    const uint32_t a1 = (vb[u].x >> sh) & 0x03030303u, a3 = (vb[u].y >> sh) & 0x03030303u;
+                    const uint32_t a0 = (xa.x >> sh) & 0x03030303u, a2 = (xa.y >> sh) & 0x03030303u;
+                    const uint32_t a1 = (xb.x >> sh) & 0x03030303u, a3 = (xb.y >> sh) & 0x03030303u;
 #pragma unroll
                     for (int n = 0; n < NT; ++n) {
                         const uint2 bv = (8 * n + g < mrows)
-                            ? *reinterpret_cast<const uint2*>(qg + (size_t)(8 * n) * qstride + 128 * bb + 32 * p)
+                            ? *reinterpret_cast<const uint2*>(qg + (size_t)(8 * n) * qstride + 128 * b + 32 * p)
                             : make_uint2(0u, 0u);
                         mma_u8s8_16832(acc[p & 1][n], a0, a1, a2, a3, bv.x, bv.y);
                     }
                 }
-            }
-        }
-        b += cnt;
-        if (b < nblk) {
-            cnt = min(kGemvUnroll, nblk - b);
-            load(b, cnt);
-            continue;
-        }
-        // Tile done: start the next tile's loads, then write this tile's outputs.
-        const int row_a = tile * kGemvRows + g;
-        const int tn = tile + tstride;
-        live = tn < ntiles;
-        rows_of(live ? tn : 0, wa, wb, ok_a, ok_b);
-        cnt = live ? min(kGemvUnroll, nblk) : 0;
-        b = 0;
-        load(0, cnt);
-        // D fragment: acc[n][0..1] = row g, tokens 8n + 2t + {0,1}; acc[n][2..3] = row g + 8, same tokens.
+                if (++b == nblk) {  // tile done: write its outputs
+                    const int row_a = tile * kGemvRows + g;
+                    // D fragment: acc[n][0..1] = row g, tokens 8n + 2t + {0,1}; acc[n][2..3] = row g + 8.
 #pragma unroll
-        for (int n = 0; n < NT; ++n)
+                    for (int n = 0; n < NT; ++n)
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const int m = 8 * n + 2 * t + (i & 1), row = row_a + 8 * (i >> 1);
-                if (m < mrows && row < N) {
-                    const float rs = __fdiv_rn(__ldg(wscale + (epi.scale_rows ? row / epi.scale_rows : 0)), s_sm[m]);
-                    float v = __fmul_rn((float)(acc[0][n][i] + acc[1][n][i] - u_sm[m]), rs);
-                    if (epi.bias) v = __fadd_rn(v, epi.bias[row]);
-                    if (epi.act == 1) v = gelu_tanh(v);
-                    if (epi.residual) v = __fadd_rn(epi.residual[(int64_t)m * epi.ld_res + row], v);
-                    y[(int64_t)m * ldy + row] = v;
+                        for (int i = 0; i < 4; ++i) {
+                            const int m = 8 * n + 2 * t + (i & 1), row = row_a + 8 * (i >> 1);
+                            if (m < mrows && row < N) {
+                                const float rs =
+                                    __fdiv_rn(__ldg(wscale + (epi.scale_rows ? row / epi.scale_rows : 0)), s_sm[m]);
+                                float v = __fmul_rn((float)(acc[0][n][i] + acc[1][n][i] - u_sm[m]), rs);
+                                if (epi.bias) v = __fadd_rn(v, epi.bias[row]);
+                                if (epi.act == 1) v = gelu_tanh(v);
+                                if (epi.residual) v = __fadd_rn(epi.residual[(int64_t)m * epi.ld_res + row], v);
+                                y[(int64_t)m * ldy + row] = v;
+                            }
+                            acc[0][n][i] = acc[1][n][i] = 0;
+                        }
+                    b = 0;
+                    tile += tstride;
                 }
-                acc[0][n][i] = acc[1][n][i] = 0;
             }
-        tile = tn;
+        }
     }
 }
 
@@ -480,11 +481,9 @@ static cudaError_t launch_mma_stream(const I2sWeight& w, const int8_t* q, int64_
                                      const GemvBatch& bt, cudaStream_t st) {
     const size_t smem = (size_t)mrows * (size_t)(w.Kp + kMmaQPad);
     auto kfn = gemv_mma_stream_kernel<NT>;
-    static int opted_in = 0;
-    if (smem > 48 * 1024 && (int)smem > opted_in) {
-        cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (smem > 48 * 1024) {
+        cudaError_t e = ensure_dynamic_smem(reinterpret_cast<const void*>(kfn), smem);
         if (e != cudaSuccess) return e;
-        opted_in = (int)smem;
     }
     const int64_t ntiles = ceil_div(w.N, kGemvRows);
     const int64_t total = ntiles * bt.count;
@@ -510,11 +509,9 @@ static cudaError_t launch_mma_nt(const I2sWeight& w, const int8_t* q, int64_t ld
                                  cudaStream_t st) {
     const size_t smem = (size_t)(8 * NT) * (size_t)(w.Kp + kMmaQPad);
     auto kfn = gemv_i2s_mma_kernel<NT, ROWT>;
-    static int opted_in = 0;
-    if (smem + sizeof(int) * kGemvWarps * kGemvRows * 8 * NT > 48 * 1024 && (int)smem > opted_in) {
-        cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (smem + sizeof(int) * kGemvWarps * kGemvRows * 8 * NT > 48 * 1024) {
+        cudaError_t e = ensure_dynamic_smem(reinterpret_cast<const void*>(kfn), smem);
         if (e != cudaSuccess) return e;
-        opted_in = (int)smem;
     }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)ceil_div(w.N, ROWT * kGemvRows), (unsigned)bt.count);
@@ -551,13 +548,15 @@ static cudaError_t launch_mma(const I2sWeight& w, const int8_t* q, int64_t ldq, 
 }
 
 // ------------------------------------------------------------------------------------------------
-// One token, streaming form for launches with many rows (batched problems): every warp owns 16 weight
-// rows at a time over the full K (lane pair per row, 16 bytes of each 32-byte block per lane, 8 loads in
-// flight per lane), loops over row groups g = blockIdx.x * 8 + warp + i * 8 * gridDim.x, and issues the
-// next group's first loads before it reduces and stores the current group. The token's codes are staged
-// once per CTA; there is no K split across warps and no shared-memory reduction, so a CTA's fixed costs
-// (one activation staging, one barrier) are paid once for many rows. Same arithmetic as gemv_i2s_kernel.
-__global__ void __launch_bounds__(kGemvWarps * 32)
+// One token, register-streaming form for launches with many rows that the TMA-fed kernel does not take
+// (problems not back to back, K % 16 != 0, unaligned activations): every warp owns 64 weight rows at a
+// time over the full K (lane (r, h) reads 16 bytes of each 32-byte block of rows r, r + 16, r + 32 and
+// r + 48), with the warp's blocks streamed through a two-item register ring (eight 16-byte loads in
+// flight per lane, refilled across group boundaries), and walks groups g = blockIdx.x * 8 + warp + i * 8 *
+// gridDim.x. The token's codes are staged once per CTA; there is no K split across warps and no
+// shared-memory reduction. The integer sums are exact, so results equal gemv_i2s_kernel's bit for bit.
+template <int R, int D>  // R rows per lane (a warp group is 16 R rows); ring depth D (items of R 16-byte loads)
+__global__ void __launch_bounds__(kGemvWarps * 32, 3)
 gemv1_stream_kernel(const uint8_t* __restrict__ codes, const float* __restrict__ wscale, int N, int Kp,
                     const int8_t* __restrict__ q, int K, const float* __restrict__ s, const int32_t* __restrict__ sums,
                     float* y, const Epilogue epi, const GemvBatch bt) {
@@ -571,20 +570,40 @@ gemv1_stream_kernel(const uint8_t* __restrict__ codes, const float* __restrict__
     const int r = lane >> 1, h = lane & 1;
     const int nblk = Kp / kQK;
     const int64_t rbytes = Kp / 4;
-    const int ngroups = (N + kGemvRows - 1) / kGemvRows;
+    constexpr int GR = 16 * R;  // rows per warp group
+    const int ngroups = (N + GR - 1) / GR;
     const int gstride = (int)gridDim.x * kGemvWarps;
-    auto row_ptr = [&](int gg) {
-        const int row = gg * kGemvRows + r;
-        return codes + (int64_t)(row < N ? row : 0) * rbytes + 16 * h;
-    };
-    int g = (int)blockIdx.x * kGemvWarps + warp;
-    bool live = g < ngroups;
-    const uint8_t* wr = row_ptr(live ? g : 0);
-    uint4 wv[kGemvUnroll];
-    int b = 0, cnt = live ? min(kGemvUnroll, nblk) : 0;
+    // Lane (r, h) owns rows r, r + 16, ..., r + 16 (R-1) of the warp's group: one activation load per
+    // bit-plane serves R rows. Rows past N read the group's first row (their outputs are not stored).
+    auto group_ptr = [&](int gg) { return codes + ((int64_t)gg * GR + r) * rbytes + 16 * h; };
+    auto row_ok = [&](int gg, int j) { return gg * GR + r + 16 * j < N; };
+    // The warp's blocks form one stream: group g0 blocks 0..nblk-1, then group g0 + gstride, ... Item i
+    // (one block of the R rows) sits in slot i % D of the ring wv; consuming it reloads the slot with
+    // item i + D, so R D 16-byte loads per lane stay in flight across group boundaries.
+    int g = (int)blockIdx.x * kGemvWarps + warp, b = 0;  // next item to consume
+    int lg = g, lb = 0;                                  // next item to load
+    const uint8_t* lp;
+    int lstep[R];  // byte offsets of the R rows from lp (Kp <= 48 K keeps 48 rows within int range)
+    auto set_group = [&](int gg) {
+        const int gc = gg < ngroups ? gg : 0;
+        lp = group_ptr(gc);
 #pragma unroll
-    for (int u = 0; u < kGemvUnroll; ++u)
-        if (u < cnt) wv[u] = ld_stream_v4(wr + 32 * u);
+        for (int j = 0; j < R; ++j) lstep[j] = row_ok(gc, j) ? 16 * j * (int)rbytes : -r * (int)rbytes;
+    };
+    set_group(lg);
+    uint4 wv[D][R];
+    auto load_next = [&](int slot) {
+#pragma unroll
+        for (int j = 0; j < R; ++j) wv[slot][j] = ld_stream_v4(lp + lstep[j] + 32 * lb);
+        if (++lb == nblk) {
+            lb = 0;
+            lg += gstride;
+            set_group(lg);
+        }
+    };
+#pragma unroll
+    for (int u = 0; u < D; ++u)
+        if (lg < ngroups) load_next(u);
     griddep_launch();
     griddep_wait();  // the token's codes come from the preceding kernel
     const bool q_vec = ((reinterpret_cast<uintptr_t>(q) & 15) == 0) && (K % 16 == 0);
@@ -603,74 +622,281 @@ gemv1_stream_kernel(const uint8_t* __restrict__ codes, const float* __restrict__
     const float s0 = s[0];
     const int32_t sum0 = sums[0];
     __syncthreads();
-    const uint4* q4 = reinterpret_cast<const uint4*>(q1_sm);
-    int acc[4] = {0, 0, 0, 0};  // one chain per bit-plane (exact int32 sums: any order gives the same total)
-    while (live) {
+    const uint4* q4 = reinterpret_cast<const uint4*>(q1_sm) + h;
+    // Bit-plane gp is masked in place (byte & (3 << (6 - 2gp))), so its chain accumulates 4^(3-gp) times
+    // the plane's exact integer dot product; the planes are shifted back when the rows are done.
+    int acc[R][4];  // [row j][plane]
 #pragma unroll
-        for (int u = 0; u < kGemvUnroll; ++u) {
-            if (u < cnt) {
-                const int bb = b + u;
-                const uint32_t w[4] = {wv[u].x, wv[u].y, wv[u].z, wv[u].w};
+    for (int j = 0; j < R; ++j)
+#pragma unroll
+        for (int p = 0; p < 4; ++p) acc[j][p] = 0;
+    while (g < ngroups) {
+#pragma unroll
+        for (int u = 0; u < D; ++u) {
+            if (g < ngroups) {
+                uint4 cur[R];
+#pragma unroll
+                for (int j = 0; j < R; ++j) cur[j] = wv[u][j];
+                if (lg < ngroups) load_next(u);
 #pragma unroll
                 for (int gp = 0; gp < 4; ++gp) {
-                    const uint4 qv = q4[8 * bb + 2 * gp + h];
-                    int a = acc[gp];
-                    a = dp4a_us((w[0] >> (6 - 2 * gp)) & 0x03030303u, (int)qv.x, a);
-                    a = dp4a_us((w[1] >> (6 - 2 * gp)) & 0x03030303u, (int)qv.y, a);
-                    a = dp4a_us((w[2] >> (6 - 2 * gp)) & 0x03030303u, (int)qv.z, a);
-                    a = dp4a_us((w[3] >> (6 - 2 * gp)) & 0x03030303u, (int)qv.w, a);
-                    acc[gp] = a;
+                    const uint32_t m = 0x03030303u << (6 - 2 * gp);
+                    const uint4 qv = q4[8 * b + 2 * gp];
+#pragma unroll
+                    for (int j = 0; j < R; ++j) {
+                        int a = acc[j][gp];
+                        a = dp4a_us(cur[j].x & m, (int)qv.x, a);
+                        a = dp4a_us(cur[j].y & m, (int)qv.y, a);
+                        a = dp4a_us(cur[j].z & m, (int)qv.z, a);
+                        a = dp4a_us(cur[j].w & m, (int)qv.w, a);
+                        acc[j][gp] = a;
+                    }
+                }
+                if (++b == nblk) {  // group done: reduce and store its rows
+                    const float ws0 = epi.scale_rows ? 0.0f : __ldg(wscale);
+#pragma unroll
+                    for (int j = 0; j < R; ++j) {
+                        const int part = ((acc[j][0] >> 6) + (acc[j][1] >> 4)) + ((acc[j][2] >> 2) + acc[j][3]);
+                        const int tot = part + __shfl_xor_sync(0xffffffffu, part, 1);
+                        const int row = g * GR + r + 16 * j;
+                        if (h == 0 && row < N) {
+                            const float wsr = epi.scale_rows ? __ldg(wscale + row / epi.scale_rows) : ws0;
+                            const float rs = __fdiv_rn(wsr, s0);
+                            float v = __fmul_rn((float)(tot - sum0), rs);
+                            if (epi.bias) v = __fadd_rn(v, epi.bias[row]);
+                            if (epi.act == 1) v = gelu_tanh(v);
+                            if (epi.residual) v = __fadd_rn(epi.residual[row], v);
+                            y[row] = v;
+                        }
+#pragma unroll
+                        for (int p = 0; p < 4; ++p) acc[j][p] = 0;
+                    }
+                    b = 0;
+                    g += gstride;
                 }
             }
         }
-        b += cnt;
-        if (b < nblk) {  // next chunk of this group
-            cnt = min(kGemvUnroll, nblk - b);
-#pragma unroll
-            for (int u = 0; u < kGemvUnroll; ++u)
-                if (u < cnt) wv[u] = ld_stream_v4(wr + 32 * (b + u));
-            continue;
-        }
-        // Group done: start the next group's loads, then reduce and store this one.
-        const int row = g * kGemvRows + r;
-        const int gn = g + gstride;
-        const bool live_n = gn < ngroups;
-        const uint8_t* wr_n = row_ptr(live_n ? gn : 0);
-        const int cnt_n = live_n ? min(kGemvUnroll, nblk) : 0;
-#pragma unroll
-        for (int u = 0; u < kGemvUnroll; ++u)
-            if (u < cnt_n) wv[u] = ld_stream_v4(wr_n + 32 * u);
-        const int part = (acc[0] + acc[1]) + (acc[2] + acc[3]);
-        const int tot = part + __shfl_xor_sync(0xffffffffu, part, 1);
-        if (h == 0 && row < N) {
-            const float rs = __fdiv_rn(__ldg(wscale + (epi.scale_rows ? row / epi.scale_rows : 0)), s0);
-            float v = __fmul_rn((float)(tot - sum0), rs);
-            if (epi.bias) v = __fadd_rn(v, epi.bias[row]);
-            if (epi.act == 1) v = gelu_tanh(v);
-            if (epi.residual) v = __fadd_rn(epi.residual[row], v);
-            y[row] = v;
-        }
-        acc[0] = acc[1] = acc[2] = acc[3] = 0;
-        g = gn;
-        wr = wr_n;
-        b = 0;
-        cnt = cnt_n;
-        live = live_n;
     }
 }
 
-// Row groups of 16 per warp: the streaming kernel serves launches with at least this many groups in total
-// (every SM busy with 8-warp CTAs); smaller launches use the K-split kernel, which spreads few rows over
-// more warps.
+// ------------------------------------------------------------------------------------------------
+// One token, TMA-fed form for launches with many rows: batched decode problems stored back to back (one
+// 2D tensor of count * N rows x Kp/4 bytes). The weight stream bypasses registers: every warp owns a
+// ring of `nst` shared-memory stages, each one 64 rows x 128 bytes (four 32-byte blocks of each row)
+// brought in by a single tiled TMA load with 128-byte swizzle, and keeps the next nst - 1 stages in flight
+// while it computes one. The grid is one persistent wave (one 8-warp CTA per SM); warp w walks the
+// contiguous range [w G / W, (w + 1) G / W) of the G = count * ceil(N / 64) row groups (problem-major), so
+// it changes problem rarely; on a change it reloads its own copy of the problem's int8 activations with
+// one bulk copy. Lane (r, h) = (lane % 16, lane / 16) reads the 16-byte half h of each block of rows
+// r + 16 j, j = 0..3; with the swizzle (16-byte chunk index XOR row % 8) the eight lanes of each
+// shared-memory phase hit eight different bank groups, and the activation loads are broadcasts. Same
+// integer arithmetic as the other one-token kernels (bit-plane masks, exact sums), same epilogue.
+// Every mbarrier wait is bounded; after a timeout the warp records it in the device error word, waits
+// (bounded) for its copies still in flight and returns.
+constexpr int kT1Warps = 8;                     // warps per CTA (one CTA per SM)
+constexpr int kT1Rows = 64;                     // rows per group
+constexpr int kT1Box = 128;                     // bytes of each row per stage
+constexpr int kT1Stage = kT1Rows * kT1Box;      // 8 KB
+
+__global__ void __launch_bounds__(kT1Warps * 32, 1)
+gemv1_tma_kernel(const __grid_constant__ CUtensorMap tmap, const float* __restrict__ wscale, int N, int Kp,
+                 const int8_t* __restrict__ q, int K, const float* __restrict__ s, const int32_t* __restrict__ sums,
+                 float* y, const Epilogue epi, const GemvBatch bt, int nst) {
+    extern __shared__ __align__(16) uint8_t t1_sm[];  // aligned to 1024 by hand below
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int r = lane & 15, h = lane >> 4;
+    // stages 1024-byte aligned (the swizzle pattern follows shared-memory address bits 7..9)
+    const uint32_t a0 = smem_u32(t1_sm), a1 = (a0 + 1023u) & ~1023u;
+    uint8_t* base = t1_sm + (a1 - a0);
+    const int kpa = (Kp + 127) & ~127;
+    uint8_t* ring = base + (size_t)warp * nst * kT1Stage;
+    uint8_t* act = base + (size_t)kT1Warps * nst * kT1Stage + (size_t)warp * kpa;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(base + (size_t)kT1Warps * nst * kT1Stage + (size_t)kT1Warps * kpa) +
+                     warp * (nst + 1);
+    uint64_t* abar = bars + nst;
+    const int nblk = Kp / kQK, rbytes = Kp / 4;
+    const int nchunk = (rbytes + kT1Box - 1) / kT1Box;
+    const int ngroups = (N + kT1Rows - 1) / kT1Rows;
+    const int64_t G = (int64_t)ngroups * bt.count;
+    const int64_t nw = (int64_t)gridDim.x * kT1Warps, gw = (int64_t)blockIdx.x * kT1Warps + warp;
+    const int64_t gbeg = gw * G / nw, gend = (gw + 1) * G / nw;
+    const int nstages = (int)(gend - gbeg) * nchunk;
+
+    if (lane == 0) {
+        for (int i = 0; i <= nst; ++i) mbar_init(&bars[i], 1);
+        fence_mbar_init();
+    }
+    __syncwarp();
+    auto issue = [&](int k) {  // lane 0
+        const int64_t gi = gbeg + k / nchunk;
+        const int p = (int)(gi / ngroups), g = (int)(gi - (int64_t)p * ngroups);
+        uint64_t* bar = &bars[k % nst];
+        mbar_arrive_expect_tx(bar, kT1Stage);
+        tma_load_2d(ring + (size_t)(k % nst) * kT1Stage, &tmap, bar, kT1Box * (k % nchunk), p * N + g * kT1Rows);
+    };
+    int issued = min(nst, nstages);
+    if (lane == 0)
+        for (int k = 0; k < issued; ++k) issue(k);
+    griddep_launch();
+    griddep_wait();  // the tokens' codes come from the preceding kernel
+    for (int i = K + 16 * lane; i < kpa; i += 16 * 32) *reinterpret_cast<uint4*>(act + i) = make_uint4(0, 0, 0, 0);
+
+    int acc[4][4];  // [row j][bit-plane], plane gp scaled by 4^(3-gp) (masked in place)
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+#pragma unroll
+        for (int p = 0; p < 4; ++p) acc[j][p] = 0;
+    int cur_p = -1;
+    uint32_t aphase = 0;
+    bool act_pending = false;
+    float s0 = 1.0f;
+    int32_t sum0 = 0;
+    bool ok = true;
+    int k = 0;
+    for (; k < nstages; ++k) {
+        const int c = k % nchunk;
+        const int64_t gi = gbeg + k / nchunk;
+        const int p = (int)(gi / ngroups), g = (int)(gi - (int64_t)p * ngroups);
+        if (p != cur_p) {  // new problem: this warp's activation copy
+            __syncwarp();
+            fence_proxy_async_smem();
+            if (lane == 0) {
+                mbar_arrive_expect_tx(abar, (uint32_t)K);
+                bulk_load(act, q + (int64_t)p * bt.q_stride, (uint32_t)K, abar);
+            }
+            act_pending = true;
+            if (!mbar_wait(abar, aphase)) {
+                ok = false;
+                break;
+            }
+            act_pending = false;
+            aphase ^= 1u;
+            s0 = s[(int64_t)p * bt.a_stride];
+            sum0 = sums[(int64_t)p * bt.a_stride];
+            cur_p = p;
+        }
+        const int slot = k % nst;
+        if (!mbar_wait(&bars[slot], (uint32_t)((k / nst) & 1))) {
+            ok = false;
+            break;
+        }
+        const uint8_t* st = ring + (size_t)slot * kT1Stage;
+        const int nb = min(4, nblk - 4 * c);
+        const uint4* q4 = reinterpret_cast<const uint4*>(act) + 32 * c + h;
+#pragma unroll
+        for (int bb = 0; bb < 4; ++bb) {
+            if (bb < nb) {
+                uint4 wv[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                    wv[j] = *reinterpret_cast<const uint4*>(st + (r + 16 * j) * kT1Box + 16 * ((2 * bb + h) ^ (r & 7)));
+#pragma unroll
+                for (int gp = 0; gp < 4; ++gp) {
+                    const uint32_t m = 0x03030303u << (6 - 2 * gp);
+                    const uint4 qv = q4[8 * bb + 2 * gp];
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        int a = acc[j][gp];
+                        a = dp4a_us(wv[j].x & m, (int)qv.x, a);
+                        a = dp4a_us(wv[j].y & m, (int)qv.y, a);
+                        a = dp4a_us(wv[j].z & m, (int)qv.z, a);
+                        a = dp4a_us(wv[j].w & m, (int)qv.w, a);
+                        acc[j][gp] = a;
+                    }
+                }
+            }
+        }
+        __syncwarp();              // every lane is done reading the slot
+        fence_proxy_async_smem();  // order those reads before the TMA load that refills it
+        if (k + nst < nstages) {
+            if (lane == 0) issue(k + nst);
+            issued = k + nst + 1;
+        }
+        if (c == nchunk - 1) {  // group done: reduce and store its 64 rows
+            float* yp = y + (int64_t)p * bt.y_stride;
+            const float ws0 = epi.scale_rows ? 0.0f : __ldg(wscale);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int part = ((acc[j][0] >> 6) + (acc[j][1] >> 4)) + ((acc[j][2] >> 2) + acc[j][3]);
+                const int tot = part + __shfl_xor_sync(0xffffffffu, part, 16);
+                const int row = g * kT1Rows + r + 16 * j;
+                if (h == 0 && row < N) {
+                    const float wsr = epi.scale_rows ? __ldg(wscale + row / epi.scale_rows) : ws0;
+                    const float rs = __fdiv_rn(wsr, s0);
+                    float v = __fmul_rn((float)(tot - sum0), rs);
+                    if (epi.bias) v = __fadd_rn(v, epi.bias[row]);
+                    if (epi.act == 1) v = gelu_tanh(v);
+                    if (epi.residual) v = __fadd_rn(epi.residual[row], v);
+                    yp[row] = v;
+                }
+#pragma unroll
+                for (int p2 = 0; p2 < 4; ++p2) acc[j][p2] = 0;
+            }
+        }
+    }
+    if (!ok) {  // drain this warp's copies still in flight before the CTA can exit
+        if (act_pending) mbar_wait(abar, aphase, 2u);
+        for (int kk = k; kk < issued; ++kk) mbar_wait(&bars[kk % nst], (uint32_t)((kk / nst) & 1), 2u);
+    }
+}
+
+// Shared memory of gemv1_tma_kernel for a ring of nst stages per warp.
+static size_t tma1_smem(int nst, int64_t Kp) {
+    const size_t kpa = (size_t)((Kp + 127) / 128 * 128);
+    return 1024 + (size_t)kT1Warps * nst * kT1Stage + (size_t)kT1Warps * kpa + (size_t)kT1Warps * (nst + 1) * 8;
+}
+
+// The TMA-fed kernel when its requirements hold (weights of all problems back to back and 16-byte
+// aligned, K % 16 == 0, aligned activations, a ring of at least two stages per warp); returns false to
+// let the caller use the register-streaming kernel.
+static bool try_launch_tma1(const I2sWeight& w, const int8_t* q, const float* s, const int32_t* sums, float* y,
+                            const Epilogue& epi, const GemvBatch& bt, cudaStream_t st, cudaError_t* err) {
+    const int64_t rbytes = w.Kp / 4;
+    if (w.K % 16 != 0 || (reinterpret_cast<uintptr_t>(q) & 15) != 0) return false;
+    if (bt.count > 1 && (bt.w_stride != w.N * rbytes || bt.q_stride % 16 != 0)) return false;
+    if (w.N * bt.count >= (int64_t)1 << 31) return false;
+    int nst = 0;
+    for (int d = 4; d >= 2 && !nst; --d)
+        if (tma1_smem(d, w.Kp) <= 227 * 1024) nst = d;
+    if (!nst) return false;
+    CUtensorMap tm;
+    if (!tmap_u8_2d(&tm, w.codes, (uint64_t)rbytes, (uint64_t)(w.N * bt.count), (uint64_t)rbytes, kT1Box, kT1Rows,
+                    CU_TENSOR_MAP_SWIZZLE_128B))
+        return false;
+    const size_t smem = tma1_smem(nst, w.Kp);
+    *err = ensure_dynamic_smem(reinterpret_cast<const void*>(gemv1_tma_kernel), smem);
+    if (*err != cudaSuccess) return true;
+    int dev = 0, sms = 148;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int64_t G = ceil_div(w.N, kT1Rows) * bt.count;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(G < (int64_t)sms * kT1Warps ? ceil_div(G, kT1Warps) : sms));
+    cfg.blockDim = dim3(kT1Warps * 32);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    *err = cudaLaunchKernelEx(&cfg, gemv1_tma_kernel, tm, w.scale, (int)w.N, (int)w.Kp, q, (int)w.K, s, sums, y, epi,
+                              bt, nst);
+    return true;
+}
+
+// 16-row tiles: the streaming kernels (TMA-fed or register ring for one token, MMA ring for 2..16) serve
+// launches with at least this many tiles in total; smaller launches use the K-split kernels, which spread
+// few rows over more warps.
 constexpr int64_t kStreamMinGroups = 148 * 8 * 2;
 
 static cudaError_t launch_stream1(const I2sWeight& w, const int8_t* q, const float* s, const int32_t* sums, float* y,
                                   const Epilogue& epi, const GemvBatch& bt, cudaStream_t st) {
-    const int64_t ngroups = ceil_div(w.N, kGemvRows);
+    const int64_t ngroups = ceil_div(w.N, (int64_t)16 * kS1R);
     const int64_t total = ngroups * bt.count;
-    // Groups per warp: enough that a CTA's fixed costs are amortized, while keeping ~8 CTAs per SM.
-    int64_t gpw = total / (148 * 8 * 8);
-    gpw = gpw < 1 ? 1 : (gpw > 8 ? 8 : gpw);
+    // Groups per warp: as few CTAs as one wave needs (each warp then streams its groups without a CTA
+    // boundary in between).
+    int64_t gpw = ceil_div(total, (int64_t)148 * 3 * kGemvWarps);
+    gpw = gpw < 1 ? 1 : gpw;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)ceil_div(ngroups, kGemvWarps * gpw), (unsigned)bt.count);
     cfg.blockDim = dim3(kGemvWarps * 32);
@@ -681,8 +907,7 @@ static cudaError_t launch_stream1(const I2sWeight& w, const int8_t* q, const flo
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, gemv1_stream_kernel, w.codes, w.scale, (int)w.N, (int)w.Kp, q, (int)w.K, s, sums,
-                              y, epi, bt);
+    return cudaLaunchKernelEx(&cfg, gemv1_stream_kernel<kS1R, kS1D>, w.codes, w.scale, (int)w.N, (int)w.Kp, q, (int)w.K, s, sums, y, epi, bt);
 }
 
 template <int MT>
@@ -691,12 +916,10 @@ static cudaError_t launch_mt(const I2sWeight& w, const int8_t* q, int64_t ldq, i
                              cudaStream_t st) {
     const size_t smem = (size_t)MT * (size_t)w.Kp;
     auto kfn = gemv_i2s_kernel<MT>;
-    // Dynamic + static shared memory above 48 KB needs the opt-in attribute (raised once per size).
-    static int opted_in = 0;
-    if (smem + sizeof(int) * kGemvWarps * kGemvRows * MT > 48 * 1024 && (int)smem > opted_in) {
-        cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    // Dynamic + static shared memory above 48 KB needs the opt-in attribute.
+    if (smem + sizeof(int) * kGemvWarps * kGemvRows * MT > 48 * 1024) {
+        cudaError_t e = ensure_dynamic_smem(reinterpret_cast<const void*>(kfn), smem);
         if (e != cudaSuccess) return e;
-        opted_in = (int)smem;
     }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)ceil_div(w.N, kGemvRows), (unsigned)bt.count);
@@ -725,12 +948,13 @@ cudaError_t launch_gemv_i2s(const I2sWeight& w, const Q8Act& a, float* y, int64_
         float* yy = y + m0 * ldy;
         Epilogue ep = epi;  // the residual rows move with the token group
         if (ep.residual) ep.residual += m0 * ep.ld_res;
-        cudaError_t e;
-        if (mt == 1 && ceil_div(w.N, kGemvRows) * bt.count >= kStreamMinGroups && w.Kp <= 48 * 1024)
+        cudaError_t e = cudaSuccess;
+        const bool many = ceil_div(w.N, kGemvRows) * bt.count >= kStreamMinGroups;
+        if (mt == 1 && many && try_launch_tma1(w, q, s, sums, yy, ep, bt, st, &e)) {
+        } else if (mt == 1 && many && w.Kp <= 48 * 1024)
             e = launch_stream1(w, q, s, sums, yy, ep, bt, st);
         else if (mt == 1) e = launch_mt<1>(w, q, a.ldq, mt, s, sums, yy, ldy, ep, bt, st);
-        else if (ceil_div(w.N, kGemvRows) * bt.count >= kStreamMinGroups &&
-                 (size_t)mt * (size_t)(w.Kp + kMmaQPad) <= 200 * 1024)
+        else if (many && (size_t)mt * (size_t)(w.Kp + kMmaQPad) <= 200 * 1024)
             e = (mt <= 8) ? launch_mma_stream<1>(w, q, a.ldq, mt, s, sums, yy, ldy, ep, bt, st)
                           : launch_mma_stream<2>(w, q, a.ldq, mt, s, sums, yy, ldy, ep, bt, st);
         else if (mt <= 8) e = launch_mma<1>(w, q, a.ldq, mt, s, sums, yy, ldy, ep, bt, st);

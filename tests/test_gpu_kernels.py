@@ -344,11 +344,13 @@ def test_errors_before_launch(b2s):
 # ------------------------------------------------------------------------------------------ batched (ggml ne[2])
 @pytest.mark.parametrize("M", [1, 5, 16, 40])
 @pytest.mark.parametrize("K,N,B", [(2560, 2560, 3), (1152, 4304, 2), (256, 40, 5), (208, 64, 3),
-                                   (256, 2560, 15), (384, 2600, 16)])
+                                   (256, 2560, 15), (384, 2600, 16), (3008, 2600, 15)])
 def test_mul_mat_q8_batched(b2s, orc, M, K, N, B):
     """B independent problems in one call (one GEMV launch for M <= 16, a GEMM per matrix above): problem b
-    equals the oracle's mul_mat of matrix b alone, bit for bit. The last two shapes have enough row groups
-    (N/16 x B >= 2368) for the streaming GEMV kernels; 2600 rows leave a partial last row group."""
+    equals the oracle's mul_mat of matrix b alone, bit for bit. The last three shapes have enough row groups
+    (N/16 x B >= 2368) for the streaming GEMV kernels (TMA-fed for one token); 2600 rows leave a partial last
+    row group, and K = 3008
+    (row-padded to 3072) streams each row in two K chunks."""
     g = wl.rng(900 + M + K + N + B)
     ws = [wl.weight(g, N, K) for _ in range(B)]
     # One tensor: the B matrices' codes back to back, then the shared 32-byte scale trailer (all matrices
