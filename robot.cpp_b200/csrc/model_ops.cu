@@ -11,7 +11,9 @@
 //   * attention: one fused fp32 kernel per (query block, head, sequence) -- scores, online softmax, P V -- the
 //     ggml graph mul_mat(K, Q) -> soft_max_ext -> mul_mat(V, KQ) of
 //     src/models/smolvla/action_expert.cpp:771-774, with grouped K/V heads (GQA) as in
-//     src/models/pi0/vlm.cpp:223-235, in a fixed operation order the CPU oracle repeats bit for bit.
+//     src/models/pi0/vlm.cpp:223-235, in a fixed operation order the CPU oracle repeats bit for bit; head
+//     dims 128 and 72 use a 128-thread wide-tile form that prefetches the next key chunk, and all forms
+//     issue their fma chains as paired fp32 instructions (fma.rn.f32x2: two independent IEEE fmas).
 //   * patch embedding (fp32 tile GEMM reading the patches straight from the image, onto bias + position
 //     embedding) and a hash-seeded token-embedding gather for random-init vocabularies (the 128256 x 2560
 //     table is never materialized).
@@ -341,6 +343,17 @@ cudaError_t launch_embed_tokens(const int32_t* tokens, int n, int D, uint32_t se
 // chunk, the 64 x 64 probability tile and per-row factors; hd % 8 == 0, hd <= 128.
 constexpr int kAtQ = 64, kAtThreads = 256, kAtPP = kAtQ + 4;  // P row stride (floats)
 
+// d0 = fma(a0, b0, d0), d1 = fma(a1, b1, d1) as one paired fp32 instruction (each lane an IEEE fma, round to
+// nearest, no flush to zero: the same results as two __fmaf_rn).
+__device__ __forceinline__ void ffma2(float& d0, float& d1, float a0, float a1, float b0, float b1) {
+    uint64_t a, b, c;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(a) : "f"(a0), "f"(a1));
+    asm("mov.b64 %0, {%1, %2};" : "=l"(b) : "f"(b0), "f"(b1));
+    asm("mov.b64 %0, {%1, %2};" : "=l"(c) : "f"(d0), "f"(d1));
+    asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(c) : "l"(a), "l"(b));
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(d0), "=f"(d1) : "l"(c));
+}
+
 size_t attention_smem_bytes(int /*T*/, int hd) {
     return sizeof(float) * ((size_t)hd * kAtQ * 2 + (size_t)kAtQ * kAtPP + 2 * kAtQ);
 }
@@ -353,7 +366,7 @@ __device__ __forceinline__ void stage_transposed(float* __restrict__ dst, const 
                                                  int64_t ldsrc, int r0, int T, int hd,
                                                  const float2* __restrict__ rope) {
     const int half = hd / 2, h4 = half / 4;
-    for (int e = threadIdx.x; e < kAtQ * h4; e += kAtThreads) {
+    for (int e = threadIdx.x; e < kAtQ * h4; e += blockDim.x) {
         const int i = e % kAtQ, d4 = 4 * (e / kAtQ);
         float4 a = make_float4(0.f, 0.f, 0.f, 0.f), b = a;
         if (r0 + i < T) {
@@ -446,11 +459,12 @@ attention_kernel(const float* __restrict__ q, int64_t ldq, const float* __restri
         for (int d = 0; d < hd; ++d) {
             const float4 a = *reinterpret_cast<const float4*>(&Qt[d * kAtQ + 4 * ty]);
             const float4 b = *reinterpret_cast<const float4*>(&KV[d * kAtQ + 4 * tx]);
-            const float av[4] = {a.x, a.y, a.z, a.w}, bv[4] = {b.x, b.y, b.z, b.w};
+            const float bv[4] = {b.x, b.y, b.z, b.w};
 #pragma unroll
-            for (int i = 0; i < 4; ++i)
-#pragma unroll
-                for (int j = 0; j < 4; ++j) sc[i][j] = __fmaf_rn(av[i], bv[j], sc[i][j]);
+            for (int j = 0; j < 4; ++j) {  // row pairs: the Q load holds them side by side
+                ffma2(sc[0][j], sc[1][j], a.x, a.y, bv[j], bv[j]);
+                ffma2(sc[2][j], sc[3][j], a.z, a.w, bv[j], bv[j]);
+            }
         }
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
@@ -507,12 +521,13 @@ attention_kernel(const float* __restrict__ q, int64_t ldq, const float* __restri
                     if (j4 + kk < jn) {
                         const float4 v0 = *reinterpret_cast<const float4*>(&KV[(j4 + kk) * hd + 8 * cg]);
                         const float4 v1 = *reinterpret_cast<const float4*>(&KV[(j4 + kk) * hd + 8 * cg + 4]);
-                        const float vv[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
 #pragma unroll
                         for (int i = 0; i < 4; ++i) {
                             const float pr = (kk == 0) ? p4[i].x : (kk == 1) ? p4[i].y : (kk == 2) ? p4[i].z : p4[i].w;
-#pragma unroll
-                            for (int j = 0; j < 8; ++j) acc[i][j] = __fmaf_rn(pr, vv[j], acc[i][j]);
+                            ffma2(acc[i][0], acc[i][1], pr, pr, v0.x, v0.y);
+                            ffma2(acc[i][2], acc[i][3], pr, pr, v0.z, v0.w);
+                            ffma2(acc[i][4], acc[i][5], pr, pr, v1.x, v1.y);
+                            ffma2(acc[i][6], acc[i][7], pr, pr, v1.z, v1.w);
                         }
                     }
                 }
@@ -539,6 +554,248 @@ attention_kernel(const float* __restrict__ q, int64_t ldq, const float* __restri
     }
 }
 
+// Wider-tile, prefetching form of attention_kernel for head dims 128 and 72 (the BitVLA decoder and ViT): 128
+// threads per (64-query block, head, sequence). Every score and output goes through the same fp32 operation
+// sequence as in attention_kernel -- ascending-d fma chains, the same 64-key chunks, a row's 64 keys spread
+// over 16 consecutive lanes (4 each) with the same max / sum butterflies, ascending-key P.V chains -- so the
+// two kernels agree bit for bit. Each thread holds 8 rows x 4 keys of the score tile and 8 rows x 8 columns
+// (HD 128) or 4 rows x 9 columns (HD 72) of the output, so each shared-memory load feeds more FMAs; output
+// rows are interleaved (rg + 64/OR * i) so the row groups of a warp read different banks of P. Chunk c + 1
+// is fetched while chunk c computes: its K rows into registers during the P.V phase (stored transposed,
+// RoPE applied, after it), its V rows by cp.async into their own buffer during the next score phase.
+// P is a 64 x 64 tile with its 16-byte chunks XOR-swizzled by row (conflict-free row-wise stores and reads).
+__device__ __forceinline__ void att_cp_async_16(void* smem_dst, const void* src, uint32_t src_bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(smem_dst)), "l"(src), "r"(src_bytes)
+                 : "memory");
+}
+
+template <int HD>
+__global__ void __launch_bounds__(128, HD == 128 ? 2 : 3)
+attention_wide_kernel(const float* __restrict__ q, int64_t ldq, const float* __restrict__ k, int64_t ldk,
+                      const float* __restrict__ v, int64_t ldv, float* __restrict__ o, int64_t ldo, int T, int heads,
+                      int kv_heads, float scale, int causal, const float2* __restrict__ rope) {
+    constexpr int OR = HD == 128 ? 8 : 4, OC = HD == 128 ? 8 : 9;  // output rows / columns per thread
+    constexpr int NCG = HD / OC;                                   // column groups (16 or 8)
+    constexpr int RS = kAtQ / OR;                                  // row stride between a thread's rows
+    constexpr int HALF = HD / 2, H4 = HALF / 4;
+    constexpr int KITEMS = (kAtQ * H4 + 127) / 128;                // K (row, 4-pair) items per thread
+    static_assert(NCG * OC == HD && RS * NCG == 128, "output tiling covers 64 x HD with 128 threads");
+    extern __shared__ __align__(16) float at_sm[];
+    float* Qt = at_sm;                    // [HD][64]
+    float* Kt = Qt + HD * kAtQ;           // K^T chunk [HD][64]
+    float* Vc = Kt + HD * kAtQ;           // V chunk [64][HD]
+    float* P = Vc + HD * kAtQ;            // [64][64], chunk q of row r at (q ^ (r & 15))
+    float* alpha_sm = P + kAtQ * kAtQ;    // [64] per-row rescale of the chunk
+    float* inv_sm = alpha_sm + kAtQ;      // [64] 1 / l at the end
+    const int h = blockIdx.x, g = h / (heads / kv_heads);
+    const int q0 = (int)(gridDim.z - 1u - blockIdx.z) * kAtQ;  // heaviest (causal) blocks first
+    const int64_t row0 = (int64_t)blockIdx.y * T;
+    const float* qh = q + row0 * ldq + (int64_t)h * HD;
+    const float* kh = k + row0 * ldk + (int64_t)g * HD;
+    const float* vh = v + row0 * ldv + (int64_t)g * HD;
+    const int t = threadIdx.x;
+    griddep_wait();  // q/k/v are written by the preceding kernel
+    griddep_launch();
+
+    const int kend = causal ? min(T, q0 + kAtQ) : T;
+    const int nchunks = (kend + kAtQ - 1) / kAtQ;
+    float4 kpa[KITEMS], kpb[KITEMS];  // K rows of the next chunk: pairs (d4.., HALF + d4..)
+    auto load_k = [&](int k0) {
+#pragma unroll
+        for (int it = 0; it < KITEMS; ++it) {
+            const int e = t + 128 * it, i = e % kAtQ, d4 = 4 * (e / kAtQ);
+            kpa[it] = kpb[it] = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (e < kAtQ * H4 && k0 + i < T) {
+                const float* row = kh + (int64_t)(k0 + i) * ldk;
+                kpa[it] = *reinterpret_cast<const float4*>(row + d4);
+                kpb[it] = *reinterpret_cast<const float4*>(row + HALF + d4);
+            }
+        }
+    };
+    auto store_k = [&](int k0) {
+#pragma unroll
+        for (int it = 0; it < KITEMS; ++it) {
+            const int e = t + 128 * it, i = e % kAtQ, d4 = 4 * (e / kAtQ);
+            if (e >= kAtQ * H4) continue;
+            float4 a = kpa[it], b = kpb[it];
+            if (rope && k0 + i < T) {
+                const float4* cs = reinterpret_cast<const float4*>(rope + (int64_t)(k0 + i) * HALF + d4);
+                const float4 c01 = cs[0], c23 = cs[1];
+                const float x0[4] = {a.x, a.y, a.z, a.w}, x1[4] = {b.x, b.y, b.z, b.w};
+                const float cv[4] = {c01.x, c01.z, c23.x, c23.z}, sv[4] = {c01.y, c01.w, c23.y, c23.w};
+                float y0[4], y1[4];
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    y0[c] = __fsub_rn(__fmul_rn(x0[c], cv[c]), __fmul_rn(x1[c], sv[c]));
+                    y1[c] = __fadd_rn(__fmul_rn(x0[c], sv[c]), __fmul_rn(x1[c], cv[c]));
+                }
+                a = make_float4(y0[0], y0[1], y0[2], y0[3]);
+                b = make_float4(y1[0], y1[1], y1[2], y1[3]);
+            }
+            Kt[(d4 + 0) * kAtQ + i] = a.x;
+            Kt[(d4 + 1) * kAtQ + i] = a.y;
+            Kt[(d4 + 2) * kAtQ + i] = a.z;
+            Kt[(d4 + 3) * kAtQ + i] = a.w;
+            Kt[(HALF + d4 + 0) * kAtQ + i] = b.x;
+            Kt[(HALF + d4 + 1) * kAtQ + i] = b.y;
+            Kt[(HALF + d4 + 2) * kAtQ + i] = b.z;
+            Kt[(HALF + d4 + 3) * kAtQ + i] = b.w;
+        }
+    };
+    auto issue_v = [&](int k0) {
+        for (int e = t; e < kAtQ * (HD / 4); e += 128) {
+            const int j = e / (HD / 4), d4 = 4 * (e % (HD / 4));
+            const bool in = k0 + j < T;
+            att_cp_async_16(&Vc[j * HD + d4], in ? (const void*)(vh + (int64_t)(k0 + j) * ldv + d4) : (const void*)vh,
+                            in ? 16u : 0u);
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+
+    stage_transposed(Qt, qh, ldq, q0, T, HD, rope);
+    load_k(0);
+    store_k(0);
+    issue_v(0);
+    __syncthreads();  // Qt and K^T of chunk 0 written
+
+    const int ty = t / 16, tx = t % 16;  // score rows 8 ty .. 8 ty + 7, keys 4 tx .. 4 tx + 3
+    float m_r[8], l_r[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        m_r[i] = -INFINITY;
+        l_r[i] = 0.0f;
+    }
+    const int rg = t / NCG, cg = t % NCG;  // output rows rg + RS i, columns OC cg ..
+    float acc[OR][OC];
+#pragma unroll
+    for (int i = 0; i < OR; ++i)
+#pragma unroll
+        for (int j = 0; j < OC; ++j) acc[i][j] = 0.0f;
+
+    for (int c = 0; c < nchunks; ++c) {
+        const int k0 = c * kAtQ;
+        float sc[8][4];
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) sc[i][j] = 0.0f;
+#pragma unroll 4
+        for (int d = 0; d < HD; ++d) {
+            const float4 a0 = *reinterpret_cast<const float4*>(&Qt[d * kAtQ + 8 * ty]);
+            const float4 a1 = *reinterpret_cast<const float4*>(&Qt[d * kAtQ + 8 * ty + 4]);
+            const float4 b = *reinterpret_cast<const float4*>(&Kt[d * kAtQ + 4 * tx]);
+            const float bv[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {  // row pairs: the Q loads hold them side by side
+                ffma2(sc[0][j], sc[1][j], a0.x, a0.y, bv[j], bv[j]);
+                ffma2(sc[2][j], sc[3][j], a0.z, a0.w, bv[j], bv[j]);
+                ffma2(sc[4][j], sc[5][j], a1.x, a1.y, bv[j], bv[j]);
+                ffma2(sc[6][j], sc[7][j], a1.z, a1.w, bv[j], bv[j]);
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const int row = 8 * ty + i, qi = q0 + row;
+            const int nk = (qi < T) ? (causal ? qi + 1 : T) : 0;
+            float cm = -INFINITY;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int key = k0 + 4 * tx + j;
+                sc[i][j] = (key < nk) ? __fmul_rn(sc[i][j], scale) : -INFINITY;
+                cm = fmaxf(cm, sc[i][j]);
+            }
+#pragma unroll
+            for (int off = 8; off > 0; off >>= 1) cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, off));
+            const float mn = fmaxf(m_r[i], cm);
+            const float alpha = det_expf(__fsub_rn(m_r[i], mn));
+            float4 pv;
+            pv.x = det_expf(__fsub_rn(sc[i][0], mn));
+            pv.y = det_expf(__fsub_rn(sc[i][1], mn));
+            pv.z = det_expf(__fsub_rn(sc[i][2], mn));
+            pv.w = det_expf(__fsub_rn(sc[i][3], mn));
+            float part = __fadd_rn(__fadd_rn(__fadd_rn(pv.x, pv.y), pv.z), pv.w);
+#pragma unroll
+            for (int off = 8; off > 0; off >>= 1) part = __fadd_rn(part, __shfl_xor_sync(0xffffffffu, part, off));
+            l_r[i] = __fadd_rn(__fmul_rn(l_r[i], alpha), part);
+            m_r[i] = mn;
+            *reinterpret_cast<float4*>(&P[row * kAtQ + 4 * (tx ^ (row & 15))]) = pv;
+            if (tx == 0) alpha_sm[row] = alpha;
+        }
+        const bool more = c + 1 < nchunks;
+        if (more) load_k(k0 + kAtQ);  // in flight during P.V
+        asm volatile("cp.async.wait_all;" ::: "memory");
+        __syncthreads();  // V of this chunk landed, P and alpha written, K^T consumed
+#pragma unroll
+        for (int i = 0; i < OR; ++i) {
+            const float al = alpha_sm[rg + RS * i];
+#pragma unroll
+            for (int j = 0; j < OC; ++j) acc[i][j] = __fmul_rn(acc[i][j], al);
+        }
+        const int jn = min(kAtQ, kend - k0);
+        for (int j4 = 0; j4 < jn; j4 += 4) {
+            float4 p4[OR];
+#pragma unroll
+            for (int i = 0; i < OR; ++i) {
+                const int row = rg + RS * i;
+                p4[i] = *reinterpret_cast<const float4*>(&P[row * kAtQ + 4 * ((j4 >> 2) ^ (row & 15))]);
+            }
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+                if (j4 + kk < jn) {
+                    float vv[OC];
+                    const float* vr = &Vc[(j4 + kk) * HD + OC * cg];
+                    if constexpr (OC == 8) {
+                        const float4 v0 = *reinterpret_cast<const float4*>(vr);
+                        const float4 v1 = *reinterpret_cast<const float4*>(vr + 4);
+                        vv[0] = v0.x; vv[1] = v0.y; vv[2] = v0.z; vv[3] = v0.w;
+                        vv[4] = v1.x; vv[5] = v1.y; vv[6] = v1.z; vv[7] = v1.w;
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < OC; ++j) vv[j] = vr[j];
+                    }
+#pragma unroll
+                    for (int i = 0; i < OR; ++i) {
+                        const float pr = (kk == 0) ? p4[i].x : (kk == 1) ? p4[i].y : (kk == 2) ? p4[i].z : p4[i].w;
+#pragma unroll
+                        for (int j = 0; j + 1 < OC; j += 2) ffma2(acc[i][j], acc[i][j + 1], pr, pr, vv[j], vv[j + 1]);
+                        if constexpr (OC % 2) acc[i][OC - 1] = __fmaf_rn(pr, vv[OC - 1], acc[i][OC - 1]);
+                    }
+                }
+            }
+        }
+        if (more) {
+            __syncthreads();  // V and P of this chunk consumed
+            store_k(k0 + kAtQ);
+            issue_v(k0 + kAtQ);  // lands during the next score phase
+            __syncthreads();     // K^T of the next chunk written
+        }
+    }
+    if (tx == 0) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) inv_sm[8 * ty + i] = (l_r[i] > 0.0f) ? __fdiv_rn(1.0f, l_r[i]) : 0.0f;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < OR; ++i) {
+        const int row = rg + RS * i, qi = q0 + row;
+        if (qi >= T) continue;
+        const float inv = inv_sm[row];
+        float* orow = o + (row0 + qi) * ldo + (int64_t)h * HD + OC * cg;
+        if constexpr (OC == 8) {
+            *reinterpret_cast<float4*>(orow) = make_float4(__fmul_rn(acc[i][0], inv), __fmul_rn(acc[i][1], inv),
+                                                           __fmul_rn(acc[i][2], inv), __fmul_rn(acc[i][3], inv));
+            *reinterpret_cast<float4*>(orow + 4) = make_float4(__fmul_rn(acc[i][4], inv), __fmul_rn(acc[i][5], inv),
+                                                               __fmul_rn(acc[i][6], inv), __fmul_rn(acc[i][7], inv));
+        } else {
+#pragma unroll
+            for (int j = 0; j < OC; ++j) orow[j] = __fmul_rn(acc[i][j], inv);
+        }
+    }
+}
+
+// Shared memory of attention_wide_kernel<HD>.
+static size_t attention_wide_smem(int hd) { return sizeof(float) * ((size_t)3 * hd * kAtQ + (size_t)kAtQ * kAtQ + 2 * kAtQ); }
+
 bool attention_supported(int T, int hd, int64_t ldq, int64_t ldk, int64_t ldv, int64_t ldo, const void* q,
                          const void* k, const void* v, const void* o) {
     auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
@@ -550,14 +807,18 @@ cudaError_t launch_attention(const float* q, int64_t ldq, const float* k, int64_
                              int batch, int T, int heads, int kv_heads, int hd, float scale, bool causal, float* o,
                              int64_t ldo, cudaStream_t st, const float2* rope) {
     if (batch <= 0 || T <= 0) return cudaSuccess;
-    const size_t smem = attention_smem_bytes(T, hd);
+    const size_t smem = (hd == 128 || hd == 72) ? attention_wide_smem(hd) : attention_smem_bytes(T, hd);
+    // head dims 128 and 72 take the wider-tile kernel (same results bit for bit)
+    const void* kfn = hd == 128 ? reinterpret_cast<const void*>(attention_wide_kernel<128>)
+                    : hd == 72  ? reinterpret_cast<const void*>(attention_wide_kernel<72>)
+                                : reinterpret_cast<const void*>(attention_kernel);
     if (smem > 48 * 1024) {
-        cudaError_t e = ensure_dynamic_smem(reinterpret_cast<const void*>(attention_kernel), smem);
+        cudaError_t e = ensure_dynamic_smem(kfn, smem);
         if (e != cudaSuccess) return e;
     }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)heads, (unsigned)batch, (unsigned)ceil_div(T, kAtQ));
-    cfg.blockDim = dim3(kAtThreads);
+    cfg.blockDim = dim3(hd == 128 || hd == 72 ? 128 : kAtThreads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
@@ -565,6 +826,12 @@ cudaError_t launch_attention(const float* q, int64_t ldq, const float* k, int64_
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
+    if (hd == 128)
+        return cudaLaunchKernelEx(&cfg, attention_wide_kernel<128>, q, ldq, k, ldk, v, ldv, o, ldo, T, heads, kv_heads,
+                                  scale, causal ? 1 : 0, rope);
+    if (hd == 72)
+        return cudaLaunchKernelEx(&cfg, attention_wide_kernel<72>, q, ldq, k, ldk, v, ldv, o, ldo, T, heads, kv_heads,
+                                  scale, causal ? 1 : 0, rope);
     return cudaLaunchKernelEx(&cfg, attention_kernel, q, ldq, k, ldk, v, ldv, o, ldo, T, heads, kv_heads, hd, scale,
                               causal ? 1 : 0, rope);
 }
