@@ -46,16 +46,6 @@ struct alignas(8) Bars {
 constexpr size_t kSmemBytes = 1024 + (size_t)kStages * (kActStageBytes + kWStageBytes) + sizeof(Bars);
 }  // namespace tcp
 
-__device__ __forceinline__ void tmem_ld_x16(uint32_t taddr, uint32_t (&r)[16]) {
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
-        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-        : "r"(taddr)
-        : "memory");
-}
-
 // Instruction descriptor, kind::i8: D s32, A unsigned 8-bit (codes), B signed 8-bit, K-major, 128 x N.
 __host__ __device__ constexpr uint32_t idesc_u8s8(int M, int N) {
     return (2u << 4) | (0u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
