@@ -152,8 +152,11 @@ def _main(argv=None) -> None:
     p.add_argument("--iters", type=int, default=10)
     p.add_argument("--seed", type=int, default=1234)
     p.add_argument("--profile-range", action="store_true")
+    p.add_argument("--attention-tc", action="store_true",
+                   help="tensor-core attention (opt-in; not bit-identical to the fixed-order fp32 kernel)")
     a = p.parse_args(argv)
     cfg = default_config()
+    cfg.attention_tc = 1 if a.attention_tc else 0
     m = Model(cfg, a.seed, max_batch=a.batch)
     img = torch.rand((a.batch, 3, cfg.image_size, cfg.image_size), device="cuda")
     tok = torch.randint(0, cfg.vocab, (a.batch, cfg.n_text), dtype=torch.int32, device="cuda")
