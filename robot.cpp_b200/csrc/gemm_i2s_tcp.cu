@@ -1,19 +1,21 @@
 // gemm_i2s_tcp.cu -- persistent i2_s x int8 GEMM on the sm_100a tensor cores (tcgen05 kind::i8), for
 // outputs with at least one tile per SM.
 //
-// One CTA per SM walks the output tiles (128 weight rows x T tokens, T <= 224; in the gate/up mode 64 gate
+// One CTA per SM walks the output tiles (128 weight rows x T tokens, T <= 192; in the gate/up mode 64 gate
 // and 64 up rows) in the order blockIdx.x, blockIdx.x + gridDim.x, ... Per 128-wide K step:
 //   * warp 4 (producer) TMA-loads the packed weight tile (128 rows x 32 bytes, local HBM, no multicast)
-//     and the int8 activation tile (T rows x 128 bytes, 128B swizzle) into a 6-stage shared-memory ring;
+//     and the int8 activation tile (T rows x 128 bytes, 128B swizzle) into a 7-stage shared-memory ring;
 //   * warps 0-3 (converters, one per TMEM lane quadrant) turn each row's 32 packed bytes into 128 unsigned
-//     2-bit codes {0,1,2} and store them with tcgen05.st into a 2-stage TMEM ring (the MMA's A operand);
+//     2-bit codes {0,1,2} and store them with tcgen05.st into a 4-stage TMEM ring (the MMA's A operand:
+//     with two stages a converter waited for the MMAs of the step before last, and that round trip --
+//     MMA issue, completion, commit, the converter's own wait -- paced the K loop);
 //   * warp 5 (MMA) issues four tcgen05.mma.kind::i8 (M=128, N=T, K=32): A = codes from TMEM, B = signed
 //     int8 activations from shared memory, int32 accumulators in one of two TMEM buffers;
 //   * warps 6-13 (epilogue, two per quadrant) read the finished buffer (tcgen05.ld) and write
 //     y = (float)(acc - sum_q[m]) * (w_scale / s[m]) (+ bias, GELU, + residual), while the MMAs of the
 //     next tile already fill the other buffer. The output writes of one tile therefore overlap the
 //     main loop of the next instead of stalling every SM at the end of a wave.
-// TMEM: columns [0,64) A ring, [64,288) and [288,512) accumulators. Every mbarrier wait is bounded (about
+// TMEM: columns [0,128) A ring, [128,320) and [320,512) accumulators. Every mbarrier wait is bounded (about
 // one second); on a timeout the kernel records the error in g_device_error, stops issuing, drains what it
 // issued (bounded), frees its TMEM and returns. The int32 accumulation is exact and the fp32 epilogue is
 // the same operation sequence as gemm_i2s_tc.cu, so both kernels give bit-identical outputs.
@@ -23,14 +25,15 @@
 namespace b2s {
 
 namespace tcp {
-constexpr int kStages = 6;
-constexpr int kAStages = 2;
-constexpr int kMaxT = 224;
-constexpr int kActStageBytes = kMaxT * 128;  // 28 KB, a multiple of 1024 (SW128 atoms)
+constexpr int kStages = 7;
+constexpr int kAStages = 4;
+constexpr int kMaxT = 192;
+constexpr int kActStageBytes = kMaxT * 128;  // 24 KB, a multiple of 1024 (SW128 atoms)
 constexpr int kWStageBytes = 128 * 32;
 constexpr int kThreads = 448;  // warps 0-3 converters, 4 TMA producer, 5 MMA, 6-13 epilogue
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kAccCol0 = kAStages * 32;  // accumulator buffer b at kAccCol0 + b * kMaxT
+static_assert(kAccCol0 + 2 * kMaxT <= kTmemCols, "TMEM budget");
 
 struct alignas(8) Bars {
     uint64_t full[kStages];     // TMA bytes of smem stage landed
@@ -302,15 +305,17 @@ gemm_i2s_tcp_kernel(const __grid_constant__ CUtensorMap tmap_w0, const __grid_co
                 const int ch = 4 * pp + 2 * grp;
                 if (ch >= nchunk) break;
                 const bool hb = ch + 1 < nchunk;
-                float ra[16], rb[16];  // residual loads in flight while the accumulators are read
-                load_res(ch, ra);
-                load_res(ch + 1, rb);
+                float res[16];  // residual rows in flight while the accumulators are read (one chunk at a time)
+                load_res(ch, res);
                 uint32_t xa[16], xb[16];
                 tmem_ld_x16(acc + (uint32_t)(16 * ch), xa);
                 if (hb) tmem_ld_x16(acc + (uint32_t)(16 * ch + 16), xb);
                 tc_wait_ld();
-                finish(ch, xa, rf[2 * pp], sm[2 * pp], ra);
-                if (hb) finish(ch + 1, xb, rf[2 * pp + 1], sm[2 * pp + 1], rb);
+                finish(ch, xa, rf[2 * pp], sm[2 * pp], res);
+                if (hb) {
+                    load_res(ch + 1, res);
+                    finish(ch + 1, xb, rf[2 * pp + 1], sm[2 * pp + 1], res);
+                }
             }
             tc_fence_before();
             __syncwarp();
