@@ -570,7 +570,7 @@ __device__ __forceinline__ void att_cp_async_16(void* smem_dst, const void* src,
 }
 
 template <int HD>
-__global__ void __launch_bounds__(128, HD == 128 ? 2 : 3)
+__global__ void __launch_bounds__(128, HD == 128 ? 2 : 4)
 attention_wide_kernel(const float* __restrict__ q, int64_t ldq, const float* __restrict__ k, int64_t ldk,
                       const float* __restrict__ v, int64_t ldv, float* __restrict__ o, int64_t ldo, int T, int heads,
                       int kv_heads, float scale, int causal, const float2* __restrict__ rope) {
@@ -583,7 +583,10 @@ attention_wide_kernel(const float* __restrict__ q, int64_t ldq, const float* __r
     extern __shared__ __align__(16) float at_sm[];
     float* Qt = at_sm;                    // [HD][64]
     float* Kt = Qt + HD * kAtQ;           // K^T chunk [HD][64]
-    float* Vc = Kt + HD * kAtQ;           // V chunk [64][HD]
+    // Lean form (head dim 72): V shares K^T's buffer and chunks are staged synchronously, so four CTAs fit on
+    // an SM and the ViT's 512-CTA grid runs as one wave (three per SM left a 68-CTA second wave).
+    constexpr bool kLean = HD == 72;
+    float* Vc = kLean ? Kt : Kt + HD * kAtQ;  // V chunk [64][HD]
     float* P = Vc + HD * kAtQ;            // [64][64], chunk q of row r at (q ^ (r & 15))
     float* alpha_sm = P + kAtQ * kAtQ;    // [64] per-row rescale of the chunk
     float* inv_sm = alpha_sm + kAtQ;      // [64] 1 / l at the end
@@ -655,7 +658,7 @@ attention_wide_kernel(const float* __restrict__ q, int64_t ldq, const float* __r
     stage_transposed(Qt, qh, ldq, q0, T, HD, rope);
     load_k(0);
     store_k(0);
-    issue_v(0);
+    if (!kLean) issue_v(0);
     __syncthreads();  // Qt and K^T of chunk 0 written
 
     const int ty = t / 16, tx = t % 16;  // score rows 8 ty .. 8 ty + 7, keys 4 tx .. 4 tx + 3
@@ -722,7 +725,12 @@ attention_wide_kernel(const float* __restrict__ q, int64_t ldq, const float* __r
             if (tx == 0) alpha_sm[row] = alpha;
         }
         const bool more = c + 1 < nchunks;
-        if (more) load_k(k0 + kAtQ);  // in flight during P.V
+        if (kLean) {
+            __syncthreads();  // K^T consumed: its buffer takes this chunk's V
+            issue_v(k0);
+        } else if (more) {
+            load_k(k0 + kAtQ);  // in flight during P.V
+        }
         asm volatile("cp.async.wait_all;" ::: "memory");
         __syncthreads();  // V of this chunk landed, P and alpha written, K^T consumed
 #pragma unroll
@@ -765,9 +773,10 @@ attention_wide_kernel(const float* __restrict__ q, int64_t ldq, const float* __r
         }
         if (more) {
             __syncthreads();  // V and P of this chunk consumed
+            if (kLean) load_k(k0 + kAtQ);
             store_k(k0 + kAtQ);
-            issue_v(k0 + kAtQ);  // lands during the next score phase
-            __syncthreads();     // K^T of the next chunk written
+            if (!kLean) issue_v(k0 + kAtQ);  // lands during the next score phase
+            __syncthreads();                 // K^T of the next chunk written
         }
     }
     if (tx == 0) {
@@ -794,7 +803,9 @@ attention_wide_kernel(const float* __restrict__ q, int64_t ldq, const float* __r
 }
 
 // Shared memory of attention_wide_kernel<HD>.
-static size_t attention_wide_smem(int hd) { return sizeof(float) * ((size_t)3 * hd * kAtQ + (size_t)kAtQ * kAtQ + 2 * kAtQ); }
+static size_t attention_wide_smem(int hd) {
+    return sizeof(float) * ((size_t)(hd == 72 ? 2 : 3) * hd * kAtQ + (size_t)kAtQ * kAtQ + 2 * kAtQ);
+}
 
 bool attention_supported(int T, int hd, int64_t ldq, int64_t ldk, int64_t ldv, int64_t ldo, const void* q,
                          const void* k, const void* v, const void* o) {
