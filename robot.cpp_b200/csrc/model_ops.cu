@@ -362,19 +362,24 @@ size_t attention_smem_bytes(int /*T*/, int hd) {
 // a rotation table (rows are positions 0 .. T-1 of their sequence) each (d, d + hd/2) pair is rotated on the
 // way in, by the same fp32 operations as rope_rotate, so Q and K arrive exactly as a separate NEOX RoPE pass
 // would have left them.
+// With src2 the tile holds two half-tiles: columns 0-31 rows r0 .. r0 + 31 of src, columns 32-63 the same
+// rows of src2 (another head of the same sequence).
 __device__ __forceinline__ void stage_transposed(float* __restrict__ dst, const float* __restrict__ src,
                                                  int64_t ldsrc, int r0, int T, int hd,
-                                                 const float2* __restrict__ rope) {
+                                                 const float2* __restrict__ rope,
+                                                 const float* __restrict__ src2 = nullptr) {
     const int half = hd / 2, h4 = half / 4;
     for (int e = threadIdx.x; e < kAtQ * h4; e += blockDim.x) {
         const int i = e % kAtQ, d4 = 4 * (e / kAtQ);
+        const int r = r0 + (src2 ? (i & 31) : i);  // position in the sequence
+        const float* base = (src2 && i >= 32) ? src2 : src;
         float4 a = make_float4(0.f, 0.f, 0.f, 0.f), b = a;
-        if (r0 + i < T) {
-            const float* row = src + (int64_t)(r0 + i) * ldsrc;
+        if (r < T) {
+            const float* row = base + (int64_t)r * ldsrc;
             a = *reinterpret_cast<const float4*>(row + d4);
             b = *reinterpret_cast<const float4*>(row + half + d4);
             if (rope) {
-                const float4* cs = reinterpret_cast<const float4*>(rope + (int64_t)(r0 + i) * half + d4);
+                const float4* cs = reinterpret_cast<const float4*>(rope + (int64_t)r * half + d4);
                 const float4 c01 = cs[0], c23 = cs[1];  // (cos, sin) of pairs d4 .. d4 + 3
                 const float x0[4] = {a.x, a.y, a.z, a.w}, x1[4] = {b.x, b.y, b.z, b.w};
                 const float cv[4] = {c01.x, c01.z, c23.x, c23.z}, sv[4] = {c01.y, c01.w, c23.y, c23.w};
@@ -591,12 +596,20 @@ attention_wide_kernel(const float* __restrict__ q, int64_t ldq, const float* __r
     float* alpha_sm = P + kAtQ * kAtQ;    // [64] per-row rescale of the chunk
     float* inv_sm = alpha_sm + kAtQ;      // [64] 1 / l at the end
     const int h = blockIdx.x, g = h / (heads / kv_heads);
-    const int q0 = (int)(gridDim.z - 1u - blockIdx.z) * kAtQ;  // heaviest (causal) blocks first
+    const int zi = (int)(gridDim.z - 1u - blockIdx.z);  // heaviest (causal) blocks first
+    const int q0 = zi * kAtQ;
+    // Paired tail: when the last query block holds at most 32 rows and heads come in pairs within a K/V
+    // group, the CTA of even head h takes the tail rows of heads h and h + 1 (tile rows 0-31 and 32-63;
+    // same keys, same values) and the CTA of h + 1 has nothing to do. Every row goes through the same
+    // operations as in an unpaired tile.
+    const bool pair = zi == (int)gridDim.z - 1 && T - q0 <= 32 && (heads / kv_heads) % 2 == 0;
+    if (pair && (h & 1)) return;
     const int64_t row0 = (int64_t)blockIdx.y * T;
     const float* qh = q + row0 * ldq + (int64_t)h * HD;
     const float* kh = k + row0 * ldk + (int64_t)g * HD;
     const float* vh = v + row0 * ldv + (int64_t)g * HD;
     const int t = threadIdx.x;
+    auto qpos = [&](int row) { return q0 + (pair ? (row & 31) : row); };  // position of a tile row
     griddep_wait();  // q/k/v are written by the preceding kernel
     griddep_launch();
 
@@ -655,7 +668,7 @@ attention_wide_kernel(const float* __restrict__ q, int64_t ldq, const float* __r
         asm volatile("cp.async.commit_group;" ::: "memory");
     };
 
-    stage_transposed(Qt, qh, ldq, q0, T, HD, rope);
+    stage_transposed(Qt, qh, ldq, q0, T, HD, rope, pair ? qh + HD : nullptr);
     load_k(0);
     store_k(0);
     if (!kLean) issue_v(0);
@@ -698,7 +711,7 @@ attention_wide_kernel(const float* __restrict__ q, int64_t ldq, const float* __r
         }
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-            const int row = 8 * ty + i, qi = q0 + row;
+            const int row = 8 * ty + i, qi = qpos(row);
             const int nk = (qi < T) ? (causal ? qi + 1 : T) : 0;
             float cm = -INFINITY;
 #pragma unroll
@@ -786,10 +799,11 @@ attention_wide_kernel(const float* __restrict__ q, int64_t ldq, const float* __r
     __syncthreads();
 #pragma unroll
     for (int i = 0; i < OR; ++i) {
-        const int row = rg + RS * i, qi = q0 + row;
+        const int row = rg + RS * i, qi = qpos(row);
         if (qi >= T) continue;
         const float inv = inv_sm[row];
-        float* orow = o + (row0 + qi) * ldo + (int64_t)h * HD + OC * cg;
+        const int ho = h + ((pair && row >= 32) ? 1 : 0);
+        float* orow = o + (row0 + qi) * ldo + (int64_t)ho * HD + OC * cg;
         if constexpr (OC == 8) {
             *reinterpret_cast<float4*>(orow) = make_float4(__fmul_rn(acc[i][0], inv), __fmul_rn(acc[i][1], inv),
                                                            __fmul_rn(acc[i][2], inv), __fmul_rn(acc[i][3], inv));

@@ -85,10 +85,13 @@ def test_rope_neox_bit_exact(b2s, orc, M, heads, hd, pos0):
 
 @pytest.mark.parametrize("M,heads,kv,hd,causal", [(256, 16, 16, 72, False), (288, 20, 5, 128, True),
                                                   (200, 8, 2, 128, False), (130, 4, 4, 128, True),
-                                                  (77, 6, 3, 72, True), (33, 4, 2, 64, True), (1, 2, 1, 8, True)])
+                                                  (77, 6, 3, 72, True), (100, 4, 2, 128, True),
+                                                  (33, 4, 2, 64, True), (1, 2, 1, 8, True)])
 def test_attention(b2s, orc, M, heads, kv, hd, causal):
     """Head dims 128 and 72 run the wide-tile kernel, others the 256-thread one; both repeat the oracle's
-    operation order, so the result is bit-exact. Ragged sizes leave partial query blocks and key chunks."""
+    operation order, so the result is bit-exact. Ragged sizes leave partial query blocks and key chunks; a
+    last block of at most 32 rows with an even number of query heads per K/V head is computed for two heads
+    in one tile (288, 200 and 77 tokens), a 36-row one is not (100 tokens)."""
     g = wl.rng(M + heads + hd)
     H, KV = heads * hd, kv * hd
     qkv = wl.activations(g, M, H + 2 * KV)
