@@ -305,10 +305,12 @@ def events():
 # ------------------------------------------------------------------------------------------- headline: server
 def kernels_per_forward(cfg) -> int:
     """Library kernels in one captured forward: patch embedding; 9 per ViT layer (norm+quant, qkv,
-    attention, quant, o, norm+quant, fc1, quant, fc2); connector 4; text embedding; 10 per decoder layer
-    (norm+quant, qkv, RoPE, attention, norm+quant, o, norm+quant, gate/up, norm+quant, down); final norm;
-    action head."""
-    return 1 + 9 * cfg.vit_layers + 4 + (1 if cfg.n_text > 0 else 0) + 10 * cfg.dec_layers + 2
+    attention, quant, o, norm+quant, fc1, quant, fc2); connector 4; text embedding; 9 per decoder layer
+    (norm+quant, qkv, attention with RoPE applied to q/k as they are staged, norm+quant, o, norm+quant,
+    gate/up, norm+quant, down; the tensor-core attention mode adds a separate RoPE pass); final norm;
+    action head. 521 for the BitVLA shape, as the ncu launch list of one forward shows."""
+    dec = 9 + (1 if getattr(cfg, "attention_tc", 0) else 0)
+    return 1 + 9 * cfg.vit_layers + 4 + (1 if cfg.n_text > 0 else 0) + dec * cfg.dec_layers + 2
 
 
 def run_server(a, D, local):
