@@ -236,48 +236,58 @@ static unsigned grid_for(int64_t total) {
 // Patch embedding of stacked CHW images ([batch][C][H][W]; patch rows of image b follow those of b - 1):
 // Y[r][d] = (bias[d] + pos[r % np][d]) + acc, acc = fma(A[r][k], W[d][k], acc) over k = 0..C*P*P-1 in
 // order from +0, with A the non-overlapping patch rows (k = c P^2 + ky P + kx) read straight from the
-// image. A 64 x 64 output tile per CTA, 4 x 4 per thread, k staged 32 at a time.
-constexpr int kPeTile = 64, kPeK = 32;
+// image. A 64 x 64 output tile per CTA, 4 x 4 per thread, k staged 32 at a time; the image offset of each
+// patch element k comes from a per-CTA table and each thread's patch row base is computed once, so staging
+// costs one load per element; the fma chains run as paired fp32 instructions (same results).
+constexpr int kPeTile = 64, kPeK = 32, kPeMaxK = 1024;
 __global__ void __launch_bounds__(256)
 patch_embed_kernel(const float* __restrict__ img, int batch, int C, int H, int W, int P, const float* __restrict__ w,
                    const float* __restrict__ bias, const float* __restrict__ pos, int D, float* __restrict__ y,
                    int64_t ldy) {
     __shared__ __align__(16) float As[kPeK][kPeTile];  // [k][patch row]
     __shared__ __align__(16) float Ws[kPeK][kPeTile];  // [k][output column]
+    __shared__ int koff[kPeMaxK];                      // image offset of patch element k (channel, row, column)
     const int gw = W / P, np = (H / P) * gw, kdim = C * P * P, rows = batch * np;
     const int r0 = blockIdx.x * kPeTile, d0 = blockIdx.y * kPeTile;
     const int t = threadIdx.x, ty = t / 16, tx = t % 16;
+    for (int k = t; k < kdim; k += 256) koff[k] = ((k / (P * P)) * H + (k / P) % P) * W + k % P;
+    // Every staging pass has this thread write column i_s of As and Ws: one patch row, one weight row.
+    const int i_s = t % kPeTile, kk0 = t / kPeTile;
+    int64_t rbase = -1;
+    if (r0 + i_s < rows) {
+        const int r = r0 + i_s, bi = r / np, p = r % np, py = p / gw, px = p % gw;
+        rbase = ((int64_t)bi * C * H + (int64_t)py * P) * W + (int64_t)px * P;
+    }
+    const float* wrow = (d0 + i_s < D) ? w + (int64_t)(d0 + i_s) * kdim : nullptr;
     float acc[4][4];
 #pragma unroll
     for (int i = 0; i < 4; ++i)
 #pragma unroll
         for (int j = 0; j < 4; ++j) acc[i][j] = 0.0f;
+    __syncthreads();  // koff written
     for (int k0 = 0; k0 < kdim; k0 += kPeK) {
-        for (int e = t; e < kPeTile * kPeK; e += 256) {
-            const int i = e % kPeTile, kk = e / kPeTile, k = k0 + kk;
+#pragma unroll
+        for (int kk = kk0; kk < kPeK; kk += 256 / kPeTile) {
+            const int k = k0 + kk;
             float a = 0.0f, b = 0.0f;
             if (k < kdim) {
-                const int c = k / (P * P), ky = (k / P) % P, kx = k % P;
-                const int r = r0 + i;
-                if (r < rows) {
-                    const int bi = r / np, p = r % np, py = p / gw, px = p % gw;
-                    a = img[(((int64_t)bi * C + c) * H + (py * P + ky)) * W + (px * P + kx)];
-                }
-                if (d0 + i < D) b = w[(int64_t)(d0 + i) * kdim + k];
+                if (rbase >= 0) a = img[rbase + koff[k]];
+                if (wrow) b = wrow[k];
             }
-            As[kk][i] = a;
-            Ws[kk][i] = b;
+            As[kk][i_s] = a;
+            Ws[kk][i_s] = b;
         }
         __syncthreads();
 #pragma unroll 8
         for (int kk = 0; kk < kPeK; ++kk) {
             const float4 a = *reinterpret_cast<const float4*>(&As[kk][4 * ty]);
             const float4 b = *reinterpret_cast<const float4*>(&Ws[kk][4 * tx]);
-            const float av[4] = {a.x, a.y, a.z, a.w}, bv[4] = {b.x, b.y, b.z, b.w};
+            const float bv[4] = {b.x, b.y, b.z, b.w};
 #pragma unroll
-            for (int i = 0; i < 4; ++i)
-#pragma unroll
-                for (int j = 0; j < 4; ++j) acc[i][j] = __fmaf_rn(av[i], bv[j], acc[i][j]);
+            for (int j = 0; j < 4; ++j) {  // row pairs: the patch load holds them side by side
+                ffma2(acc[0][j], acc[1][j], a.x, a.y, bv[j], bv[j]);
+                ffma2(acc[2][j], acc[3][j], a.z, a.w, bv[j], bv[j]);
+            }
         }
         __syncthreads();
     }
@@ -299,6 +309,7 @@ patch_embed_kernel(const float* __restrict__ img, int batch, int C, int H, int W
 cudaError_t launch_patch_embed(const float* img, int batch, int C, int H, int W, int P, const float* w,
                                const float* bias, const float* pos, int D, float* y, int64_t ldy, cudaStream_t st) {
     const int rows = batch * (H / P) * (W / P);
+    if (C * P * P > kPeMaxK) return cudaErrorInvalidValue;  // the per-CTA offset table holds 1024 patch elements
     const dim3 grid((unsigned)ceil_div(rows, kPeTile), (unsigned)ceil_div(D, kPeTile));
     patch_embed_kernel<<<grid, 256, 0, st>>>(img, batch, C, H, W, P, w, bias, pos, D, y, ldy);
     return cudaGetLastError();
@@ -342,17 +353,6 @@ cudaError_t launch_embed_tokens(const int32_t* tokens, int n, int D, uint32_t se
 // Query head h reads K/V head h / (heads / kv_heads) (GQA). Shared memory: Q^T [hd][64], one K^T or V
 // chunk, the 64 x 64 probability tile and per-row factors; hd % 8 == 0, hd <= 128.
 constexpr int kAtQ = 64, kAtThreads = 256, kAtPP = kAtQ + 4;  // P row stride (floats)
-
-// d0 = fma(a0, b0, d0), d1 = fma(a1, b1, d1) as one paired fp32 instruction (each lane an IEEE fma, round to
-// nearest, no flush to zero: the same results as two __fmaf_rn).
-__device__ __forceinline__ void ffma2(float& d0, float& d1, float a0, float a1, float b0, float b1) {
-    uint64_t a, b, c;
-    asm("mov.b64 %0, {%1, %2};" : "=l"(a) : "f"(a0), "f"(a1));
-    asm("mov.b64 %0, {%1, %2};" : "=l"(b) : "f"(b0), "f"(b1));
-    asm("mov.b64 %0, {%1, %2};" : "=l"(c) : "f"(d0), "f"(d1));
-    asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(c) : "l"(a), "l"(b));
-    asm("mov.b64 {%0, %1}, %2;" : "=f"(d0), "=f"(d1) : "l"(c));
-}
 
 size_t attention_smem_bytes(int /*T*/, int hd) {
     return sizeof(float) * ((size_t)hd * kAtQ * 2 + (size_t)kAtQ * kAtPP + 2 * kAtQ);
