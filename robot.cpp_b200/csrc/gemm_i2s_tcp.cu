@@ -137,7 +137,9 @@ gemm_i2s_tcp_kernel(const __grid_constant__ CUtensorMap tmap_w0, const __grid_co
         // ------------------------------------------------------------------ MMA issuer
         if (lane == 0) {
             const uint32_t idesc = idesc_u8s8(128, T);
-            const uint32_t act_base = smem_u32(act_sm);
+            // B descriptors: the ring's first one, computed once; stage s and K slice kk add their byte offset
+            // / 16 to the start-address field (exact: shared addresses stay below 2^18 bytes).
+            const uint64_t desc0 = umma_desc_k_sw128(smem_u32(act_sm));
             uint32_t g = 0, i = 0;
             bool issued_any = false, stop = false;
             for (int t = blockIdx.x; t < total && !stop; t += gridDim.x, ++i) {
@@ -154,12 +156,12 @@ gemm_i2s_tcp_kernel(const __grid_constant__ CUtensorMap tmap_w0, const __grid_co
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t b_base = act_base + s * (uint32_t)kActStageBytes;
+                    const uint64_t bd = desc0 + (uint64_t)(s * (uint32_t)(kActStageBytes >> 4));
                     const uint32_t a_base = tmem_base + a * 32u;
-#pragma unroll
-                    for (int kk = 0; kk < 4; ++kk)
-                        tc_mma_i8_ts(d_tmem, a_base + kk * 8, umma_desc_k_sw128(b_base + kk * 32), idesc,
-                                     (kt > 0 || kk > 0) ? 1u : 0u);
+                    tc_mma_i8_ts(d_tmem, a_base, bd, idesc, kt > 0 ? 1u : 0u);
+                    tc_mma_i8_ts_acc(d_tmem, a_base + 8, bd + 2, idesc);
+                    tc_mma_i8_ts_acc(d_tmem, a_base + 16, bd + 4, idesc);
+                    tc_mma_i8_ts_acc(d_tmem, a_base + 24, bd + 6, idesc);
                     issued_any = true;
                     tc_commit(&bars->sfree[s]);
                     tc_commit(&bars->afree[a]);
