@@ -2,15 +2,19 @@
 // outputs with at least one tile per SM.
 //
 // One CTA per SM walks the output tiles (128 weight rows x T tokens, T <= 192; in the gate/up mode 64 gate
-// and 64 up rows) in the order blockIdx.x, blockIdx.x + gridDim.x, ... Per 128-wide K step:
-//   * warp 4 (producer) TMA-loads the packed weight tile (128 rows x 32 bytes, local HBM, no multicast)
-//     and the int8 activation tile (T rows x 128 bytes, 128B swizzle) into a 7-stage shared-memory ring;
-//   * warps 0-3 (converters, one per TMEM lane quadrant) turn each row's 32 packed bytes into 128 unsigned
-//     2-bit codes {0,1,2} and store them with tcgen05.st into a 4-stage TMEM ring (the MMA's A operand:
-//     with two stages a converter waited for the MMAs of the step before last, and that round trip --
-//     MMA issue, completion, commit, the converter's own wait -- paced the K loop);
-//   * warp 5 (MMA) issues four tcgen05.mma.kind::i8 (M=128, N=T, K=32): A = codes from TMEM, B = signed
-//     int8 activations from shared memory, int32 accumulators in one of two TMEM buffers;
+// and 64 up rows) in the order blockIdx.x, blockIdx.x + gridDim.x, ... Work moves between the roles in
+// stages of two 128-wide K steps: a stage's barrier waits, arrivals, fences and commits cost about as much
+// as a step's MMAs at these tile sizes (time per tile, measured over token tiles of 64..192, is ~3/4 a
+// fixed per-handoff cost), so each handoff carries twice the work. Per stage:
+//   * warp 4 (producer) TMA-loads, for each of its two K steps, the packed weight tile (128 rows x 32 bytes,
+//     local HBM, no multicast) and the int8 activation tile (T rows x 128 bytes, 128B swizzle) into a
+//     3-stage shared-memory ring; past Kp (an odd step count) the boxes read zeros, which add nothing;
+//   * warps 0-3 (converters, one per TMEM lane quadrant) turn each row's 2 x 32 packed bytes into 2 x 128
+//     unsigned 2-bit codes {0,1,2} and store them with tcgen05.st into a 2-stage TMEM ring (the MMA's A
+//     operand), one store wait and one arrival per stage;
+//   * warp 5 (MMA) issues eight tcgen05.mma.kind::i8 (M=128, N=T, K=32): A = codes from TMEM, B = signed
+//     int8 activations from shared memory (descriptors derived from one precomputed ring descriptor),
+//     int32 accumulators in one of two TMEM buffers;
 //   * warps 6-13 (epilogue, two per quadrant) read the finished buffer (tcgen05.ld) and write
 //     y = (float)(acc - sum_q[m]) * (w_scale / s[m]) (+ bias, GELU, + residual), while the MMAs of the
 //     next tile already fill the other buffer. The output writes of one tile therefore overlap the
@@ -25,14 +29,17 @@
 namespace b2s {
 
 namespace tcp {
-constexpr int kStages = 7;
-constexpr int kAStages = 4;
+constexpr int kKS = 2;       // 128-wide K steps per stage and per handoff between the roles
+constexpr int kStages = 3;   // shared-memory ring (stages of kKS K steps)
+constexpr int kAStages = 2;  // TMEM ring of converted codes (stages of kKS x 32 columns)
 constexpr int kMaxT = 192;
-constexpr int kActStageBytes = kMaxT * 128;  // 24 KB, a multiple of 1024 (SW128 atoms)
-constexpr int kWStageBytes = 128 * 32;
+constexpr int kActSubBytes = kMaxT * 128;             // one K step's activation tile (24 KB, SW128 atoms)
+constexpr int kActStageBytes = kKS * kActSubBytes;
+constexpr int kWSubBytes = 128 * 32;                  // one K step's packed weight tile
+constexpr int kWStageBytes = kKS * kWSubBytes;
 constexpr int kThreads = 448;  // warps 0-3 converters, 4 TMA producer, 5 MMA, 6-13 epilogue
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kAccCol0 = kAStages * 32;  // accumulator buffer b at kAccCol0 + b * kMaxT
+constexpr uint32_t kAccCol0 = kAStages * kKS * 32;  // accumulator buffer b at kAccCol0 + b * kMaxT
 static_assert(kAccCol0 + 2 * kMaxT <= kTmemCols, "TMEM budget");
 
 struct alignas(8) Bars {
@@ -73,8 +80,9 @@ gemm_i2s_tcp_kernel(const __grid_constant__ CUtensorMap tmap_w0, const __grid_co
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     constexpr int rows_per_w = (MODE == 1) ? 64 : 128;
     const int nkt = Kp / 128;
+    const int nks = (nkt + kKS - 1) / kKS;  // stages per tile (past Kp the boxes read zeros, which add 0)
     const int total = n_tiles * m_tiles;
-    const uint32_t tx = (uint32_t)T * 128u + (uint32_t)kWStageBytes;
+    const uint32_t tx = (uint32_t)kKS * ((uint32_t)T * 128u + (uint32_t)kWSubBytes);
 
     if (threadIdx.x == 128) {
         for (int i = 0; i < kStages; ++i) {
@@ -114,7 +122,7 @@ gemm_i2s_tcp_kernel(const __grid_constant__ CUtensorMap tmap_w0, const __grid_co
             bool stop = false;
             for (int t = blockIdx.x; t < total && !stop; t += gridDim.x) {
                 const int nb = (t % n_tiles) * rows_per_w, m0 = (t / n_tiles) * T;
-                for (int kt = 0; kt < nkt; ++kt, ++g) {
+                for (int ks = 0; ks < nks; ++ks, ++g) {
                     const uint32_t s = g % kStages, u = g / kStages;
                     if (u > 0 && (!mbar_wait(&bars->sfree[s], (u - 1) & 1u) || *abort_flag)) {
                         *abort_flag = 1;
@@ -122,10 +130,15 @@ gemm_i2s_tcp_kernel(const __grid_constant__ CUtensorMap tmap_w0, const __grid_co
                         break;
                     }
                     mbar_arrive_expect_tx(&bars->full[s], tx);
-                    uint8_t* wst = w_sm + (size_t)s * kWStageBytes;
-                    tma_load_2d(wst, &tmap_w0, &bars->full[s], kt * 32, nb);
-                    if (MODE == 1) tma_load_2d(wst + 64 * 32, &tmap_w1, &bars->full[s], kt * 32, nb);
-                    tma_load_2d(act_sm + (size_t)s * kActStageBytes, &tmap_q, &bars->full[s], kt * 128, m0);
+#pragma unroll
+                    for (int j = 0; j < kKS; ++j) {
+                        const int kt = kKS * ks + j;
+                        uint8_t* wst = w_sm + (size_t)s * kWStageBytes + (size_t)j * kWSubBytes;
+                        tma_load_2d(wst, &tmap_w0, &bars->full[s], kt * 32, nb);
+                        if (MODE == 1) tma_load_2d(wst + 64 * 32, &tmap_w1, &bars->full[s], kt * 32, nb);
+                        tma_load_2d(act_sm + (size_t)s * kActStageBytes + (size_t)j * kActSubBytes, &tmap_q,
+                                    &bars->full[s], kt * 128, m0);
+                    }
                 }
             }
             // Copies still in flight must land before the CTA's shared memory goes away: wait for the
@@ -147,7 +160,7 @@ gemm_i2s_tcp_kernel(const __grid_constant__ CUtensorMap tmap_w0, const __grid_co
                 if (v > 0 && !mbar_wait(&bars->accfree[b], (v - 1) & 1u)) { *abort_flag = 1; break; }
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + kAccCol0 + b * (uint32_t)kMaxT;
-                for (int kt = 0; kt < nkt; ++kt, ++g) {
+                for (int ks = 0; ks < nks; ++ks, ++g) {
                     const uint32_t s = g % kStages, a = g % kAStages;
                     if (!mbar_wait(&bars->afull[a], (g / kAStages) & 1u) ||
                         !mbar_wait(&bars->full[s], (g / kStages) & 1u) || *abort_flag) {
@@ -156,12 +169,16 @@ gemm_i2s_tcp_kernel(const __grid_constant__ CUtensorMap tmap_w0, const __grid_co
                         break;
                     }
                     tc_fence_after();
-                    const uint64_t bd = desc0 + (uint64_t)(s * (uint32_t)(kActStageBytes >> 4));
-                    const uint32_t a_base = tmem_base + a * 32u;
-                    tc_mma_i8_ts(d_tmem, a_base, bd, idesc, kt > 0 ? 1u : 0u);
-                    tc_mma_i8_ts_acc(d_tmem, a_base + 8, bd + 2, idesc);
-                    tc_mma_i8_ts_acc(d_tmem, a_base + 16, bd + 4, idesc);
-                    tc_mma_i8_ts_acc(d_tmem, a_base + 24, bd + 6, idesc);
+#pragma unroll
+                    for (int j = 0; j < kKS; ++j) {
+                        const uint64_t bd =
+                            desc0 + (uint64_t)((s * (uint32_t)kActStageBytes + j * (uint32_t)kActSubBytes) >> 4);
+                        const uint32_t a_base = tmem_base + a * (uint32_t)(kKS * 32) + j * 32u;
+                        tc_mma_i8_ts(d_tmem, a_base, bd, idesc, (ks > 0 || j > 0) ? 1u : 0u);
+                        tc_mma_i8_ts_acc(d_tmem, a_base + 8, bd + 2, idesc);
+                        tc_mma_i8_ts_acc(d_tmem, a_base + 16, bd + 4, idesc);
+                        tc_mma_i8_ts_acc(d_tmem, a_base + 24, bd + 6, idesc);
+                    }
                     issued_any = true;
                     tc_commit(&bars->sfree[s]);
                     tc_commit(&bars->afree[a]);
@@ -185,29 +202,36 @@ gemm_i2s_tcp_kernel(const __grid_constant__ CUtensorMap tmap_w0, const __grid_co
         uint32_t g = 0;
         bool ok = true;
         for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
-            for (int kt = 0; kt < nkt; ++kt, ++g) {
+            for (int ks = 0; ks < nks; ++ks, ++g) {
                 const uint32_t s = g % kStages, a = g % kAStages, ua = g / kAStages;
                 int good = 1;
                 if (lane == 0) good = (*abort_flag == 0) && mbar_wait(&bars->full[s], (g / kStages) & 1u);
                 if (!__shfl_sync(0xffffffffu, good, 0)) { ok = false; break; }
                 (void)mbar_try_wait(&bars->full[s], (g / kStages) & 1u);  // each lane acquires the phase
                 // 32-byte swizzle: rows 4-7 of every 8 have their 16-byte halves swapped (TMA SWIZZLE_32B)
-                const uint8_t* rowp = w_sm + (size_t)s * kWStageBytes + r_sm * 32;
                 const int sw = (r_sm >> 2) & 1;
-                const uint4 p0 = *reinterpret_cast<const uint4*>(rowp + 16 * sw);
-                const uint4 p1 = *reinterpret_cast<const uint4*>(rowp + 16 * (1 - sw));
+                uint4 p0[kKS], p1[kKS];
+#pragma unroll
+                for (int j = 0; j < kKS; ++j) {
+                    const uint8_t* rowp = w_sm + (size_t)s * kWStageBytes + (size_t)j * kWSubBytes + r_sm * 32;
+                    p0[j] = *reinterpret_cast<const uint4*>(rowp + 16 * sw);
+                    p1[j] = *reinterpret_cast<const uint4*>(rowp + 16 * (1 - sw));
+                }
                 if (lane == 0 && ua > 0) good = mbar_wait(&bars->afree[a], (ua - 1) & 1u);
                 if (!__shfl_sync(0xffffffffu, good, 0)) { ok = false; break; }
-                const uint32_t w[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
-                uint32_t out[32];
 #pragma unroll
-                for (int p = 0; p < 8; ++p) {
-                    out[p] = (w[p] >> 6) & 0x03030303u;
-                    out[8 + p] = (w[p] >> 4) & 0x03030303u;
-                    out[16 + p] = (w[p] >> 2) & 0x03030303u;
-                    out[24 + p] = w[p] & 0x03030303u;
+                for (int j = 0; j < kKS; ++j) {
+                    const uint32_t w[8] = {p0[j].x, p0[j].y, p0[j].z, p0[j].w, p1[j].x, p1[j].y, p1[j].z, p1[j].w};
+                    uint32_t out[32];
+#pragma unroll
+                    for (int p = 0; p < 8; ++p) {
+                        out[p] = (w[p] >> 6) & 0x03030303u;
+                        out[8 + p] = (w[p] >> 4) & 0x03030303u;
+                        out[16 + p] = (w[p] >> 2) & 0x03030303u;
+                        out[24 + p] = w[p] & 0x03030303u;
+                    }
+                    tmem_st_32x32b_x32(lane_base + a * (uint32_t)(kKS * 32) + j * 32u, out);
                 }
-                tmem_st_32x32b_x32(lane_base + a * 32u, out);
                 tc_wait_st();
                 tc_fence_before();
                 __syncwarp();
