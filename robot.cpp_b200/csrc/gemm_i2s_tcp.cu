@@ -8,7 +8,7 @@
 // fixed per-handoff cost), so each handoff carries twice the work. Per stage:
 //   * warp 4 (producer) TMA-loads, for each of its two K steps, the packed weight tile (128 rows x 32 bytes,
 //     local HBM, no multicast) and the int8 activation tile (T rows x 128 bytes, 128B swizzle) into a
-//     3-stage shared-memory ring; past Kp (an odd step count) the boxes read zeros, which add nothing;
+//     4-stage shared-memory ring; past Kp (an odd step count) the boxes read zeros, which add nothing;
 //   * warps 0-3 (converters, one per TMEM lane quadrant) turn each row's 2 x 32 packed bytes into 2 x 128
 //     unsigned 2-bit codes {0,1,2} and store them with tcgen05.st into a 2-stage TMEM ring (the MMA's A
 //     operand), one store wait and one arrival per stage;
@@ -30,7 +30,7 @@ namespace b2s {
 
 namespace tcp {
 constexpr int kKS = 2;       // 128-wide K steps per stage and per handoff between the roles
-constexpr int kStages = 3;   // shared-memory ring (stages of kKS K steps)
+constexpr int kStages = 4;   // shared-memory ring (stages of kKS K steps)
 constexpr int kAStages = 2;  // TMEM ring of converted codes (stages of kKS x 32 columns)
 constexpr int kMaxT = 192;
 constexpr int kActSubBytes = kMaxT * 128;             // one K step's activation tile (24 KB, SW128 atoms)
@@ -54,6 +54,7 @@ struct alignas(8) Bars {
     uint32_t abort;
 };
 constexpr size_t kSmemBytes = 1024 + (size_t)kStages * (kActStageBytes + kWStageBytes) + sizeof(Bars);
+static_assert(kSmemBytes <= 227 * 1024, "dynamic shared memory per CTA");
 }  // namespace tcp
 
 // Instruction descriptor, kind::i8: D s32, A unsigned 8-bit (codes), B signed 8-bit, K-major, 128 x N.
