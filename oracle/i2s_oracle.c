@@ -213,10 +213,24 @@ float orc_det_expf(float x) {
     return p * two_n;
 }
 
-/* tanh(u) = sign(u) (1 - 2 / (e^{2|u|} + 1)), |u| > 9 -> +-1 (the device's det_tanhf). */
+/* 1 / d for a normal d > 0 (the device's det_recipf): the bit-pattern seed 0x7EF311C3 - bits(d) (within
+ * 12.5%) and three Newton-Raphson steps y <- y + y (1 - d y), each two fused multiply-adds; relative error
+ * below 2^-22. */
+float orc_det_recipf(float d) {
+    uint32_t bits;
+    memcpy(&bits, &d, sizeof bits);
+    bits = 0x7EF311C3u - bits;
+    float y;
+    memcpy(&y, &bits, sizeof y);
+    for (int i = 0; i < 3; ++i) y = fmaf(y, fmaf(-d, y, 1.0f), y);
+    return y;
+}
+
+/* tanh(u) = sign(u) (1 - 2 / (e^{2|u|} + 1)) with the reciprocal of orc_det_recipf, |u| > 9 -> +-1 (the
+ * device's det_tanhf). */
 float orc_det_tanhf(float u) {
     const float a = fabsf(u);
-    const float t = (a > 9.0f) ? 1.0f : 1.0f - 2.0f / (orc_det_expf(2.0f * a) + 1.0f);
+    const float t = (a > 9.0f) ? 1.0f : 1.0f - 2.0f * orc_det_recipf(orc_det_expf(2.0f * a) + 1.0f);
     return copysignf(t, u);
 }
 

@@ -91,6 +91,7 @@ void orc_ffn_block(const float *X, int64_t M, int64_t H, int64_t F,
 
 /* ---- deterministic fp32 transcendental functions shared with the device kernels ---- */
 float orc_det_expf(float x);
+float orc_det_recipf(float d);
 float orc_det_tanhf(float u);
 float orc_warp_order_sum(const float *e, int64_t n);
 

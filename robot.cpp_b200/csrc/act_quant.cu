@@ -155,8 +155,9 @@ act_quant_kernel(const float* __restrict__ x, int64_t ldx, const float* __restri
 // warp shuffles and one TPR/32-entry shared-memory step. The kernel is latency-bound (a row of P is in
 // L2 when it runs): wide CTAs keep the per-thread dependency chains short, and the configuration keeps
 // every row of a prefill batch (a few hundred rows) resident in one wave (4 CTAs of 256 threads per SM).
-// KIND: 0 RMSNorm, 1 LayerNorm, 2 no norm. The fp32 operation sequence per element is the one of
-// act_quant_kernel / norm_kernel; only the (double) summation order differs.
+// KIND: 0 RMSNorm, 1 LayerNorm, 2 no norm, 3 GELU then no norm (gelu_tanh, the GEMM epilogue's fp32
+// operations, applied here to a GEMM output written without it). The fp32 operation sequence per element
+// is the one of act_quant_kernel / norm_kernel; only the (double) summation order differs.
 template <int NW>
 __device__ __forceinline__ double row_sum_d(double v, double* red) {
     v = warp_sum_d(v);
@@ -223,7 +224,7 @@ rowq_kernel(const float* __restrict__ x, int64_t ldx, const float* __restrict__ 
         }
         mean = (float)(row_sum_d<NW>(acc, red_d) / (double)K);
     }
-    if (KIND != 2) {
+    if (KIND < 2) {
         double acc2 = 0.0;
 #pragma unroll
         for (int i = 0; i < VPT; ++i) {
@@ -243,6 +244,7 @@ rowq_kernel(const float* __restrict__ x, int64_t ldx, const float* __restrict__ 
     const float4* g4 = reinterpret_cast<const float4*>(g);
     const float4* b4 = reinterpret_cast<const float4*>(b);
     auto val = [&](float v, float gv, float bv) -> float {
+        if (KIND == 3) return gelu_tanh(v);
         if (KIND == 2) return v;
         if (KIND == 1) v = __fsub_rn(v, mean);
         v = __fmul_rn(v, nscale);
@@ -254,8 +256,8 @@ rowq_kernel(const float* __restrict__ x, int64_t ldx, const float* __restrict__ 
     for (int i = 0; i < VPT; ++i) {
         const int c = threadIdx.x + TPR * i;
         if (c >= K4) continue;
-        const float4 gv = (KIND != 2 && g) ? g4[c] : make_float4(0.f, 0.f, 0.f, 0.f);
-        const float4 bv = (KIND != 2 && b) ? b4[c] : make_float4(0.f, 0.f, 0.f, 0.f);
+        const float4 gv = (KIND < 2 && g) ? g4[c] : make_float4(0.f, 0.f, 0.f, 0.f);
+        const float4 bv = (KIND < 2 && b) ? b4[c] : make_float4(0.f, 0.f, 0.f, 0.f);
         r[i].x = val(r[i].x, gv.x, bv.x);
         r[i].y = val(r[i].y, gv.y, bv.y);
         r[i].z = val(r[i].z, gv.z, bv.z);
@@ -346,6 +348,7 @@ cudaError_t launch_rowq(int kind, bool quant, const float* x, int64_t ldx, const
         if (quant) return launch_rowq_k<1, true>(x, ldx, g, b, eps, M, k, y, ldy, q, ldq, s, sums, st);
         return launch_rowq_k<1, false>(x, ldx, g, b, eps, M, k, y, ldy, q, ldq, s, sums, st);
     }
+    if (kind == 3) return launch_rowq_k<3, true>(x, ldx, nullptr, nullptr, 0.0f, M, k, y, ldy, q, ldq, s, sums, st);
     return launch_rowq_k<2, true>(x, ldx, nullptr, nullptr, 0.0f, M, k, y, ldy, q, ldq, s, sums, st);
 }
 

@@ -57,15 +57,17 @@ __device__ __forceinline__ float warp_sum_f(float v) {
 
 // ---------------------------------------------------------------- deterministic transcendental functions
 // exp and tanh of the library's fp32 kernels, built from IEEE operations only (fused multiply-adds,
-// products, one division) so that the CPU oracle reproduces them bit for bit: Cody and Waite's range
+// products, sums) so that the CPU oracle reproduces them bit for bit: Cody and Waite's range
 // reduction x = n ln2 + r (|r| <= ln2/2, ln2 split into a 16-bit head and a tail) and the degree-7
 // Taylor polynomial of e^r in Horner form, scaled by 2^n. Relative error below 2 ulp; inputs below
-// -86 return 0 (no subnormal results), above 88 saturate at e^88.
+// -86 return 0 (no subnormal results), above 88 saturate at e^88. Written without branches (the
+// out-of-range inputs are clamped and their result selected away) so that unrolled loops of independent
+// calls interleave.
 __device__ __forceinline__ float det_expf(float x) {
-    if (!(x >= -86.0f)) return 0.0f;  // also NaN -> 0
-    x = fminf(x, 88.0f);
-    const float n = rintf(__fmul_rn(x, 1.44269502162933349609375f));
-    float r = __fmaf_rn(-n, 0.693145751953125f, x);
+    const bool low = !(x >= -86.0f);  // also NaN -> 0
+    const float xc = low ? -86.0f : fminf(x, 88.0f);
+    const float n = rintf(__fmul_rn(xc, 1.44269502162933349609375f));
+    float r = __fmaf_rn(-n, 0.693145751953125f, xc);
     r = __fmaf_rn(-n, 1.428606765330187045e-06f, r);
     float p = 1.98412698412698412698e-04f;
     p = __fmaf_rn(p, r, 1.38888888888888888889e-03f);
@@ -75,13 +77,24 @@ __device__ __forceinline__ float det_expf(float x) {
     p = __fmaf_rn(p, r, 0.5f);
     p = __fmaf_rn(p, r, 1.0f);
     p = __fmaf_rn(p, r, 1.0f);
-    return __fmul_rn(p, __int_as_float(((int)n + 127) << 23));
+    const float v = __fmul_rn(p, __int_as_float(((int)n + 127) << 23));
+    return low ? 0.0f : v;
 }
-// tanh(u) = sign(u) (1 - 2 / (e^{2|u|} + 1)); |u| > 9 gives +-1.
+// 1 / d for a normal d > 0: the bit-pattern seed 0x7EF311C3 - bits(d) (within 12.5%) and three
+// Newton-Raphson steps y <- y + y (1 - d y), each two fused multiply-adds; relative error below 2^-22.
+// Every step is an IEEE operation, so the CPU oracle's restatement gives the same bits.
+__device__ __forceinline__ float det_recipf(float d) {
+    float y = __uint_as_float(0x7EF311C3u - __float_as_uint(d));
+#pragma unroll
+    for (int i = 0; i < 3; ++i) y = __fmaf_rn(y, __fmaf_rn(-d, y, 1.0f), y);
+    return y;
+}
+// tanh(u) = sign(u) (1 - 2 / (e^{2|u|} + 1)) with the reciprocal of det_recipf; |u| > 9 gives +-1. No
+// branches: a NaN or |u| > 9 is clamped before the exponential and its result selected away.
 __device__ __forceinline__ float det_tanhf(float u) {
-    const float a = fabsf(u);
-    const float t = (a > 9.0f) ? 1.0f : __fsub_rn(1.0f, __fdiv_rn(2.0f, __fadd_rn(det_expf(__fmul_rn(2.0f, a)), 1.0f)));
-    return copysignf(t, u);
+    const float a = fminf(fabsf(u), 9.5f);
+    const float t = __fsub_rn(1.0f, __fmul_rn(2.0f, det_recipf(__fadd_rn(det_expf(__fmul_rn(2.0f, a)), 1.0f))));
+    return copysignf(fabsf(u) > 9.0f ? 1.0f : t, u);
 }
 
 // ---------------------------------------------------------------- programmatic dependent launch

@@ -38,7 +38,7 @@ struct Q8Act {
 };
 
 // Register-resident norm / act-quant of rows of K <= 8192 (act_quant.cu); kind 0 RMSNorm, 1 LayerNorm,
-// 2 no norm (quant only). rowq_eligible: K % 4 == 0, 16-byte aligned rows and parameters.
+// 2 no norm (quant only), 3 GELU (gelu_tanh) then act-quant (quant only). rowq_eligible: K % 4 == 0, 16-byte aligned rows and parameters.
 bool rowq_eligible(const float* x, int64_t ldx, const float* g, const float* b, int64_t K, const void* out,
                    int64_t ldo, bool quant);
 cudaError_t launch_rowq(int kind, bool quant, const float* x, int64_t ldx, const float* g, const float* b, float eps,

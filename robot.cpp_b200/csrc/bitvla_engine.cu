@@ -9,9 +9,10 @@
 //
 // Every linear layer runs through the library's int8 activation path: the producer kernel (norm or
 // act-quant) writes int8 codes + per-token scale + code sum, the ternary GEMM consumes them, and the
-// GEMM's epilogue adds bias, applies GELU and adds the residual in place. q/k/v of a layer are one
-// stacked ternary weight (each part keeps its own scale), so one GEMM produces [q | k | v] rows and one
-// RoPE launch rotates the q and k heads together. Attention is one fused fp32 kernel over all
+// GEMM's epilogue adds bias and adds the residual in place; GELU runs in the act-quant kernel that reads
+// the GEMM output for the next layer. q/k/v of a layer are one stacked ternary weight (each part keeps its
+// own scale), so one GEMM produces [q | k | v] rows, and the fp32 attention kernel rotates the q and k heads
+// (RoPE) as it stages them. Attention is one fused fp32 kernel over all
 // (query block, head, observation) triples of the batch.
 //
 // HBM layout: one arena for all weights (packed ternary rows padded to 128 weights, scales, fp32
@@ -499,6 +500,11 @@ int enqueue_forward(b2s_bitvla* m, int B, cudaStream_t st) {
                                      D, m->vx, D, st),
              "patch_embed");
     const float vit_scale = 1.0f / sqrtf((float)(D / c.vit_heads));
+    // GELU of the fc1 and first connector outputs runs in the act-quant kernel that reads them for the next
+    // GEMM (the epilogue's fp32 operations, applied at full occupancy instead of by the GEMM's epilogue warps)
+    // whenever that kernel takes the shape; otherwise the GEMM epilogue applies it.
+    const bool vit_gelu_q = b2s::rowq_eligible(m->vh, F, nullptr, nullptr, F, m->q8, ldq, true);
+    const bool conn_gelu_q = b2s::rowq_eligible(m->ch, c.conn_hidden, nullptr, nullptr, c.conn_hidden, m->q8, ldq, true);
     for (int l = 0; l < c.vit_layers; ++l) {
         const VitLayer& L = m->vit[(size_t)l];
         TRY_CUDA(b2s::launch_norm(1, true, m->vx, D, L.ln1_w, L.ln1_b, c.vit_eps, Mv, D, nullptr, 0, m->q8, ldq, m->qs,
@@ -514,8 +520,11 @@ int enqueue_forward(b2s_bitvla* m, int B, cudaStream_t st) {
         TRY_CUDA(b2s::launch_norm(1, true, m->vx, D, L.ln2_w, L.ln2_b, c.vit_eps, Mv, D, nullptr, 0, m->q8, ldq, m->qs,
                                   m->qsum, st),
                  "vit ln2");
-        TRY_B2S(gemm(L.fc1, Mv, m->vh, F, L.fc1_b, nullptr, 1));
-        TRY_CUDA(b2s::launch_act_quant(m->vh, F, nullptr, false, 0.0f, Mv, F, m->q8, ldq, m->qs, m->qsum, st),
+        TRY_B2S(gemm(L.fc1, Mv, m->vh, F, L.fc1_b, nullptr, vit_gelu_q ? 0 : 1));
+        TRY_CUDA(vit_gelu_q ? b2s::launch_rowq(3, true, m->vh, F, nullptr, nullptr, 0.0f, Mv, F, nullptr, 0, m->q8, ldq,
+                                               m->qs, m->qsum, st)
+                            : b2s::launch_act_quant(m->vh, F, nullptr, false, 0.0f, Mv, F, m->q8, ldq, m->qs, m->qsum,
+                                                    st),
                  "vit fc2 act_quant");
         TRY_B2S(gemm(L.fc2, Mv, m->vx, D, L.fc2_b, m->vx, 0));
     }
@@ -523,9 +532,11 @@ int enqueue_forward(b2s_bitvla* m, int B, cudaStream_t st) {
     TRY_CUDA(b2s::launch_norm(1, true, m->vx, D, m->post_w, m->post_b, c.vit_eps, Mv, D, nullptr, 0, m->q8, ldq, m->qs,
                               m->qsum, st),
              "post layernorm");
-    TRY_B2S(gemm(m->conn1, Mv, m->ch, c.conn_hidden, m->conn1_b, nullptr, 1));
-    TRY_CUDA(b2s::launch_act_quant(m->ch, c.conn_hidden, nullptr, false, 0.0f, Mv, c.conn_hidden, m->q8, ldq, m->qs,
-                                   m->qsum, st),
+    TRY_B2S(gemm(m->conn1, Mv, m->ch, c.conn_hidden, m->conn1_b, nullptr, conn_gelu_q ? 0 : 1));
+    TRY_CUDA(conn_gelu_q ? b2s::launch_rowq(3, true, m->ch, c.conn_hidden, nullptr, nullptr, 0.0f, Mv, c.conn_hidden,
+                                            nullptr, 0, m->q8, ldq, m->qs, m->qsum, st)
+                         : b2s::launch_act_quant(m->ch, c.conn_hidden, nullptr, false, 0.0f, Mv, c.conn_hidden, m->q8,
+                                                 ldq, m->qs, m->qsum, st),
              "connector act_quant");
     if (B == 1) {
         TRY_B2S(gemm(m->conn2, Mv, m->dx, H, m->conn2_b, nullptr, 0));

@@ -487,16 +487,21 @@ gemm_i2s_tc_kernel(const __grid_constant__ CUtensorMap tmap_w0, const __grid_con
         auto finish = [&](int ch, const int32_t (&raw)[16], const float (&res)[16]) {
             const int t0 = ch * 16;
             if (mode == 0) {
+                // all 16 values first (independent chains that interleave), then the guarded stores
+                float val[16];
 #pragma unroll
                 for (int j = 0; j < 16; ++j) {
-                    const int t = t0 + j, m = m0 + t;
+                    const int t = t0 + j;
                     float v = __fmul_rn((float)(raw[j] - sumq[t]), rfac[t]);
-                    if (good && m < M && n < N) {
-                        if (EPI & kEpiBias) v = __fadd_rn(v, bias_n);
-                        if (EPI & kEpiGelu) v = gelu_tanh(v);
-                        if (EPI & kEpiResidual) v = __fadd_rn(res[j], v);
-                        y[(int64_t)m * ldy + n] = v;
-                    }
+                    if (EPI & kEpiBias) v = __fadd_rn(v, bias_n);
+                    if (EPI & kEpiGelu) v = gelu_tanh(v);
+                    if (EPI & kEpiResidual) v = __fadd_rn(res[j], v);
+                    val[j] = v;
+                }
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    const int m = m0 + t0 + j;
+                    if (good && m < M && n < N) y[(int64_t)m * ldy + n] = val[j];
                 }
             } else {
                 float p[16];

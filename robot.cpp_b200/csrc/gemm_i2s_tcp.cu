@@ -274,14 +274,6 @@ gemm_i2s_tcp_kernel(const __grid_constant__ CUtensorMap tmap_w0, const __grid_co
                 sm[c] = ok ? sum_act[mj] : 0;
                 rf[c] = ok ? __fdiv_rn(wsl, s_act[mj]) : 0.0f;
             }
-            int good = 1;
-            if (lane == 0) good = (*abort_flag == 0) && mbar_wait(&bars->accfull[b], v & 1u);
-            if (!__shfl_sync(0xffffffffu, good, 0)) {
-                if (lane == 0) *abort_flag = 1;
-                break;
-            }
-            tc_fence_after();
-            const uint32_t acc = lane_base + kAccCol0 + b * (uint32_t)kMaxT;
             auto load_res = [&](int ch, float (&r)[16]) {
 #pragma unroll
                 for (int j = 0; j < 16; ++j) {
@@ -291,21 +283,36 @@ gemm_i2s_tcp_kernel(const __grid_constant__ CUtensorMap tmap_w0, const __grid_co
                                : 0.0f;
                 }
             };
+            // residual rows run one chunk ahead of the stores: the first chunk's are fetched before the wait
+            float resa[16], resb[16];
+            load_res(2 * grp, resa);
+            int good = 1;
+            if (lane == 0) good = (*abort_flag == 0) && mbar_wait(&bars->accfull[b], v & 1u);
+            if (!__shfl_sync(0xffffffffu, good, 0)) {
+                if (lane == 0) *abort_flag = 1;
+                break;
+            }
+            tc_fence_after();
+            const uint32_t acc = lane_base + kAccCol0 + b * (uint32_t)kMaxT;
             auto finish = [&](int ch, const uint32_t (&raw)[16], float rfc, int smc, const float (&res)[16]) {
                 const int t0 = 16 * ch;
                 if (MODE == 0) {
+                    // all 16 values first (independent chains that interleave), then the guarded stores
+                    float val[16];
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        const float rfj = __shfl_sync(0xffffffffu, rfc, j);
+                        const int smj = __shfl_sync(0xffffffffu, smc, j);
+                        float v = __fmul_rn((float)((int32_t)raw[j] - smj), rfj);
+                        if (EPI & kPEpiBias) v = __fadd_rn(v, bias_n);
+                        if (EPI & kPEpiGelu) v = gelu_tanh(v);
+                        if (EPI & kPEpiResidual) v = __fadd_rn(res[j], v);
+                        val[j] = v;
+                    }
 #pragma unroll
                     for (int j = 0; j < 16; ++j) {
                         const int m = m0 + t0 + j;
-                        const float rfj = __shfl_sync(0xffffffffu, rfc, j);
-                        const int smj = __shfl_sync(0xffffffffu, smc, j);
-                        float val = __fmul_rn((float)((int32_t)raw[j] - smj), rfj);
-                        if (m < M && n < N) {
-                            if (EPI & kPEpiBias) val = __fadd_rn(val, bias_n);
-                            if (EPI & kPEpiGelu) val = gelu_tanh(val);
-                            if (EPI & kPEpiResidual) val = __fadd_rn(res[j], val);
-                            y[(int64_t)m * ldy + n] = val;
-                        }
+                        if (m < M && n < N) y[(int64_t)m * ldy + n] = val[j];
                     }
                 } else {
                     float p[16];
@@ -332,17 +339,14 @@ gemm_i2s_tcp_kernel(const __grid_constant__ CUtensorMap tmap_w0, const __grid_co
                 const int ch = 4 * pp + 2 * grp;
                 if (ch >= nchunk) break;
                 const bool hb = ch + 1 < nchunk;
-                float res[16];  // residual rows in flight while the accumulators are read (one chunk at a time)
-                load_res(ch, res);
                 uint32_t xa[16], xb[16];
                 tmem_ld_x16(acc + (uint32_t)(16 * ch), xa);
                 if (hb) tmem_ld_x16(acc + (uint32_t)(16 * ch + 16), xb);
                 tc_wait_ld();
-                finish(ch, xa, rf[2 * pp], sm[2 * pp], res);
-                if (hb) {
-                    load_res(ch + 1, res);
-                    finish(ch + 1, xb, rf[2 * pp + 1], sm[2 * pp + 1], res);
-                }
+                if (hb) load_res(ch + 1, resb);
+                finish(ch, xa, rf[2 * pp], sm[2 * pp], resa);
+                if (ch + 4 < nchunk) load_res(ch + 4, resa);
+                if (hb) finish(ch + 1, xb, rf[2 * pp + 1], sm[2 * pp + 1], resb);
             }
             tc_fence_before();
             __syncwarp();
