@@ -15,7 +15,8 @@
 //   * warp 5 (MMA) issues eight tcgen05.mma.kind::i8 (M=128, N=T, K=32): A = codes from TMEM, B = signed
 //     int8 activations from shared memory (descriptors derived from one precomputed ring descriptor),
 //     int32 accumulators in one of two TMEM buffers;
-//   * warps 6-13 (epilogue, two per quadrant) read the finished buffer (tcgen05.ld) and write
+//   * warps 6.. (epilogue, two per quadrant, three for the plain and +bias forms at K <= 2560) read the
+//     finished buffer (tcgen05.ld) and write
 //     y = (float)(acc - sum_q[m]) * (w_scale / s[m]) (+ bias, GELU, + residual), while the MMAs of the
 //     next tile already fill the other buffer. The output writes of one tile therefore overlap the
 //     main loop of the next instead of stalling every SM at the end of a wave.
@@ -37,7 +38,7 @@ constexpr int kActSubBytes = kMaxT * 128;             // one K step's activation
 constexpr int kActStageBytes = kKS * kActSubBytes;
 constexpr int kWSubBytes = 128 * 32;                  // one K step's packed weight tile
 constexpr int kWStageBytes = kKS * kWSubBytes;
-constexpr int kThreads = 448;  // warps 0-3 converters, 4 TMA producer, 5 MMA, 6-13 epilogue
+// warps 0-3 converters, 4 TMA producer, 5 MMA, 6.. epilogue (G per TMEM quadrant, see tcp_threads)
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kAccCol0 = kAStages * kKS * 32;  // accumulator buffer b at kAccCol0 + b * kMaxT
 static_assert(kAccCol0 + 2 * kMaxT <= kTmemCols, "TMEM budget");
@@ -48,7 +49,7 @@ struct alignas(8) Bars {
     uint64_t afull[kAStages];   // converters wrote TMEM A stage (4 arrivals)
     uint64_t afree[kAStages];   // MMAs reading TMEM A stage done (commit)
     uint64_t accfull[2];        // accumulator buffer complete (commit)
-    uint64_t accfree[2];        // epilogue drained accumulator buffer (8 arrivals)
+    uint64_t accfree[2];        // epilogue drained accumulator buffer (one arrival per epilogue warp)
     uint64_t drain;
     uint32_t tmem_slot;
     uint32_t abort;
@@ -64,8 +65,17 @@ __host__ __device__ constexpr uint32_t idesc_u8s8(int M, int N) {
 
 constexpr int kPEpiBias = 1, kPEpiGelu = 2, kPEpiResidual = 4;
 
-template <int MODE, int EPI>
-__global__ void __launch_bounds__(tcp::kThreads, 1)
+// Epilogue warps per TMEM lane quadrant (template parameter G). A tile's epilogue runs latency-bound at
+// two warps per scheduler; where the K loop is short (K <= 2560: 1152 has five stages per tile) that
+// took longer than the next tile's K loop, so the plain and +bias forms there take three warps per
+// quadrant (2048 x 1152 -> 4304: 25.6 -> 21.2 µs; 16384 x 1152 -> 4304: 0.35 -> 0.45 of the int8 peak).
+// At K = 6912, where the epilogue hides behind a long K loop, three measured no better (16384 x 6912 ->
+// 2560: 238 µs against 226-235 µs with two in other runs), so long K keeps two, as do the residual forms
+// (128 registers) and the gate/up form.
+__host__ __device__ constexpr int tcp_threads(int groups) { return 32 * (6 + 4 * groups); }
+
+template <int MODE, int EPI, int G>
+__global__ void __launch_bounds__(tcp_threads(G), 1)
 gemm_i2s_tcp_kernel(const __grid_constant__ CUtensorMap tmap_w0, const __grid_constant__ CUtensorMap tmap_w1,
                     const __grid_constant__ CUtensorMap tmap_q, const float* __restrict__ w0_scale,
                     const float* __restrict__ w1_scale, const float* __restrict__ s_act,
@@ -96,7 +106,7 @@ gemm_i2s_tcp_kernel(const __grid_constant__ CUtensorMap tmap_w0, const __grid_co
         }
         for (int i = 0; i < 2; ++i) {
             mbar_init(&bars->accfull[i], 1);
-            mbar_init(&bars->accfree[i], 8);
+            mbar_init(&bars->accfree[i], 4 * G);
         }
         mbar_init(&bars->drain, 1);
         bars->abort = 0;
@@ -241,17 +251,17 @@ gemm_i2s_tcp_kernel(const __grid_constant__ CUtensorMap tmap_w0, const __grid_co
         }
         if (!ok && lane == 0) *abort_flag = 1;
     } else {
-        // ------------------------------------------------------------------ epilogue (warps 6-13)
-        // The two warps of a quadrant take alternate 16-token chunk pairs. Before a tile's accumulators
+        // ------------------------------------------------------------------ epilogue (warps 6..)
+        // The G warps of a quadrant take every G-th 16-token chunk pair. Before a tile's accumulators
         // are waited for, each lane fetches the scales (w_scale / s[m], one IEEE division) and code sums of
         // the tokens its warp will write, so no global-memory latency sits between accumulator and store.
         const int q = warp & 3;             // TMEM lane quadrant
-        const int grp = (warp - 6) >> 2;
+        const int grp = (warp - 6) >> 2;  // 0 .. G-1 (G epilogue warps per quadrant)
         const int row = 32 * q + lane;
         const int gu = (MODE == 1) ? (lane >> 4) : 0;
         const uint32_t lane_base = tmem_base + ((uint32_t)(q * 32) << 16);
         const int nchunk = T / 16;
-        constexpr int kPairs = (kMaxT / 16 + 3) / 4;  // chunk pairs per warp
+        constexpr int kPairs = (kMaxT / 16 + 2 * G - 1) / (2 * G);  // chunk pairs per warp
         griddep_wait();  // scales, sums and residual come from the preceding kernels
         uint32_t i = 0;
         for (int t = blockIdx.x; t < total; t += gridDim.x, ++i) {
@@ -263,12 +273,12 @@ gemm_i2s_tcp_kernel(const __grid_constant__ CUtensorMap tmap_w0, const __grid_co
             const float ws1 = (MODE == 1) ? __ldg(w1_scale) : ws0;
             const float wsl = (MODE == 1 && lane >= 16) ? ws1 : ws0;
             const float bias_n = ((EPI & kPEpiBias) && n < N) ? epi.bias[n] : 0.0f;
-            // chunk pair p of this warp: chunks 4p + 2 grp and 4p + 2 grp + 1; lane l holds token l & 15
+            // chunk pair p of this warp: chunks 2 (G p + grp) and 2 (G p + grp) + 1; lane l holds token l & 15
             float rf[2 * kPairs];
             int sm[2 * kPairs];
 #pragma unroll
             for (int c = 0; c < 2 * kPairs; ++c) {
-                const int ch = 4 * (c >> 1) + 2 * grp + (c & 1);
+                const int ch = 2 * (G * (c >> 1) + grp) + (c & 1);
                 const int mj = m0 + 16 * ch + (lane & 15);
                 const bool ok = ch < nchunk && mj < M;
                 sm[c] = ok ? sum_act[mj] : 0;
@@ -336,7 +346,7 @@ gemm_i2s_tcp_kernel(const __grid_constant__ CUtensorMap tmap_w0, const __grid_co
             };
 #pragma unroll
             for (int pp = 0; pp < kPairs; ++pp) {
-                const int ch = 4 * pp + 2 * grp;
+                const int ch = 2 * (G * pp + grp);
                 if (ch >= nchunk) break;
                 const bool hb = ch + 1 < nchunk;
                 uint32_t xa[16], xb[16];
@@ -345,7 +355,7 @@ gemm_i2s_tcp_kernel(const __grid_constant__ CUtensorMap tmap_w0, const __grid_co
                 tc_wait_ld();
                 if (hb) load_res(ch + 1, resb);
                 finish(ch, xa, rf[2 * pp], sm[2 * pp], resa);
-                if (ch + 4 < nchunk) load_res(ch + 4, resa);
+                if (ch + 2 * G < nchunk) load_res(ch + 2 * G, resa);
                 if (hb) finish(ch + 1, xb, rf[2 * pp + 1], sm[2 * pp + 1], resb);
             }
             tc_fence_before();
@@ -363,14 +373,14 @@ gemm_i2s_tcp_kernel(const __grid_constant__ CUtensorMap tmap_w0, const __grid_co
     }
 }
 
-template <int MODE, int EPI>
-static cudaError_t launch_tcp_variant(const TcGemmArgs& a, int grid, cudaStream_t st) {
-    auto kfn = gemm_i2s_tcp_kernel<MODE, EPI>;
+template <int MODE, int EPI, int G>
+static cudaError_t launch_tcp_groups(const TcGemmArgs& a, int grid, cudaStream_t st) {
+    auto kfn = gemm_i2s_tcp_kernel<MODE, EPI, G>;
     cudaError_t e = ensure_dynamic_smem(reinterpret_cast<const void*>(kfn), tcp::kSmemBytes);
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)grid);
-    cfg.blockDim = dim3(tcp::kThreads);
+    cfg.blockDim = dim3(tcp_threads(G));
     cfg.dynamicSmemBytes = tcp::kSmemBytes;
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
@@ -380,6 +390,14 @@ static cudaError_t launch_tcp_variant(const TcGemmArgs& a, int grid, cudaStream_
     cfg.numAttrs = 1;
     return cudaLaunchKernelEx(&cfg, kfn, a.tmap_w0, a.tmap_w1, a.tmap_q, a.w0_scale, a.w1_scale, a.s, a.sums, a.y,
                               a.ldy, a.M, a.N, a.Kp, a.T, a.n_tiles, a.m_tiles, a.epi);
+}
+
+template <int MODE, int EPI>
+static cudaError_t launch_tcp_variant(const TcGemmArgs& a, int grid, cudaStream_t st) {
+    if constexpr (MODE == 0 && !(EPI & kPEpiResidual)) {
+        if (a.Kp <= 2560) return launch_tcp_groups<MODE, EPI, 3>(a, grid, st);
+    }
+    return launch_tcp_groups<MODE, EPI, 2>(a, grid, st);
 }
 
 int tcp_max_tokens() { return tcp::kMaxT; }
