@@ -267,15 +267,20 @@ int run_tc(const b2s::I2sWeight& w0, const b2s::I2sWeight* w1, const int8_t* q, 
     // 64), the 64 standing for the per-tile fixed costs. Up to 8 more token tiles than the minimum are
     // tried, so that a shape whose fewest tiles leave a thin last wave can take smaller ones (the ViT's
     // 2048 x 1152 -> 3456 GEMM: 16 tiles of 128 tokens fill 97% of the SMs' slots, 13 of 160 only 79%).
+    // Where the one-tile-per-CTA kernel would split K instead, a persistent grid of one wave wins when a
+    // token tile of at least 64 gives 90-100% of the SMs exactly one tile each (no split-K exchange, two
+    // K steps per handoff): the ViT's 2048 x 1152 -> 1152 (+bias, +residual) 17.4 -> 13.7 µs and
+    // 2048 x 4304 -> 1152 24.2 -> 19.3 µs with 144 tiles of 128 tokens.
+    const bool one_wave = (int64_t)t.n_tiles * t.m_tiles <= nsm && t.splits > 1;
     int p_grid = 0;
-    if ((int64_t)t.n_tiles * t.m_tiles > nsm) {
+    if ((int64_t)t.n_tiles * t.m_tiles > nsm || one_wave) {
         const int64_t n_tiles = b2s::ceil_div(w0.N, rows), mt0 = b2s::ceil_div(M, b2s::tcp_max_tokens());
         int64_t best = -1;
         for (int64_t mt = mt0; mt <= mt0 + 8; ++mt) {
             const int64_t T = b2s::round_up(b2s::ceil_div(M, mt), 16);
             if (T > b2s::tcp_max_tokens() || b2s::ceil_div(M, T) != mt) continue;
             const int64_t tiles = n_tiles * mt;
-            if (tiles < nsm) continue;
+            if (one_wave ? (tiles > nsm || tiles * 10 < (int64_t)nsm * 9 || T < 64) : tiles < nsm) continue;
             const int64_t cost = b2s::ceil_div(tiles, nsm) * (T + 64);
             if (best < 0 || cost < best) {
                 best = cost;
