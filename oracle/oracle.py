@@ -85,6 +85,8 @@ def lib():
         L.orc_layer_norm.argtypes = [_f32p, C.c_void_p, C.c_void_p, _i64, _i64, C.c_float, _f32p]
         L.orc_gelu_tanh.restype = C.c_float
         L.orc_gelu_tanh.argtypes = [C.c_float]
+        L.orc_det_recipf.restype = C.c_float
+        L.orc_det_recipf.argtypes = [C.c_float]
         L.orc_rope_table.restype = None
         L.orc_rope_table.argtypes = [C.c_float, C.c_int, C.c_int, _f32p]
         L.orc_rope_neox.restype = None
@@ -360,6 +362,12 @@ def layer_norm(x, g, b, eps: float) -> np.ndarray:
 def gelu_tanh(x: np.ndarray) -> np.ndarray:
     f = lib().orc_gelu_tanh
     return np.array([f(float(v)) for v in np.asarray(x, np.float32).reshape(-1)], np.float32).reshape(np.shape(x))
+
+
+def det_recipf(d: np.ndarray) -> np.ndarray:
+    """1/d by the device's seed-and-Newton sequence (i2s_oracle.c: orc_det_recipf)."""
+    f = lib().orc_det_recipf
+    return np.array([f(float(v)) for v in np.asarray(d, np.float32).reshape(-1)], np.float32).reshape(np.shape(d))
 
 
 def rope_table(base: float, hd: int, n_pos: int) -> np.ndarray:

@@ -159,3 +159,26 @@ def test_forward_amplifies_rounding_differences(orc):
     m.close()
     rel = float(np.max(np.abs(h1.astype(np.float64) - h0)) / np.max(np.abs(h0)))
     assert rel > 1e-2, rel
+
+
+def test_det_recipf_accuracy(orc):
+    """The reciprocal inside tanh (bit-pattern seed, three Newton-Raphson steps) is within 2^-22 of 1/d over
+    the whole range tanh feeds it (e^{2|u|} + 1 in [2, e^19 + 1]) and beyond, powers of two included."""
+    g = np.random.default_rng(7)
+    d = np.concatenate([np.exp(g.uniform(0, 19, 4000)) + 1, g.uniform(1, 2, 2000) * 2.0 ** g.integers(-20, 60, 2000),
+                        2.0 ** np.arange(-20, 60), np.nextafter(np.float32(2.0) ** np.arange(-20, 60), 0)])
+    d = d.astype(np.float32)
+    y = orc.det_recipf(d).astype(np.float64)
+    assert np.max(np.abs(y * d.astype(np.float64) - 1.0)) <= 2.0 ** -22
+
+
+def test_gelu_tanh_accuracy(orc):
+    """GELU (tanh form) with the oracle's exp and reciprocal stays within 1e-6 x max(1, |x|) of the float64
+    evaluation of the same formula, across the saturating tails."""
+    x = np.concatenate([np.linspace(-12, 12, 24001), np.random.default_rng(8).standard_normal(4000) * 3]).astype(
+        np.float32)
+    got = orc.gelu_tanh(x).astype(np.float64)
+    x64 = x.astype(np.float64)
+    ref = 0.5 * x64 * (1.0 + np.tanh(np.sqrt(2.0 / np.pi) * (x64 + 0.044715 * x64 ** 3)))
+    assert np.all(np.abs(got - ref) <= 1e-6 * np.maximum(1.0, np.abs(x64)))
+
